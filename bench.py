@@ -1,0 +1,590 @@
+"""Benchmark of the hexel-kernel hot path on B200: fwd+bwd Mpix/s (and frames/s).
+
+Default workload: the Image-GS 2D fit step at 2048x2048 with 100,000
+Gaussians (projection -> binning -> top-10 normalised compositing -> L2 loss
+-> backward to the Gaussian parameters).  One JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU (torchrun, one rank per GPU): the image is split into horizontal
+stripes of 16-pixel tile rows, Gaussians are replicated, each rank renders
+and back-propagates its stripe and the packed per-Gaussian gradients are
+summed with one NCCL all-reduce (strong scaling: total work fixed).
+
+`--impl reference` times the CPU restatement of the reference's algorithm
+(the reference ships no CPU implementation) on the host's cores, on a bounded
+sample of the same workload.  When the reference's own CUDA kernels were
+built from its sources (oracle/_ref), our line also reports them timed on
+the same GPU under "ref_cuda_sm100a".
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "hexel-kernel_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "fwd+bwd Mpix/s"
+UNIT = "Mpix/s"
+L2_FLUSH_BYTES = 256 << 20
+FP32_LANES_PER_SM = 128
+NUM_SMS = 148
+
+
+# ---------------------------------------------------------------------------
+# environment helpers
+# ---------------------------------------------------------------------------
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d.get("hbm_gbs", 6650.0), "source": "measured",
+                "sm_max_mhz": d.get("sm_max_mhz", 1965.0)}
+    return {"hbm_gbs": 6650.0, "source": "fallback", "sm_max_mhz": 1965.0}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# Image-GS fit step
+# ---------------------------------------------------------------------------
+def stripe_rows(tiles_y: int, world: int, rank: int):
+    if world == 1:
+        return None
+    b = tiles_y * rank // world
+    e = tiles_y * (rank + 1) // world
+    return (b, e)
+
+
+class ImageGSStep:
+    """Device-resident fit step, stage by stage (the same kernels as the
+    public autograd API), with CUDA events between stages."""
+
+    STAGES = ("project", "scan", "bin", "raster_fwd", "loss", "raster_bwd", "project_bwd",
+              "allreduce")
+
+    def __init__(self, w, world: int, rank: int):
+        import gsplat
+        from gsplat import csrc
+        from gsplat.utils import bin_gaussians_fused, compute_cumulative_intersects, \
+            count_tiles_in_rows
+
+        self.gs, self.csrc = gsplat, csrc
+        self.bin, self.scan, self.count_rows = (bin_gaussians_fused,
+                                                compute_cumulative_intersects,
+                                                count_tiles_in_rows)
+        self.w = w
+        self.world, self.rank = world, rank
+        self.rows = stripe_rows(w.tile_bounds[1], world, rank)
+        self.H, self.W = w.height, w.width
+        self.numel = w.height * w.width * 3
+        dev = torch.device("cuda")
+        self.m, self.s, self.r, self.c = (w.means2d.to(dev), w.scales2d.to(dev),
+                                          w.rotation.to(dev), w.colors.to(dev))
+        self.target = w.target.to(dev)
+        if self.rows is not None:
+            self.r0, self.r1 = self.rows[0] * 16, min(self.rows[1] * 16, self.H)
+        else:
+            self.r0, self.r1 = 0, self.H
+        self.events = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.STAGES) + 1)]
+        self.stage_ms = {k: 0.0 for k in self.STAGES}
+        self.info = {}
+
+    def run(self, timed: bool):
+        ev = self.events
+        csrc, w = self.csrc, self.w
+        ev[0].record()
+        xys, radii, conics, nth = csrc.project_gaussians_2d_scale_rot_forward(
+            w.num_points, self.m, self.s, self.r, self.H, self.W, w.tile_bounds)
+        ev[1].record()
+        if self.rows is not None:
+            nth = self.count_rows(xys, radii, w.tile_bounds, self.rows)
+        n_isect, cum = self.scan(nth)
+        ev[2].record()
+        ids, bins = self.bin(w.num_points, n_isect, xys, radii, cum, w.tile_bounds, self.rows)
+        ev[3].record()
+        img, topk = csrc.nd_rasterize_forward_topk_norm(
+            w.tile_bounds, (16, 16, 1), (self.W, self.H, 1), ids, bins, xys, conics, self.c)
+        ev[4].record()
+        diff = img[self.r0:self.r1] - self.target[self.r0:self.r1]
+        loss = (diff * diff).sum() / self.numel
+        v_img = torch.zeros_like(img)
+        v_img[self.r0:self.r1] = diff * (2.0 / self.numel)
+        ev[5].record()
+        v_xy, v_conic, v_colors = csrc.nd_rasterize_backward_topk_norm(
+            self.H, self.W, 16, 16, ids, bins, xys, conics, self.c, v_img, topk)
+        ev[6].record()
+        _, v_mean, v_scale, v_rot = csrc.project_gaussians_2d_scale_rot_backward(
+            w.num_points, self.m, self.s, self.r, self.H, self.W, radii, conics, v_xy, v_conic)
+        ev[7].record()
+        if self.world > 1:
+            import torch.distributed as dist
+
+            packed = torch.cat([v_mean.view(-1), v_scale.view(-1), v_rot.view(-1),
+                                v_colors.view(-1), loss.view(1)])
+            dist.all_reduce(packed)
+        ev[8].record()
+        self.info = {"num_intersects": n_isect, "bins": bins}
+        self._last = (loss, v_mean, v_scale, v_rot, v_colors)
+        return loss
+
+    def collect(self):
+        for i, k in enumerate(self.STAGES):
+            self.stage_ms[k] += self.events[i].elapsed_time(self.events[i + 1])
+
+
+def run_ours(args, world, rank, local):
+    import workloads
+    from gsplat._lib import lib
+
+    w = getattr(workloads, args.config)()
+    step = ImageGSStep(w, world, rank)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    for _ in range(args.warmup):
+        step.run(False)
+    torch.cuda.synchronize()
+    # per-stage work of this rank's share (for the roofline)
+    bins = step.info["bins"].cpu()
+    counts = (bins[:, 1] - bins[:, 0]).to(torch.int64)
+    tx, ty, _ = w.tile_bounds
+    ty_idx = torch.arange(tx * ty) // tx
+    tx_idx = torch.arange(tx * ty) % tx
+    px_in_tile = ((torch.clamp(w.height - ty_idx * 16, max=16)) *
+                  (torch.clamp(w.width - tx_idx * 16, max=16)))
+    pairs = int((counts * px_in_tile).sum())
+    n_isect = int(step.info["num_intersects"])
+
+    clocks = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    launches0 = lib.dll.hx_launch_count()
+    total_ms = 0.0
+    start_ev = torch.cuda.Event(enable_timing=True)
+    end_ev = torch.cuda.Event(enable_timing=True)
+    for _ in range(args.steps):
+        flush.zero_()
+        start_ev.record()
+        step.run(True)
+        end_ev.record()
+        torch.cuda.synchronize()
+        step.collect()
+        total_ms += start_ev.elapsed_time(end_ev)
+    launches = lib.dll.hx_launch_count() - launches0
+    barrier(world)
+    clk = clocks.stop()
+    total_ms = max_over_ranks(total_ms, world)
+    ms_per_step = total_ms / args.steps
+    stage_ms = {k: max_over_ranks(v / args.steps, world) for k, v in step.stage_ms.items()}
+
+    # end-to-end: public autograd API from pinned host buffers, loss read back
+    e2e = run_e2e(w, args, world, rank)
+
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    mpix = w.height * w.width / 1e6
+    value = mpix / (ms_per_step / 1e3)
+    sm_mhz = clk.get("sm_mhz") or peaks["sm_max_mhz"]
+    fp32_peak_tflops = NUM_SMS * FP32_LANES_PER_SM * 2 * peaks["sm_max_mhz"] * 1e6 / 1e12
+    fwd_ms = stage_ms["raster_fwd"]
+    fwd_flops = pairs * 14.0
+    stages = {k: round(v, 4) for k, v in stage_ms.items()}
+    sort_bits = max(1, (tx * ty - 1).bit_length())
+    sort_bytes = n_isect * (8 + 16 * ((sort_bits + 7) // 8))
+    roofline = {
+        "kernel": "topk_fwd_kernel (nd_rasterize_forward_topk_norm)",
+        "bound": "fp32",
+        "achieved": round(fwd_flops / (fwd_ms / 1e3) / 1e12, 3),
+        "peak": round(fp32_peak_tflops, 2),
+        "unit": "TFLOP/s",
+        "frac": round(fwd_flops / (fwd_ms / 1e3) / 1e12 / fp32_peak_tflops, 4),
+        "traffic": None,
+        "peak_source": "nominal FP32 FMA rate, 148 SMs x 128 lanes x 2 x max SM clock "
+                       "(no measured FP32 peak in MEASURED_PEAKS.json)",
+        "work": f"{pairs} (pixel, candidate) pairs x 14 FLOP",
+        "bin_sort_hbm": {
+            "achieved_gbs": round(sort_bytes / (stage_ms["bin"] / 1e3) / 1e9, 1),
+            "peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"],
+            "frac": round(sort_bytes / (stage_ms["bin"] / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+            "bytes": sort_bytes,
+        },
+    }
+    line = {
+        "metric": METRIC,
+        "value": round(value * 1.0, 3),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "frames_per_s": round(1e3 / ms_per_step, 3),
+        "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded; the reference publishes no dataset)",
+        "config": {
+            "workload": w.name,
+            "height": w.height, "width": w.width, "num_gaussians": w.num_points,
+            "top_k": 10, "tile": 16, "channels": 3,
+            "num_intersects": n_isect,
+            "parallelism": f"tile-row stripes x{world}" if world > 1 else "single GPU",
+            "l2": "flushed between timed steps (256 MB write)",
+        },
+        "stages_ms": stages,
+        "roofline": roofline,
+        "e2e": e2e,
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+    if world == 1:
+        line["cpu_baseline"] = cpu_baseline(args, w)
+        ref = ref_cuda_timing(args, w)
+        if ref is not None:
+            line["ref_cuda_sm100a"] = ref
+    return line
+
+
+def run_e2e(w, args, world, rank):
+    """Same step through the public API (autograd), inputs copied each step
+    from pinned host memory and the loss read back."""
+    import gsplat
+
+    rows = stripe_rows(w.tile_bounds[1], world, rank)
+    host = [t.pin_memory() for t in (w.means2d, w.scales2d, w.rotation, w.colors, w.target)]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    if rows is not None:
+        r0, r1 = rows[0] * 16, min(rows[1] * 16, w.height)
+    else:
+        r0, r1 = 0, w.height
+    numel = w.height * w.width * 3
+
+    def one():
+        m, s, r, c, tgt = (t.to("cuda", non_blocking=True) for t in host)
+        for p in (m, s, r, c):
+            p.requires_grad_(True)
+        xys, radii, conics, nth = gsplat.project_gaussians_2d_scale_rot(m, s, r, w.height, w.width,
+                                                                        w.tile_bounds)
+        img = gsplat.rasterize_gaussians_sum(xys, radii, conics, nth, c, w.height, w.width,
+                                             topk_norm=True, tile_rows=rows)
+        d = img[r0:r1] - tgt[r0:r1]
+        loss = (d * d).sum() / numel
+        loss.backward()
+        if world > 1:
+            import torch.distributed as dist
+
+            packed = torch.cat([m.grad.view(-1), s.grad.view(-1), r.grad.view(-1),
+                                c.grad.view(-1), loss.detach().view(1)])
+            dist.all_reduce(packed)
+            loss = packed[-1]
+        return float(loss.item())
+
+    for _ in range(max(1, args.warmup)):
+        one()
+    torch.cuda.synchronize()
+    barrier(world)
+    st = torch.cuda.Event(enable_timing=True)
+    en = torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(args.steps):
+        one()
+    en.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(st.elapsed_time(en) / args.steps, world)
+    return {"value": round(w.height * w.width / 1e6 / (ms / 1e3), 3), "unit": UNIT,
+            "ms_per_step": round(ms, 4), "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": 4,
+            "path": "gsplat.project_gaussians_2d_scale_rot + gsplat.rasterize_gaussians_sum"
+                    "(topk_norm=True) + L2 loss + backward"}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle (restated reference algorithm) on host cores
+# ---------------------------------------------------------------------------
+def cpu_sample_run(w, crop_tiles: int):
+    """One fwd+bwd of the oracle over a crop of crop_tiles x crop_tiles tiles
+    at the image centre; returns (seconds, megapixels)."""
+    import numpy as np
+
+    from oracle import raster2d as o
+
+    tx, ty, _ = w.tile_bounds
+    x0 = max(0, tx // 2 - crop_tiles // 2)
+    y0 = max(0, ty // 2 - crop_tiles // 2)
+    xs = np.arange(x0, min(tx, x0 + crop_tiles))
+    ys = np.arange(y0, min(ty, y0 + crop_tiles))
+    tiles = (ys[:, None] * tx + xs[None, :]).reshape(-1)
+    t0 = time.perf_counter()
+    m = w.means2d.clone().requires_grad_(False)
+    xys, radii, conics, nth = o.project_2d(m, w.scales2d, w.rotation, w.height, w.width,
+                                           w.tile_bounds)
+    # bin only Gaussians whose rectangle meets the crop
+    rx0, ry0, rx1, ry1 = o.tile_rect(xys.numpy(), radii.numpy().astype(np.float32), tx, ty)
+    meet = ((radii.numpy() > 0) & (rx1 > xs[0]) & (rx0 <= xs[-1]) & (ry1 > ys[0]) &
+            (ry0 <= ys[-1]))
+    sub = np.nonzero(meet)[0]
+    keys, ids = o.map_intersects(xys.numpy()[sub], radii.numpy()[sub], None, w.tile_bounds,
+                                 tile_rows=(int(ys[0]), int(ys[-1]) + 1))
+    ids = sub[ids] if ids.size else ids
+    _, ids_sorted, bins = o.sort_and_bin(keys, ids.astype(np.int32), tx * ty)
+    img, topk, _, _ = o.rasterize_topk_forward(xys, conics, w.colors, torch.from_numpy(ids_sorted),
+                                               bins, w.height, w.width, tile_ids=tiles)
+    v_img = torch.zeros_like(img)
+    rows = slice(int(ys[0]) * 16, min((int(ys[-1]) + 1) * 16, w.height))
+    cols = slice(int(xs[0]) * 16, min((int(xs[-1]) + 1) * 16, w.width))
+    v_img[rows, cols] = 2.0 * (img[rows, cols] - w.target[rows, cols]) / img.numel()
+    topk_crop = torch.full_like(topk, -1)
+    topk_crop[rows, cols] = topk[rows, cols]
+    v_xy, v_conic, v_colors = o.rasterize_topk_backward(xys, conics, w.colors, v_img, topk_crop,
+                                                        w.height, w.width)
+    o.project_2d_backward(w.scales2d, w.rotation, w.height, w.width, radii, conics, v_xy, v_conic)
+    secs = time.perf_counter() - t0
+    mpix = (rows.stop - rows.start) * (cols.stop - cols.start) / 1e6
+    return secs, mpix
+
+
+def cpu_baseline(args, w):
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    crop = max(1, min(args.cpu_crop_tiles, w.tile_bounds[0]))
+    secs, mpix = cpu_sample_run(w, crop)
+    return {"value": round(mpix / secs, 5), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"one fwd+bwd over a {crop}x{crop}-tile ({mpix:.4f} Mpix) centre crop of "
+                      f"{w.name}: projection of all Gaussians, binning of those meeting the "
+                      f"crop, top-10 compositing and backward; {secs:.2f} s",
+            "seconds": round(secs, 3)}
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the CPU restatement of the reference's algorithm (the
+    reference has no CPU implementation), all host threads, bounded sample per step."""
+    if rank != 0:
+        return None
+    import workloads
+
+    w = getattr(workloads, args.config)()
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    crop = max(1, min(args.cpu_crop_tiles, w.tile_bounds[0]))
+    for _ in range(min(args.warmup, 1)):
+        cpu_sample_run(w, crop)
+    secs_total, mpix_total = 0.0, 0.0
+    steps = max(1, min(args.steps, args.ref_max_steps))
+    for _ in range(steps):
+        s, mp = cpu_sample_run(w, crop)
+        secs_total += s
+        mpix_total += mp
+    value = mpix_total / secs_total
+    return {
+        "metric": METRIC, "value": round(value, 5), "unit": UNIT, "impl": "reference",
+        "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 1),
+        "ms_per_step": round(secs_total / steps * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": w.name, "height": w.height, "width": w.width,
+                   "num_gaussians": w.num_points, "top_k": 10, "tile": 16},
+        "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads,
+                         "kind": "port",
+                         "sample": f"each step: one fwd+bwd over a {crop}x{crop}-tile centre "
+                                   f"crop ({mpix_total / steps:.4f} Mpix); the reference ships "
+                                   "CUDA only, so this is its algorithm restated on the CPU"},
+        "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------------------------------
+# the reference's own CUDA kernels (built from its sources), same GPU
+# ---------------------------------------------------------------------------
+def ref_cuda_timing(args, w):
+    path = os.path.join(ROOT, "oracle", "_ref", "_ref_gsplat_csrc.so")
+    if not os.path.exists(path):
+        return None
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_ref_gsplat_csrc", path)
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    dev = torch.device("cuda")
+    m, s, r, c, tgt = (t.to(dev) for t in (w.means2d, w.scales2d, w.rotation, w.colors, w.target))
+    H, W, tb, n = w.height, w.width, w.tile_bounds, w.num_points
+    numel = H * W * 3
+
+    def step():
+        # the reference's own call sequence (rasterize_sum.py:54-226, utils.py:96-162)
+        xys, radii, conics, nth = ref.project_gaussians_2d_scale_rot_forward(n, m, s, r, H, W, tb)
+        cum = torch.cumsum(nth, dim=0, dtype=torch.int32)
+        ni = int(cum[-1].item())
+        isect, gids = ref.map_gaussian_to_intersects(n, ni, xys, radii, cum, tb)
+        isect_s, order = torch.sort(isect)
+        gids_s = torch.gather(gids, 0, order)
+        bins = ref.get_tile_bin_edges(ni, tb[0] * tb[1], isect_s)
+        img, topk = ref.nd_rasterize_forward_topk_norm(tb, (16, 16, 1), (W, H, 1), gids_s, bins,
+                                                       xys, conics, c)
+        d = img - tgt
+        loss = (d * d).sum() / numel
+        v_img = d * (2.0 / numel)
+        v_xy, v_conic, v_col = ref.nd_rasterize_backward_topk_norm(H, W, 16, 16, gids_s, bins, xys,
+                                                                   conics, c, v_img, topk)
+        ref.project_gaussians_2d_scale_rot_backward(n, m, s, r, H, W, radii, conics, v_xy, v_conic)
+        return loss
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    total = 0.0
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(args.steps):
+        flush.zero_()
+        st.record()
+        step()
+        en.record()
+        torch.cuda.synchronize()
+        total += st.elapsed_time(en)
+    ms = total / args.steps
+    return {"value": round(H * W / 1e6 / (ms / 1e3), 3), "unit": UNIT, "ms_per_step": round(ms, 4),
+            "what": "reference CUDA kernels compiled from its sources for sm_100a "
+                    "(-O3 --use_fast_math), driven by its own Python call sequence"}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="imagegs_large",
+                    choices=["imagegs_large", "imagegs_small"])
+    ap.add_argument("--cpu-crop-tiles", type=int, default=16)
+    ap.add_argument("--ref-max-steps", type=int, default=3)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        line = run_ours(args, world, rank, local)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,749 @@
+// S3 / S4: Image-GS compositing — top-K normalised weighted sum, plain sum and
+// the tile-less brute-force variant, forward and backward.
+//
+// Per-pixel arithmetic follows gsplat/cuda/csrc/forward.cu:76-410 and
+// backward.cu:23-438 of the reference in the same operation order, compiled
+// with the same fast-math flags, so images and top-K ids match bit for bit.
+// What differs is the schedule:
+//   * forward: candidates are staged per batch as packed float4/float2 in
+//     shared memory, and the top-K minimum is cached and rescanned only after
+//     an insertion instead of for every candidate (same insertion rule: first
+//     empty slot, else first minimum, replace iff strictly greater);
+//   * top-K backward: instead of ~80 global atomics per pixel, each CTA
+//     accumulates per-Gaussian partials in a shared-memory hash table and
+//     flushes one global atomic per (Gaussian, component) per tile;
+//   * plain-sum backward: warp shuffle reduction, then shared-memory
+//     accumulation across the CTA's warps, then one global atomic per
+//     candidate component per tile.
+#include "hx_common.cuh"
+
+namespace hx {
+
+constexpr double kEpsTopK = 1e-4;     // EPS (config.h:9)
+constexpr double kEpsNoTiles = 1e-7;  // EPS_no_tiles (config.h:10)
+
+// Gaussian falloff exponent at pixel offset delta = xy - pixel.
+__device__ __forceinline__ float gauss_sigma(const float3 conic, const float2 delta) {
+    return 0.5f * (conic.x * delta.x * delta.x + conic.z * delta.y * delta.y) +
+           conic.y * delta.x * delta.y;
+}
+
+__device__ __forceinline__ bool sigma_invalid(float sigma) {
+    return sigma < 0.f || isnan(sigma) || isinf(sigma);
+}
+
+// Top-K slot selection: the first empty slot (value -1), else the first
+// minimum of the stored values (forward.cu:263-275).
+template <int K>
+__device__ __forceinline__ void topk_find_min(const int (&ids)[K], const float (&vals)[K],
+                                              int& min_id, float& min_val) {
+    min_id = -1;
+    min_val = 1e30f;
+    bool found_empty = false;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        if (!found_empty) {
+            if (ids[k] < 0) {
+                min_id = k;
+                min_val = -1.0f;
+                found_empty = true;
+            } else if (vals[k] < min_val) {
+                min_id = k;
+                min_val = vals[k];
+            }
+        }
+    }
+}
+
+template <int K>
+__device__ __forceinline__ void topk_insert(int (&ids)[K], float (&vals)[K], int& min_id,
+                                            float& min_val, int g, float alpha) {
+    if (alpha > min_val) {
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            if (k == min_id) {
+                ids[k] = g;
+                vals[k] = alpha;
+            }
+        }
+        topk_find_min<K>(ids, vals, min_id, min_val);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Top-K forward (forward.cu:172-320), one 16x16 tile per CTA.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) topk_fwd_kernel(
+    int tiles_x, unsigned img_w, unsigned img_h, int channels,
+    const int* __restrict__ gaussian_ids_sorted, const int2* __restrict__ tile_bins,
+    const float2* __restrict__ xys, const float3* __restrict__ conics,
+    const float* __restrict__ colors, float* __restrict__ out_img, int* __restrict__ pixel_topk,
+    float* __restrict__ out_weights_sum, float* __restrict__ out_entropy) {
+    __shared__ float4 s_a[kBlockSize];  // xy.x, xy.y, conic.x, conic.y
+    __shared__ float2 s_b[kBlockSize];  // conic.z, id bits
+
+    const int tile_id = blockIdx.y * tiles_x + blockIdx.x;
+    const unsigned i = blockIdx.y * kBlockY + threadIdx.y;
+    const unsigned j = blockIdx.x * kBlockX + threadIdx.x;
+    const int tr = threadIdx.y * kBlockX + threadIdx.x;
+    const float px = (float)j;
+    const float py = (float)i;
+    const int pix_id = i * img_w + j;
+    const bool inside = (i < img_h && j < img_w);
+
+    const int2 range = tile_bins[tile_id];
+    int ids[kTopK];
+    float vals[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        ids[k] = -1;
+        vals[k] = 0.f;
+    }
+    int min_id = 0;
+    float min_val = -1.f;
+
+    for (int batch_start = range.x; batch_start < range.y; batch_start += kBlockSize) {
+        __syncthreads();
+        const int idx = batch_start + tr;
+        if (idx < range.y) {
+            const int g = gaussian_ids_sorted[idx];
+            const float2 xy = xys[g];
+            const float3 c = conics[g];
+            s_a[tr] = make_float4(xy.x, xy.y, c.x, c.y);
+            s_b[tr] = make_float2(c.z, __int_as_float(g));
+        }
+        __syncthreads();
+        const int batch_size = min(kBlockSize, range.y - batch_start);
+        if (inside) {
+            for (int t = 0; t < batch_size; ++t) {
+                const float4 a = s_a[t];
+                const float2 b = s_b[t];
+                const float2 delta = {a.x - px, a.y - py};
+                const float sigma = gauss_sigma(make_float3(a.z, a.w, b.x), delta);
+                if (sigma_invalid(sigma)) continue;
+                const float alpha = __expf(-sigma);
+                topk_insert<kTopK>(ids, vals, min_id, min_val, __float_as_int(b.y), alpha);
+            }
+        }
+    }
+    if (!inside) return;
+
+    float sum_val = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k)
+        if (ids[k] >= 0) sum_val += vals[k];
+    const float denom = (float)((double)sum_val + kEpsTopK);
+
+    for (int c = 0; c < channels; ++c) {
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            const int g = ids[k];
+            if (g < 0) continue;
+            const float vis = vals[k] / denom;
+            acc += colors[g * channels + c] * vis;
+        }
+        out_img[pix_id * channels + c] = acc;
+    }
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) pixel_topk[pix_id * kTopK + k] = ids[k];
+    if (out_weights_sum) out_weights_sum[pix_id] = denom;
+    if (out_entropy) {
+        float entropy = 0.f;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            if (ids[k] < 0) continue;
+            const float p = vals[k] / denom;
+            entropy += -p * logf(p + 1e-7f);
+        }
+        out_entropy[pix_id] = entropy;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Plain-sum forward (forward.cu:76-170).
+// ---------------------------------------------------------------------------
+template <int MAXC>
+__global__ void __launch_bounds__(256) sum_fwd_kernel(
+    int tiles_x, unsigned img_w, unsigned img_h, int channels,
+    const int* __restrict__ gaussian_ids_sorted, const int2* __restrict__ tile_bins,
+    const float2* __restrict__ xys, const float3* __restrict__ conics,
+    const float* __restrict__ colors, float* __restrict__ out_img) {
+    __shared__ float4 s_a[kBlockSize];
+    __shared__ float2 s_b[kBlockSize];
+    const int tile_id = blockIdx.y * tiles_x + blockIdx.x;
+    const unsigned i = blockIdx.y * kBlockY + threadIdx.y;
+    const unsigned j = blockIdx.x * kBlockX + threadIdx.x;
+    const int tr = threadIdx.y * kBlockX + threadIdx.x;
+    const float px = (float)j;
+    const float py = (float)i;
+    const int pix_id = i * img_w + j;
+    const bool inside = (i < img_h && j < img_w);
+    const int2 range = tile_bins[tile_id];
+    float pix_out[MAXC];
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) pix_out[c] = 0.f;
+
+    for (int batch_start = range.x; batch_start < range.y; batch_start += kBlockSize) {
+        __syncthreads();
+        const int idx = batch_start + tr;
+        if (idx < range.y) {
+            const int g = gaussian_ids_sorted[idx];
+            const float2 xy = xys[g];
+            const float3 c = conics[g];
+            s_a[tr] = make_float4(xy.x, xy.y, c.x, c.y);
+            s_b[tr] = make_float2(c.z, __int_as_float(g));
+        }
+        __syncthreads();
+        const int batch_size = min(kBlockSize, range.y - batch_start);
+        if (inside) {
+            for (int t = 0; t < batch_size; ++t) {
+                const float4 a = s_a[t];
+                const float2 b = s_b[t];
+                const float2 delta = {a.x - px, a.y - py};
+                const float sigma = gauss_sigma(make_float3(a.z, a.w, b.x), delta);
+                if (sigma_invalid(sigma)) continue;
+                const float vis = __expf(-sigma);
+                const int g = __float_as_int(b.y);
+#pragma unroll
+                for (int c = 0; c < MAXC; ++c)
+                    if (c < channels) pix_out[c] += colors[g * channels + c] * vis;
+            }
+        }
+    }
+    if (inside) {
+#pragma unroll
+        for (int c = 0; c < MAXC; ++c)
+            if (c < channels) out_img[pix_id * channels + c] = pix_out[c];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Plain-sum backward (backward.cu:23-157).  `valid` is sticky per pixel as in
+// the reference: once a candidate has an invalid exponent, that pixel stops
+// contributing for the rest of the tile.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <int MAXC>
+__global__ void __launch_bounds__(256) sum_bwd_kernel(
+    int tiles_x, unsigned img_w, unsigned img_h, int channels,
+    const int* __restrict__ gaussian_ids_sorted, const int2* __restrict__ tile_bins,
+    const float2* __restrict__ xys, const float3* __restrict__ conics,
+    const float* __restrict__ colors, const float* __restrict__ v_output,
+    float* __restrict__ v_xy, float* __restrict__ v_conic, float* __restrict__ v_colors) {
+    constexpr int NCOMP = 5 + MAXC;
+    __shared__ float4 s_a[kBlockSize];
+    __shared__ float2 s_b[kBlockSize];
+    __shared__ float s_rgb[kBlockSize][MAXC];
+    __shared__ float s_acc[kBlockSize][NCOMP];
+
+    const int tile_id = blockIdx.y * tiles_x + blockIdx.x;
+    const unsigned i = blockIdx.y * kBlockY + threadIdx.y;
+    const unsigned j = blockIdx.x * kBlockX + threadIdx.x;
+    const int tr = threadIdx.y * kBlockX + threadIdx.x;
+    const int lane = tr & 31;
+    const float px = (float)j;
+    const float py = (float)i;
+    const int pix_id = min(i * img_w + j, img_w * img_h - 1);
+    const bool inside = (i < img_h && j < img_w);
+    const int2 range = tile_bins[tile_id];
+
+    float v_out[MAXC];
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) v_out[c] = (c < channels) ? v_output[channels * pix_id + c] : 0.f;
+
+    bool valid = inside;
+    for (int batch_start = range.x; batch_start < range.y; batch_start += kBlockSize) {
+        __syncthreads();
+        const int idx = batch_start + tr;
+        if (idx < range.y) {
+            const int g = gaussian_ids_sorted[idx];
+            const float2 xy = xys[g];
+            const float3 c = conics[g];
+            s_a[tr] = make_float4(xy.x, xy.y, c.x, c.y);
+            s_b[tr] = make_float2(c.z, __int_as_float(g));
+#pragma unroll
+            for (int c2 = 0; c2 < MAXC; ++c2)
+                s_rgb[tr][c2] = (c2 < channels) ? colors[channels * g + c2] : 0.f;
+        }
+#pragma unroll
+        for (int q = 0; q < NCOMP; ++q) s_acc[tr][q] = 0.f;
+        __syncthreads();
+        const int batch_size = min(kBlockSize, range.y - batch_start);
+        for (int t = 0; t < batch_size; ++t) {
+            const float4 a = s_a[t];
+            const float2 b = s_b[t];
+            const float3 conic = make_float3(a.z, a.w, b.x);
+            const float2 delta = {a.x - px, a.y - py};
+            const float sigma = gauss_sigma(conic, delta);
+            const float d = __expf(-sigma);
+            if (sigma_invalid(sigma)) valid = false;
+            float v_rgb_local[MAXC];
+            float vc0 = 0.f, vc1 = 0.f, vc2 = 0.f, vx = 0.f, vy = 0.f;
+#pragma unroll
+            for (int c = 0; c < MAXC; ++c) v_rgb_local[c] = 0.f;
+            if (valid) {
+#pragma unroll
+                for (int c = 0; c < MAXC; ++c)
+                    if (c < channels) v_rgb_local[c] = d * v_out[c];
+                float v_sigma = 0.f;
+#pragma unroll
+                for (int c = 0; c < MAXC; ++c)
+                    if (c < channels) v_sigma += s_rgb[t][c] * v_out[c];
+                v_sigma *= -d;
+                vc0 = 0.5f * v_sigma * delta.x * delta.x;
+                vc1 = v_sigma * delta.x * delta.y;
+                vc2 = 0.5f * v_sigma * delta.y * delta.y;
+                vx = v_sigma * (conic.x * delta.x + conic.y * delta.y);
+                vy = v_sigma * (conic.y * delta.x + conic.z * delta.y);
+            }
+#pragma unroll
+            for (int c = 0; c < MAXC; ++c)
+                if (c < channels) v_rgb_local[c] = warp_sum(v_rgb_local[c]);
+            vc0 = warp_sum(vc0);
+            vc1 = warp_sum(vc1);
+            vc2 = warp_sum(vc2);
+            vx = warp_sum(vx);
+            vy = warp_sum(vy);
+            if (lane == 0) {
+                atomicAdd(&s_acc[t][0], vx);
+                atomicAdd(&s_acc[t][1], vy);
+                atomicAdd(&s_acc[t][2], vc0);
+                atomicAdd(&s_acc[t][3], vc1);
+                atomicAdd(&s_acc[t][4], vc2);
+#pragma unroll
+                for (int c = 0; c < MAXC; ++c)
+                    if (c < channels) atomicAdd(&s_acc[t][5 + c], v_rgb_local[c]);
+            }
+        }
+        __syncthreads();
+        if (tr < batch_size) {
+            const int g = __float_as_int(s_b[tr].y);
+            atomicAdd(v_xy + 2 * g + 0, s_acc[tr][0]);
+            atomicAdd(v_xy + 2 * g + 1, s_acc[tr][1]);
+            atomicAdd(v_conic + 3 * g + 0, s_acc[tr][2]);
+            atomicAdd(v_conic + 3 * g + 1, s_acc[tr][3]);
+            atomicAdd(v_conic + 3 * g + 2, s_acc[tr][4]);
+#pragma unroll
+            for (int c = 0; c < MAXC; ++c)
+                if (c < channels) atomicAdd(v_colors + channels * g + c, s_acc[tr][5 + c]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory hash table of per-Gaussian gradient partials.
+// ---------------------------------------------------------------------------
+struct GradTable {
+    int* keys;    // [cap], -1 = free
+    float* acc;   // [cap][ncomp]
+    int cap;      // power of two
+    int ncomp;
+};
+
+// Slot of Gaussian g (inserted on first use), or -1 when a bounded probe
+// sequence finds no room; callers then fall back to global atomics.
+__device__ __forceinline__ int table_slot(const GradTable& t, int g) {
+    const unsigned mask = (unsigned)t.cap - 1u;
+    unsigned h = ((unsigned)g * 2654435761u) & mask;
+    volatile int* keys = t.keys;
+#pragma unroll 1
+    for (int probe = 0; probe < 32; ++probe) {
+        const unsigned s = (h + probe) & mask;
+        const int k = keys[s];
+        if (k == g) return (int)s;
+        if (k == -1) {
+            const int prev = atomicCAS(t.keys + s, -1, g);
+            if (prev == -1 || prev == g) return (int)s;
+        }
+    }
+    return -1;
+}
+
+__device__ __forceinline__ void table_init(const GradTable& t, int tid, int nthreads) {
+    for (int s = tid; s < t.cap; s += nthreads) t.keys[s] = -1;
+    for (int s = tid; s < t.cap * t.ncomp; s += nthreads) t.acc[s] = 0.f;
+}
+
+// ---------------------------------------------------------------------------
+// Top-K backward (backward.cu:159-316 tiled, 318-438 tile-less).  One CTA per
+// BX x BY pixel block; `eps` is the normaliser offset of the forward.
+// ---------------------------------------------------------------------------
+template <int BX, int BY, int SMEM_C>
+__global__ void __launch_bounds__(BX * BY) topk_bwd_kernel(
+    unsigned img_w, unsigned img_h, int channels, int num_points, float eps,
+    const float2* __restrict__ xys, const float3* __restrict__ conics,
+    const float* __restrict__ rgbs, const float* __restrict__ v_output,
+    const float* __restrict__ v_weights_sum, const float* __restrict__ v_entropy,
+    const int* __restrict__ pixel_topk, float* __restrict__ v_xy, float* __restrict__ v_conic,
+    float* __restrict__ v_rgb, int table_cap) {
+    extern __shared__ __align__(16) unsigned char s_raw[];
+    constexpr int NT = BX * BY;
+    const int ncomp = 5 + (channels <= SMEM_C ? channels : 0);
+    GradTable table;
+    table.keys = reinterpret_cast<int*>(s_raw);
+    table.acc = reinterpret_cast<float*>(s_raw + sizeof(int) * table_cap);
+    table.cap = table_cap;
+    table.ncomp = ncomp;
+    const int tid = threadIdx.y * BX + threadIdx.x;
+    table_init(table, tid, NT);
+    __syncthreads();
+
+    const unsigned i = blockIdx.y * BY + threadIdx.y;
+    const unsigned j = blockIdx.x * BX + threadIdx.x;
+    const float px = (float)j;
+    const float py = (float)i;
+    const bool inside = (i < img_h && j < img_w);
+    if (inside) {
+        const int pix_id = min((int)(i * img_w + j), (int)(img_w * img_h - 1));
+        const float* v_out = v_output + channels * pix_id;
+        int topk[kTopK];
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            const int g = pixel_topk[pix_id * kTopK + k];
+            topk[k] = (g < num_points) ? g : -1;
+        }
+        float d_local[kTopK];
+        float denom = eps;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            d_local[k] = 0.f;
+            const int g = topk[k];
+            if (g < 0) continue;
+            const float3 conic = conics[g];
+            const float2 xy = xys[g];
+            const float2 delta = {xy.x - px, xy.y - py};
+            const float d = __expf(-gauss_sigma(conic, delta));
+            denom += d;
+            d_local[k] = d;
+        }
+        float v_d_local[kTopK];
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) v_d_local[k] = 0.f;
+
+        int slots[kTopK];
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            slots[k] = -1;
+            const int g = topk[k];
+            if (g < 0) continue;
+            const float d = d_local[k];
+            const float norm_d = d / denom;
+            const int slot = table_slot(table, g);
+            slots[k] = slot;
+            float v_norm_d = 0.f;
+            for (int c = 0; c < channels; ++c) {
+                const float vo = v_out[c];
+                const float contrib = norm_d * vo;
+                if (slot >= 0 && channels <= SMEM_C)
+                    atomicAdd(&table.acc[slot * ncomp + 5 + c], contrib);
+                else
+                    atomicAdd(v_rgb + channels * g + c, contrib);
+                v_norm_d += rgbs[channels * g + c] * vo;
+            }
+            const float tmp = -d / (denom * denom) * v_norm_d;
+#pragma unroll
+            for (int l = 0; l < kTopK; ++l) {
+                if (l == k)
+                    v_d_local[l] += v_norm_d / denom + tmp;
+                else
+                    v_d_local[l] += tmp;
+            }
+        }
+
+        const float v_ws = v_weights_sum ? v_weights_sum[pix_id] : 0.f;
+        if (v_ws != 0.f) {
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k)
+                if (topk[k] >= 0) v_d_local[k] += v_ws;
+        }
+        const float v_ent = v_entropy ? v_entropy[pix_id] : 0.f;
+        if (v_ent != 0.f) {
+            float dHdp[kTopK];
+            float avg = 0.f;
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) {
+                dHdp[k] = 0.f;
+                if (topk[k] < 0) continue;
+                const float p = d_local[k] / denom;
+                const float dhdp = -(logf(p + 1e-7f) + 1.f);
+                dHdp[k] = dhdp;
+                avg += p * dhdp;
+            }
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) {
+                if (topk[k] < 0) continue;
+                const float dhdw = (dHdp[k] - avg) / denom;
+                v_d_local[k] += v_ent * dhdw;
+            }
+        }
+
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            const int g = topk[k];
+            if (g < 0) continue;
+            float v_sigma = v_d_local[k];
+            v_sigma *= -d_local[k];
+            const float3 conic = conics[g];
+            const float2 xy = xys[g];
+            const float2 delta = {xy.x - px, xy.y - py};
+            const float vc0 = 0.5f * v_sigma * delta.x * delta.x;
+            const float vc1 = v_sigma * delta.x * delta.y;
+            const float vc2 = 0.5f * v_sigma * delta.y * delta.y;
+            const float vx = v_sigma * (conic.x * delta.x + conic.y * delta.y);
+            const float vy = v_sigma * (conic.y * delta.x + conic.z * delta.y);
+            const int slot = slots[k];
+            if (slot >= 0) {
+                float* a = table.acc + slot * ncomp;
+                atomicAdd(a + 0, vx);
+                atomicAdd(a + 1, vy);
+                atomicAdd(a + 2, vc0);
+                atomicAdd(a + 3, vc1);
+                atomicAdd(a + 4, vc2);
+            } else {
+                atomicAdd(v_xy + 2 * g + 0, vx);
+                atomicAdd(v_xy + 2 * g + 1, vy);
+                atomicAdd(v_conic + 3 * g + 0, vc0);
+                atomicAdd(v_conic + 3 * g + 1, vc1);
+                atomicAdd(v_conic + 3 * g + 2, vc2);
+            }
+        }
+    }
+    __syncthreads();
+    for (int s = tid; s < table_cap; s += NT) {
+        const int g = table.keys[s];
+        if (g < 0) continue;
+        const float* a = table.acc + s * ncomp;
+        if (a[0] != 0.f) atomicAdd(v_xy + 2 * g + 0, a[0]);
+        if (a[1] != 0.f) atomicAdd(v_xy + 2 * g + 1, a[1]);
+        if (a[2] != 0.f) atomicAdd(v_conic + 3 * g + 0, a[2]);
+        if (a[3] != 0.f) atomicAdd(v_conic + 3 * g + 1, a[3]);
+        if (a[4] != 0.f) atomicAdd(v_conic + 3 * g + 2, a[4]);
+        for (int c = 5; c < ncomp; ++c)
+            if (a[c] != 0.f) atomicAdd(v_rgb + channels * g + (c - 5), a[c]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Tile-less top-K forward (forward.cu:322-410): every pixel scans all N
+// Gaussians; Gaussians are staged through shared memory 1024 at a time.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) no_tiles_fwd_kernel(
+    unsigned img_w, unsigned img_h, int channels, int num_points, const float2* __restrict__ xys,
+    const float3* __restrict__ conics, const float* __restrict__ colors,
+    float* __restrict__ out_img, int* __restrict__ pixel_topk) {
+    __shared__ float4 s_a[1024];
+    __shared__ float s_b[1024];
+    const unsigned i = blockIdx.y * 32 + threadIdx.y;
+    const unsigned j = blockIdx.x * 32 + threadIdx.x;
+    const int tr = threadIdx.y * 32 + threadIdx.x;
+    const float px = (float)j;
+    const float py = (float)i;
+    const int pix_id = i * img_w + j;
+    const bool inside = (i < img_h && j < img_w);
+    int ids[kTopK];
+    float vals[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        ids[k] = -1;
+        vals[k] = 0.f;
+    }
+    int min_id = 0;
+    float min_val = -1.f;
+    for (int base = 0; base < num_points; base += 1024) {
+        __syncthreads();
+        if (base + tr < num_points) {
+            const float2 xy = xys[base + tr];
+            const float3 c = conics[base + tr];
+            s_a[tr] = make_float4(xy.x, xy.y, c.x, c.y);
+            s_b[tr] = c.z;
+        }
+        __syncthreads();
+        const int cnt = min(1024, num_points - base);
+        if (inside) {
+            for (int t = 0; t < cnt; ++t) {
+                const float4 a = s_a[t];
+                const float2 delta = {a.x - px, a.y - py};
+                const float sigma = gauss_sigma(make_float3(a.z, a.w, s_b[t]), delta);
+                if (sigma_invalid(sigma)) continue;
+                const float alpha = __expf(-sigma);
+                topk_insert<kTopK>(ids, vals, min_id, min_val, base + t, alpha);
+            }
+        }
+    }
+    if (!inside) return;
+    for (int c = 0; c < channels; ++c) {
+        float sum_val = 0.f;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k)
+            if (ids[k] >= 0) sum_val += vals[k];
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            const int g = ids[k];
+            if (g < 0) continue;
+            // float / double promotes: the reference divides in double here.
+            const float vis = (float)((double)vals[k] / ((double)sum_val + kEpsNoTiles));
+            acc += colors[g * channels + c] * vis;
+        }
+        out_img[pix_id * channels + c] = acc;
+    }
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) pixel_topk[pix_id * kTopK + k] = ids[k];
+}
+
+template <int BX, int BY, int SMEM_C>
+int launch_topk_bwd(unsigned img_w, unsigned img_h, int channels, int num_points, float eps,
+                    const float* xys, const float* conics, const float* colors,
+                    const float* v_output, const float* v_ws, const float* v_ent,
+                    const int* pixel_topk, float* v_xy, float* v_conic, float* v_colors,
+                    int table_cap, cudaStream_t stream) {
+    const int ncomp = 5 + (channels <= SMEM_C ? channels : 0);
+    const size_t smem = sizeof(int) * table_cap + sizeof(float) * (size_t)table_cap * ncomp;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    HX_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        HX_CUDA_TRY(cudaFuncSetAttribute(topk_bwd_kernel<BX, BY, SMEM_C>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(sizeof(int) * table_cap +
+                                               sizeof(float) * (size_t)table_cap * (5 + SMEM_C))));
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    dim3 grid(ceil_div((int)img_w, BX), ceil_div((int)img_h, BY));
+    dim3 block(BX, BY);
+    topk_bwd_kernel<BX, BY, SMEM_C><<<grid, block, smem, stream>>>(
+        img_w, img_h, channels, num_points, eps, (const float2*)xys, (const float3*)conics, colors,
+        v_output, v_ws, v_ent, pixel_topk, v_xy, v_conic, v_colors, table_cap);
+    HX_LAUNCH_CHECK("topk_bwd_kernel");
+    return HX_OK;
+}
+
+}  // namespace hx
+
+using namespace hx;
+
+extern "C" int hx_nd_rasterize_forward(int tiles_x, int tiles_y, unsigned img_width,
+                                       unsigned img_height, int channels,
+                                       const int32_t* gaussian_ids_sorted,
+                                       const int32_t* tile_bins, const float* xys,
+                                       const float* conics, const float* colors, float* out_img,
+                                       cudaStream_t stream) {
+    HX_REQUIRE(channels >= 1 && channels <= kMaxChannels,
+               "nd_rasterize_forward supports 1..%d channels (got %d)", kMaxChannels, channels);
+    HX_REQUIRE(tiles_x >= 0 && tiles_y >= 0, "bad tile bounds");
+    if (tiles_x == 0 || tiles_y == 0 || img_width == 0 || img_height == 0) return HX_OK;
+    HX_REQUIRE(gaussian_ids_sorted && tile_bins && xys && conics && colors && out_img,
+               "nd_rasterize_forward: null pointer");
+    dim3 grid(tiles_x, tiles_y), block(kBlockX, kBlockY);
+    if (channels <= 3)
+        sum_fwd_kernel<3><<<grid, block, 0, stream>>>(
+            tiles_x, img_width, img_height, channels, gaussian_ids_sorted, (const int2*)tile_bins,
+            (const float2*)xys, (const float3*)conics, colors, out_img);
+    else
+        sum_fwd_kernel<kMaxChannels><<<grid, block, 0, stream>>>(
+            tiles_x, img_width, img_height, channels, gaussian_ids_sorted, (const int2*)tile_bins,
+            (const float2*)xys, (const float3*)conics, colors, out_img);
+    HX_LAUNCH_CHECK("sum_fwd_kernel");
+    return HX_OK;
+}
+
+extern "C" int hx_nd_rasterize_backward(int tiles_x, int tiles_y, unsigned img_width,
+                                        unsigned img_height, int channels,
+                                        const int32_t* gaussian_ids_sorted,
+                                        const int32_t* tile_bins, const float* xys,
+                                        const float* conics, const float* colors,
+                                        const float* v_output, float* v_xy, float* v_conic,
+                                        float* v_colors, cudaStream_t stream) {
+    HX_REQUIRE(channels >= 1 && channels <= kMaxChannels,
+               "nd_rasterize_backward supports 1..%d channels (got %d)", kMaxChannels, channels);
+    if (tiles_x == 0 || tiles_y == 0 || img_width == 0 || img_height == 0) return HX_OK;
+    HX_REQUIRE(gaussian_ids_sorted && tile_bins && xys && conics && colors && v_output && v_xy &&
+                   v_conic && v_colors,
+               "nd_rasterize_backward: null pointer");
+    dim3 grid(tiles_x, tiles_y), block(kBlockX, kBlockY);
+    if (channels <= 3)
+        sum_bwd_kernel<3><<<grid, block, 0, stream>>>(
+            tiles_x, img_width, img_height, channels, gaussian_ids_sorted, (const int2*)tile_bins,
+            (const float2*)xys, (const float3*)conics, colors, v_output, v_xy, v_conic, v_colors);
+    else
+        sum_bwd_kernel<kMaxChannels><<<grid, block, 0, stream>>>(
+            tiles_x, img_width, img_height, channels, gaussian_ids_sorted, (const int2*)tile_bins,
+            (const float2*)xys, (const float3*)conics, colors, v_output, v_xy, v_conic, v_colors);
+    HX_LAUNCH_CHECK("sum_bwd_kernel");
+    return HX_OK;
+}
+
+extern "C" int hx_nd_rasterize_forward_topk_norm(
+    int tiles_x, int tiles_y, unsigned img_width, unsigned img_height, int channels,
+    const int32_t* gaussian_ids_sorted, const int32_t* tile_bins, const float* xys,
+    const float* conics, const float* colors, float* out_img, int32_t* pixel_topk,
+    float* weights_sum, float* entropy, cudaStream_t stream) {
+    HX_REQUIRE(channels >= 1, "nd_rasterize_forward_topk_norm: channels must be >= 1");
+    if (tiles_x == 0 || tiles_y == 0 || img_width == 0 || img_height == 0) return HX_OK;
+    HX_REQUIRE(gaussian_ids_sorted && tile_bins && xys && conics && colors && out_img && pixel_topk,
+               "nd_rasterize_forward_topk_norm: null pointer");
+    HX_REQUIRE((unsigned)ceil_div((int)img_width, kBlockX) <= (unsigned)tiles_x &&
+                   (unsigned)ceil_div((int)img_height, kBlockY) <= (unsigned)tiles_y,
+               "tile bounds do not cover the image");
+    dim3 grid(tiles_x, tiles_y), block(kBlockX, kBlockY);
+    topk_fwd_kernel<<<grid, block, 0, stream>>>(
+        tiles_x, img_width, img_height, channels, gaussian_ids_sorted, (const int2*)tile_bins,
+        (const float2*)xys, (const float3*)conics, colors, out_img, pixel_topk, weights_sum,
+        entropy);
+    HX_LAUNCH_CHECK("topk_fwd_kernel");
+    return HX_OK;
+}
+
+extern "C" int hx_nd_rasterize_backward_topk_norm(
+    unsigned img_width, unsigned img_height, int channels, int num_points, const float* xys,
+    const float* conics, const float* colors, const float* v_output, const float* v_weights_sum,
+    const float* v_entropy, const int32_t* pixel_topk, float* v_xy, float* v_conic,
+    float* v_colors, cudaStream_t stream) {
+    HX_REQUIRE(channels >= 1, "nd_rasterize_backward_topk_norm: channels must be >= 1");
+    if (img_width == 0 || img_height == 0 || num_points == 0) return HX_OK;
+    HX_REQUIRE(xys && conics && colors && v_output && pixel_topk && v_xy && v_conic && v_colors,
+               "nd_rasterize_backward_topk_norm: null pointer");
+    return launch_topk_bwd<16, 16, 4>(img_width, img_height, channels, num_points,
+                                      (float)kEpsTopK, xys, conics, colors, v_output,
+                                      v_weights_sum, v_entropy, pixel_topk, v_xy, v_conic,
+                                      v_colors, 1024, stream);
+}
+
+extern "C" int hx_nd_rasterize_forward_no_tiles(unsigned img_width, unsigned img_height,
+                                                int channels, int num_points, const float* xys,
+                                                const float* conics, const float* colors,
+                                                float* out_img, int32_t* pixel_topk,
+                                                cudaStream_t stream) {
+    HX_REQUIRE(channels >= 1, "nd_rasterize_forward_no_tiles: channels must be >= 1");
+    HX_REQUIRE(num_points >= 0, "nd_rasterize_forward_no_tiles: bad num_points");
+    if (img_width == 0 || img_height == 0) return HX_OK;
+    HX_REQUIRE(out_img && pixel_topk && (num_points == 0 || (xys && conics && colors)),
+               "nd_rasterize_forward_no_tiles: null pointer");
+    dim3 grid(ceil_div((int)img_width, 32), ceil_div((int)img_height, 32)), block(32, 32);
+    no_tiles_fwd_kernel<<<grid, block, 0, stream>>>(img_width, img_height, channels, num_points,
+                                                    (const float2*)xys, (const float3*)conics,
+                                                    colors, out_img, pixel_topk);
+    HX_LAUNCH_CHECK("no_tiles_fwd_kernel");
+    return HX_OK;
+}
+
+extern "C" int hx_nd_rasterize_backward_no_tiles(unsigned img_width, unsigned img_height,
+                                                 int channels, int num_points, const float* xys,
+                                                 const float* conics, const float* colors,
+                                                 const float* v_output, const int32_t* pixel_topk,
+                                                 float* v_xy, float* v_conic, float* v_colors,
+                                                 cudaStream_t stream) {
+    HX_REQUIRE(channels >= 1, "nd_rasterize_backward_no_tiles: channels must be >= 1");
+    if (img_width == 0 || img_height == 0 || num_points == 0) return HX_OK;
+    HX_REQUIRE(xys && conics && colors && v_output && pixel_topk && v_xy && v_conic && v_colors,
+               "nd_rasterize_backward_no_tiles: null pointer");
+    return launch_topk_bwd<32, 32, 4>(img_width, img_height, channels, num_points,
+                                      (float)kEpsNoTiles, xys, conics, colors, v_output, nullptr,
+                                      nullptr, pixel_topk, v_xy, v_conic, v_colors, 2048, stream);
+}

@@ -1,0 +1,108 @@
+"""Loader of ``libhexel_b200.so`` — the C-ABI declared in ``include/hexel_b200.h``.
+
+The Python host code in this package calls the CUDA kernels only through this
+module.  Pointers are raw device addresses (``Tensor.data_ptr()``), the stream
+is PyTorch's current stream on the tensors' device, and a non-zero status is
+raised as ``RuntimeError`` carrying the library's message.  There is no
+fallback: if the library is missing or was built for a different ABI version,
+importing this module fails.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+from typing import Optional
+
+import torch
+
+ABI_VERSION = 1
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libhexel_b200.so")
+
+_HEADER = os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+    "include", "hexel_b200.h",
+)
+
+_RET = {"int": ctypes.c_int, "size_t": ctypes.c_size_t, "const char*": ctypes.c_char_p,
+        "void": None, "unsigned long long": ctypes.c_ulonglong}
+
+
+def _arg_type(decl: str):
+    decl = decl.strip()
+    if "*" in decl or decl.startswith("cudaStream_t"):
+        return ctypes.c_void_p
+    base = decl.rsplit(" ", 1)[0].replace("const ", "").strip()
+    return {"int": ctypes.c_int, "unsigned": ctypes.c_uint, "float": ctypes.c_float,
+            "size_t": ctypes.c_size_t, "int32_t": ctypes.c_int32,
+            "int64_t": ctypes.c_int64}[base]
+
+
+def parse_header(path: str = _HEADER) -> dict:
+    """{name: (restype, [argtypes])} for every HX_API function of the header."""
+    text = re.sub(r"/\*.*?\*/", "", open(path).read(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"HX_API\s+(int|size_t|const char\*|void|unsigned long long)\s+"
+                         r"(hx_\w+)\s*\((.*?)\);",
+                         text, flags=re.S):
+        ret, name, args = m.group(1), m.group(2), " ".join(m.group(3).split())
+        argv = [] if args in ("", "void") else [_arg_type(a) for a in args.split(",")]
+        out[name] = (_RET[ret], argv)
+    return out
+
+
+class _Lib:
+    def __init__(self, path: str):
+        if not os.path.exists(path):
+            raise ImportError(
+                f"{path} is missing: build the CUDA library with "
+                "`python hexel-kernel_b200/build.py` (or __graft_entry__.build())."
+            )
+        self.path = path
+        self.dll = ctypes.CDLL(path)
+        self.signatures = parse_header()
+        for name, (res, args) in self.signatures.items():
+            fn = getattr(self.dll, name)
+            fn.restype = res
+            fn.argtypes = args
+        ver = self.dll.hx_abi_version()
+        if ver != ABI_VERSION:
+            raise ImportError(f"{path} has ABI version {ver}, expected {ABI_VERSION}; rebuild it")
+
+    def call(self, name: str, *args) -> None:
+        rc = getattr(self.dll, name)(*args)
+        if rc != 0:
+            msg = self.dll.hx_last_error().decode(errors="replace")
+            raise RuntimeError(f"{name} failed ({rc}): {msg}")
+
+    def query(self, name: str, *args) -> int:
+        return int(getattr(self.dll, name)(*args))
+
+
+lib = _Lib(_LIB_PATH)
+
+
+def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    """Device address of a tensor, or None (NULL) for an absent one."""
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def stream(device: torch.device) -> int:
+    """The current CUDA stream of `device` as a raw cudaStream_t."""
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    """Caller-owned scratch memory from PyTorch's caching allocator."""
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def check_input(t: torch.Tensor, name: str) -> None:
+    """Mirrors the reference's CHECK_INPUT (gsplat/cuda/csrc/bindings.h:10-15)."""
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")

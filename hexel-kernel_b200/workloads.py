@@ -1,0 +1,78 @@
+"""Seeded synthetic workloads of the benchmark configurations.
+
+The reference publishes no datasets or benchmark scenes for this path, so the
+inputs are synthetic, drawn on the CPU in fp32 from
+``torch.Generator().manual_seed(20261201 + config_index)``:
+
+  0  imagegs_small : Image-GS fit step, 256x256 RGB, 4,096 Gaussians
+  1  imagegs_large : Image-GS fit step, 2048x2048 RGB, 100,000 Gaussians
+  2  hexels2d      : 2D image hexels, 1024x1024 RGB, 50,000 hexagons
+
+Image-GS: means2d ~ U[0,1)^2, scales2d = exp(N(ln s0, 0.5)) pixels
+(s0 = 2 at 256^2; scaled with the image, s0 = 16 at 2048^2), rotation ~
+U[0, 2pi), colours ~ U[0,1], target image ~ U[0,1]; top-K=10 normalised
+weighted sum, 16x16 tiles, loss = mean((img - target)^2).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Dict
+
+import torch
+
+SEED_BASE = 20261201
+
+
+@dataclass
+class ImageGSWorkload:
+    name: str
+    height: int
+    width: int
+    means2d: torch.Tensor
+    scales2d: torch.Tensor
+    rotation: torch.Tensor
+    colors: torch.Tensor
+    target: torch.Tensor
+    extra: Dict[str, float] = field(default_factory=dict)
+
+    @property
+    def num_points(self) -> int:
+        return self.means2d.shape[0]
+
+    @property
+    def tile_bounds(self):
+        return ((self.width + 15) // 16, (self.height + 15) // 16, 1)
+
+    def to(self, device) -> "ImageGSWorkload":
+        kw = {k: getattr(self, k).to(device) for k in
+              ("means2d", "scales2d", "rotation", "colors", "target")}
+        return ImageGSWorkload(self.name, self.height, self.width, extra=dict(self.extra), **kw)
+
+
+def imagegs(config_index: int, height: int, width: int, num_points: int, scale_px: float,
+            name: str) -> ImageGSWorkload:
+    g = torch.Generator().manual_seed(SEED_BASE + config_index)
+    means2d = torch.rand((num_points, 2), generator=g, dtype=torch.float32)
+    scales2d = torch.exp(math.log(scale_px) + 0.5 * torch.randn((num_points, 2), generator=g))
+    rotation = 2 * math.pi * torch.rand((num_points, 1), generator=g, dtype=torch.float32)
+    colors = torch.rand((num_points, 3), generator=g, dtype=torch.float32)
+    target = torch.rand((height, width, 3), generator=g, dtype=torch.float32)
+    return ImageGSWorkload(name, height, width, means2d, scales2d.float(), rotation, colors,
+                           target, {"scale_px": scale_px})
+
+
+def imagegs_small() -> ImageGSWorkload:
+    return imagegs(0, 256, 256, 4096, 2.0, "imagegs_small_256x256_n4096")
+
+
+def imagegs_large() -> ImageGSWorkload:
+    return imagegs(1, 2048, 2048, 100_000, 2.0 * 2048 / 256, "imagegs_large_2048x2048_n100000")
+
+
+def imagegs_tiny(seed: int = 7, height: int = 48, width: int = 72, num_points: int = 96,
+                 scale_px: float = 3.0) -> ImageGSWorkload:
+    """Small ragged case for parity tests (image not a multiple of 16)."""
+    return imagegs(1000 + seed, height, width, num_points, scale_px,
+                   f"imagegs_tiny_{height}x{width}_n{num_points}")

@@ -1,0 +1,202 @@
+/*
+ * hexel_b200.h — C-ABI of the B200 (sm_100a) hexel / Image-GS rasteriser.
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA
+ * stream, launches hand-written sm_100a kernels on that stream and returns an
+ * hx_status.  None of them allocates device memory: outputs are written into
+ * caller buffers and any scratch space is passed in as a "workspace" whose
+ * size is reported by the matching *_workspace_bytes() query.  Layouts are the
+ * reference's: row-major, fp32 unless stated, int32 ids, int64 intersection
+ * keys.  Where a reference launcher returns zero-initialised tensors that its
+ * kernel only partly writes, the kernel here writes every element itself, so
+ * output buffers need no prior clearing unless the comment says so.
+ *
+ * Each declaration names the reference interface it replaces
+ * (honeycomb-surfels/hexel-kernel, path:line).  Optional pointer arguments
+ * are "absent" when NULL, mirroring the reference's empty-tensor convention.
+ */
+#ifndef HEXEL_B200_H
+#define HEXEL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#if defined(__GNUC__)
+#define HX_API __attribute__((visibility("default")))
+#else
+#define HX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HX_ABI_VERSION 1
+
+enum hx_status {
+    HX_OK = 0,
+    HX_ERR_INVALID_ARGUMENT = 1, /* bad size, pointer or option */
+    HX_ERR_CUDA = 2,             /* a CUDA runtime call or launch failed */
+    HX_ERR_WORKSPACE = 3,        /* workspace missing or too small */
+    HX_ERR_OVERFLOW = 4          /* a count does not fit in int32 */
+};
+
+/* ---- library ---------------------------------------------------------- */
+HX_API int hx_abi_version(void);
+/* Message describing the last failure on the calling host thread. */
+HX_API const char* hx_last_error(void);
+HX_API void hx_clear_error(void);
+/* Number of kernels this library has launched since it was loaded. */
+HX_API unsigned long long hx_launch_count(void);
+
+/* ---- S1: 2D Gaussian projection ---------------------------------------- */
+
+/* Replaces project_gaussians_2d_scale_rot_forward_tensor
+ * (gsplat/cuda/csrc/bindings.cu:2746-2797) and its kernel
+ * (gsplat/cuda/csrc/foward2d.cu:9-59).  means2d, scales2d: (N,2); rotation:
+ * (N,).  Writes xys (N,2), radii (N,), conics (N,3), num_tiles_hit (N,); all
+ * elements are written (zeros where the reference leaves its zero fill). */
+HX_API int hx_project_gaussians_2d_scale_rot_forward(
+    int num_points, const float* means2d, const float* scales2d, const float* rotation,
+    unsigned img_height, unsigned img_width, int tiles_x, int tiles_y,
+    float* xys, int32_t* radii, float* conics, int32_t* num_tiles_hit, cudaStream_t stream);
+
+/* Replaces project_gaussians_2d_scale_rot_backward_tensor
+ * (gsplat/cuda/csrc/bindings.cu:2800-2846; kernel backward2d.cu:53-100).
+ * Writes v_cov2d (N,3), v_mean2d (N,2), v_scale (N,2), v_rot (N,); zeros for
+ * culled points (radii <= 0). */
+HX_API int hx_project_gaussians_2d_scale_rot_backward(
+    int num_points, const float* means2d, const float* scales2d, const float* rotation,
+    unsigned img_height, unsigned img_width, const int32_t* radii, const float* conics,
+    const float* v_xy, const float* v_conic,
+    float* v_cov2d, float* v_mean2d, float* v_scale, float* v_rot, cudaStream_t stream);
+
+/* Replaces compute_cov2d_bounds_tensor (gsplat/cuda/csrc/bindings.cu:20-60).
+ * covs2d (N,3) upper triangle -> conics (N,3), radii (N,) as float.  Rows
+ * with a zero determinant get zeros (the reference leaves them undefined). */
+HX_API int hx_compute_cov2d_bounds(int num_points, const float* covs2d, float* conics, float* radii,
+                            cudaStream_t stream);
+
+/* ---- S2 / S7: scan, intersection keys, radix sort, tile ranges ---------- */
+
+/* Inclusive int32 prefix sum; replaces torch.cumsum(num_tiles_hit, int32)
+ * (gsplat/utils.py:113) and cub::DeviceScan::InclusiveSum
+ * (gsplat/cuda_hexels3d/csrc/hexels3d_forward.cu:2975-2981).  total_out
+ * (device int64, may be NULL) receives the sum computed in 64 bits so that an
+ * int32 overflow of the running sum can be detected by the caller. */
+HX_API size_t hx_scan_workspace_bytes(int n);
+HX_API int hx_inclusive_scan_i32(const int32_t* in, int32_t* out, int n, int64_t* total_out,
+                          void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Replaces map_gaussian_to_intersects_tensor (gsplat/cuda/csrc/bindings.cu:62-97;
+ * kernel forward.cu:13-44).  Writes isect_ids (I,) = (tile << 32) | 0 and
+ * gaussian_ids (I,) in Gaussian-major, tile-row-major order.  Writes are
+ * bounded by num_intersects. */
+HX_API int hx_map_gaussian_to_intersects(
+    int num_points, int num_intersects, const float* xys, const int32_t* radii,
+    const int32_t* cum_tiles_hit, int tiles_x, int tiles_y,
+    int64_t* isect_ids, int32_t* gaussian_ids, cudaStream_t stream);
+
+/* Stable LSD radix sort of (uint64 key, int32 value) pairs on key bits
+ * [begin_bit, end_bit).  Replaces torch.sort + torch.gather of the 2D path
+ * (gsplat/utils.py:159-160) and cub::DeviceRadixSort::SortPairs of the 3D
+ * path (hexels3d_forward.cu:3011-3035).  Inputs are not modified. */
+HX_API size_t hx_sort_pairs_workspace_bytes(int n, int key_bytes);
+HX_API int hx_sort_pairs_u64(const uint64_t* keys_in, const int32_t* vals_in, uint64_t* keys_out,
+                      int32_t* vals_out, int n, int begin_bit, int end_bit,
+                      void* workspace, size_t workspace_bytes, cudaStream_t stream);
+HX_API int hx_sort_pairs_u32(const uint32_t* keys_in, const int32_t* vals_in, uint32_t* keys_out,
+                      int32_t* vals_out, int n, int begin_bit, int end_bit,
+                      void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Replaces get_tile_bin_edges_tensor (gsplat/cuda/csrc/bindings.cu:99-116;
+ * kernel forward.cu:49-71).  tile_bins (num_tiles,2) is fully written:
+ * [first, last+1) for occupied tiles, (0,0) for empty ones. */
+HX_API int hx_get_tile_bin_edges(int num_intersects, int num_tiles, const int64_t* isect_ids_sorted,
+                          int32_t* tile_bins, cudaStream_t stream);
+
+/* Fused 2D binning used by rasterize_gaussians_sum: the composition of
+ * map_gaussian_to_intersects, a stable sort by tile and get_tile_bin_edges
+ * (gsplat/utils.py:118-162) without materialising 64-bit keys.  Produces
+ * gaussian_ids_sorted (I,), tile_bins (num_tiles,2) and, if isect_ids_sorted
+ * is not NULL, the sorted 64-bit keys.  Results are identical to the
+ * reference's sorted lists (within a tile: ascending Gaussian id).
+ * tile_row_begin/tile_row_end restrict emission to a horizontal stripe of
+ * tile rows (pass 0 and tiles_y for the whole image); cum_tiles_hit must then
+ * count only the stripe's tiles (see hx_count_tiles_2d). */
+HX_API size_t hx_bin_gaussians_2d_workspace_bytes(int num_intersects, int num_tiles);
+HX_API int hx_bin_gaussians_2d(
+    int num_points, int num_intersects, const float* xys, const int32_t* radii,
+    const int32_t* cum_tiles_hit, int tiles_x, int tiles_y, int tile_row_begin, int tile_row_end,
+    int32_t* gaussian_ids_sorted, int32_t* tile_bins, int64_t* isect_ids_sorted,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Per-Gaussian count of tiles in rows [tile_row_begin, tile_row_end) of its
+ * tile rectangle (the same rectangle as map_gaussian_to_intersects); used to
+ * shard an image into horizontal stripes of tile rows. */
+HX_API int hx_count_tiles_2d(int num_points, const float* xys, const int32_t* radii, int tiles_x,
+                      int tiles_y, int tile_row_begin, int tile_row_end, int32_t* counts,
+                      cudaStream_t stream);
+
+/* ---- S3: Image-GS compositing ------------------------------------------ */
+
+/* Replaces nd_rasterize_forward_tensor (gsplat/cuda/csrc/bindings.cu:175-232;
+ * kernel forward.cu:76-170) and rasterize_forward_tensor (bindings.cu:118-173,
+ * channels == 3).  Plain sum of colour * exp(-sigma) per pixel.  channels <= 12.
+ * out_img (H,W,C). */
+HX_API int hx_nd_rasterize_forward(
+    int tiles_x, int tiles_y, unsigned img_width, unsigned img_height, int channels,
+    const int32_t* gaussian_ids_sorted, const int32_t* tile_bins, const float* xys,
+    const float* conics, const float* colors, float* out_img, cudaStream_t stream);
+
+/* Replaces nd_rasterize_backward_tensor (bindings.cu:234-308; kernel
+ * backward.cu:23-157) and rasterize_backward_tensor (bindings.cu:2683-2744).
+ * v_xy (N,2), v_conic (N,3), v_colors (N,C) are ACCUMULATED into: clear them
+ * first. */
+HX_API int hx_nd_rasterize_backward(
+    int tiles_x, int tiles_y, unsigned img_width, unsigned img_height, int channels,
+    const int32_t* gaussian_ids_sorted, const int32_t* tile_bins, const float* xys,
+    const float* conics, const float* colors, const float* v_output,
+    float* v_xy, float* v_conic, float* v_colors, cudaStream_t stream);
+
+/* Replaces nd_rasterize_forward_topk_norm_tensor and _stats_tensor
+ * (bindings.cu:310-444; kernel forward.cu:172-320).  Top-10 normalised
+ * weighted sum.  out_img (H,W,C), pixel_topk (H,W,10) int32 (-1 = empty);
+ * weights_sum (H,W) and entropy (H,W) are optional. */
+HX_API int hx_nd_rasterize_forward_topk_norm(
+    int tiles_x, int tiles_y, unsigned img_width, unsigned img_height, int channels,
+    const int32_t* gaussian_ids_sorted, const int32_t* tile_bins, const float* xys,
+    const float* conics, const float* colors, float* out_img, int32_t* pixel_topk,
+    float* weights_sum, float* entropy, cudaStream_t stream);
+
+/* Replaces nd_rasterize_backward_topk_norm_tensor and _stats_tensor
+ * (bindings.cu:446-565; kernel backward.cu:159-316).  v_weights_sum and
+ * v_entropy (H,W) are optional.  Gradients are ACCUMULATED: clear them first. */
+HX_API int hx_nd_rasterize_backward_topk_norm(
+    unsigned img_width, unsigned img_height, int channels, int num_points, const float* xys,
+    const float* conics, const float* colors, const float* v_output,
+    const float* v_weights_sum, const float* v_entropy, const int32_t* pixel_topk,
+    float* v_xy, float* v_conic, float* v_colors, cudaStream_t stream);
+
+/* ---- S4: tile-less Image-GS -------------------------------------------- */
+
+/* Replaces nd_rasterize_forward_no_tiles_tensor (bindings.cu:2459-2510;
+ * kernel forward.cu:322-410). */
+HX_API int hx_nd_rasterize_forward_no_tiles(
+    unsigned img_width, unsigned img_height, int channels, int num_points, const float* xys,
+    const float* conics, const float* colors, float* out_img, int32_t* pixel_topk,
+    cudaStream_t stream);
+
+/* Replaces nd_rasterize_backward_no_tiles_tensor (bindings.cu:2512-2565;
+ * kernel backward.cu:318-438).  Gradients are ACCUMULATED: clear them first. */
+HX_API int hx_nd_rasterize_backward_no_tiles(
+    unsigned img_width, unsigned img_height, int channels, int num_points, const float* xys,
+    const float* conics, const float* colors, const float* v_output, const int32_t* pixel_topk,
+    float* v_xy, float* v_conic, float* v_colors, cudaStream_t stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* HEXEL_B200_H */

@@ -1,0 +1,79 @@
+"""CPU checks of the C-ABI boundary: the library loads, exports every symbol
+that include/hexel_b200.h declares, reports its ABI version and rejects bad
+arguments with a status code and a message (no GPU work is launched)."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "hexel_b200.h")
+LIB = os.path.join(ROOT, "hexel-kernel_b200", "gsplat", "libhexel_b200.so")
+
+
+def declared():
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    return re.findall(r"HX_API\s+[\w\s\*]+?\s+\**(hx_\w+)\s*\(", text)
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    assert len(names) == len(set(names))
+    assert "hx_nd_rasterize_forward_topk_norm" in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(LIB)
+    missing = [n for n in declared() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_abi_version_and_error_path():
+    from gsplat._lib import lib, ABI_VERSION
+
+    assert lib.dll.hx_abi_version() == ABI_VERSION
+    with pytest.raises(RuntimeError, match="non-negative"):
+        lib.call("hx_project_gaussians_2d_scale_rot_forward", -1, None, None, None, 4, 4, 1, 1,
+                 None, None, None, None, None)
+    with pytest.raises(RuntimeError, match="bit range"):
+        lib.call("hx_sort_pairs_u64", None, None, None, None, 10, 0, 65, None, 0, None)
+    with pytest.raises(RuntimeError, match="workspace"):
+        lib.call("hx_sort_pairs_u32", 1, 1, 1, 1, 10, 0, 8, None, 0, None)
+
+
+def test_python_surface_matches_reference_names():
+    import gsplat
+    import gsplat.cuda as C
+    from gsplat import csrc
+
+    two_d = """nd_rasterize_forward nd_rasterize_backward nd_rasterize_forward_topk_norm
+    nd_rasterize_backward_topk_norm nd_rasterize_forward_topk_norm_stats
+    nd_rasterize_backward_topk_norm_stats nd_rasterize_forward_no_tiles
+    nd_rasterize_backward_no_tiles nd_rasterize_forward_simple nd_rasterize_backward_simple
+    rasterize_forward rasterize_backward project_gaussians_2d_scale_rot_forward
+    project_gaussians_2d_scale_rot_backward compute_cov2d_bounds map_gaussian_to_intersects
+    get_tile_bin_edges""".split()
+    for n in two_d:
+        assert callable(getattr(csrc, n)), n
+        assert callable(getattr(C, n)), n
+    for n in ("project_gaussians_2d_scale_rot", "rasterize_gaussians_sum",
+              "rasterize_gaussians_no_tiles", "rasterize_gaussians_simple",
+              "bin_and_sort_gaussians", "compute_cumulative_intersects", "compute_cov2d_bounds",
+              "get_tile_bin_edges", "map_gaussian_to_intersects"):
+        assert callable(getattr(gsplat, n)), n
+
+
+def test_cpu_tensors_rejected_like_reference():
+    import torch
+    from gsplat import csrc
+
+    x = torch.zeros(4, 2)
+    with pytest.raises(RuntimeError, match="gaussian_ids_sorted must be a CUDA tensor"):
+        csrc.nd_rasterize_forward_topk_norm((1, 1, 1), (16, 16, 1), (16, 16, 1),
+                                            torch.zeros(4, dtype=torch.int32),
+                                            torch.zeros(1, 2, dtype=torch.int32), x,
+                                            torch.zeros(4, 3), torch.zeros(4, 3))

@@ -76,3 +76,63 @@ def imagegs_tiny(seed: int = 7, height: int = 48, width: int = 72, num_points: i
     """Small ragged case for parity tests (image not a multiple of 16)."""
     return imagegs(1000 + seed, height, width, num_points, scale_px,
                    f"imagegs_tiny_{height}x{width}_n{num_points}")
+
+
+@dataclass
+class HexelsWorkload:
+    """2D image hexels: pixel-space centres, scale/rotation geometry and the
+    binning radius the caller uses (the reference's hexel kernels take their
+    binning from the caller)."""
+
+    name: str
+    height: int
+    width: int
+    xys: torch.Tensor        # (N,2) pixel centres
+    scales: torch.Tensor     # (N,2)
+    rotation: torch.Tensor   # (N,1)
+    colors: torch.Tensor     # (N,3)
+    radii: torch.Tensor      # (N,) int32 binning radius in pixels
+    target: torch.Tensor
+    softness: float = 10.0
+    aa_kernel_size: float = 0.0
+    extra: Dict[str, torch.Tensor] = field(default_factory=dict)
+
+    @property
+    def num_points(self) -> int:
+        return self.xys.shape[0]
+
+    @property
+    def tile_bounds(self):
+        return ((self.width + 15) // 16, (self.height + 15) // 16, 1)
+
+
+def hexels(config_index: int, height: int, width: int, num_points: int, radius_px: float,
+           softness: float, name: str) -> HexelsWorkload:
+    """Centres ~ U[0,W) x U[0,H), circumradius R = exp(N(ln r0, 0.4)) pixels,
+    scales = (R sqrt(3)/2, R sqrt(3)/2) (the SDF's circumradius along u is
+    (2/sqrt(3)) s_x and its apothem along v is s_y), rotation ~ U[0, pi/3),
+    colours ~ U[0,1].  The opacity ~ sigmoid(N(0,1)) draw of the configuration
+    is made (to keep the random stream) but is not an input of these kernels.
+    Binning radius: ceil(R (1 + ln(254) / softness)) + 1 pixels."""
+    g = torch.Generator().manual_seed(SEED_BASE + config_index)
+    xys = torch.rand((num_points, 2), generator=g) * torch.tensor([float(width), float(height)])
+    R = torch.exp(math.log(radius_px) + 0.4 * torch.randn((num_points,), generator=g))
+    s = R * (math.sqrt(3.0) / 2.0)
+    scales = torch.stack([s, s], 1).float()
+    rotation = (math.pi / 3.0) * torch.rand((num_points, 1), generator=g)
+    colors = torch.rand((num_points, 3), generator=g)
+    opacity = torch.sigmoid(torch.randn((num_points,), generator=g))
+    target = torch.rand((height, width, 3), generator=g)
+    radii = (torch.ceil(R * (1.0 + math.log(254.0) / softness)) + 1).to(torch.int32)
+    return HexelsWorkload(name, height, width, xys.float(), scales, rotation.float(), colors,
+                          radii, target, softness, 0.0, {"opacity_unused": opacity})
+
+
+def hexels2d() -> HexelsWorkload:
+    return hexels(2, 1024, 1024, 50_000, 4.0, 10.0, "hexels2d_1024x1024_n50000")
+
+
+def hexels2d_tiny(seed: int = 3, height: int = 40, width: int = 56,
+                  num_points: int = 60) -> HexelsWorkload:
+    return hexels(2000 + seed, height, width, num_points, 4.0, 10.0,
+                  f"hexels2d_tiny_{height}x{width}_n{num_points}")

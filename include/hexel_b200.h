@@ -195,6 +195,42 @@ HX_API int hx_nd_rasterize_backward_no_tiles(
     const float* conics, const float* colors, const float* v_output, const int32_t* pixel_topk,
     float* v_xy, float* v_conic, float* v_colors, cudaStream_t stream);
 
+/* ---- S5: 2D image hexels ------------------------------------------------ */
+
+/* One entry point for the eight forward variants
+ * nd_rasterize_forward_topk_norm_hexels[_color_grad][_affine][_softness]
+ * (gsplat/cuda/csrc/bindings.cu:566-2457; kernels hexels_forward.cu:169-859).
+ * Geometry: scales (N,2) + rotation (N,) when affines is NULL, else affines
+ * (N,2,2) in the row-vector convention.  color_grads (N,2,C) selects the
+ * linear colour-gradient variant.  softnesses (N,) or (N,3) with
+ * softness_stride 1 or 3, or NULL to use softness_default.  sharpness (N,) and
+ * emission (N,C) optional.  Writes out_img (H,W,C), pixel_topk (H,W,10) and,
+ * if given, weights_sum and entropy (H,W). */
+HX_API int hx_hexels2d_forward(
+    int tiles_x, int tiles_y, unsigned img_width, unsigned img_height, int channels,
+    int num_points, const int32_t* gaussian_ids_sorted, const int32_t* tile_bins,
+    const float* xys, const float* scales, const float* rotation, const float* affines,
+    const float* colors, const float* color_grads, float color_grad_scale, float aa_kernel_size,
+    const float* softnesses, int softness_stride, float softness_default, const float* sharpness,
+    const float* emission, float* out_img, int32_t* pixel_topk, float* weights_sum,
+    float* entropy, cudaStream_t stream);
+
+/* One entry point for the eight backward variants (bindings.cu:911-2457;
+ * kernels hexels_backward.cu:233-1387).  Gradient outputs are ACCUMULATED
+ * (clear them first): v_xy (N,2); v_scale (N,2) + v_rot (N,) or v_affines
+ * (N,4); v_colors (N,C); v_color_grads (N,2,C) with color_grads; v_emission
+ * (N,C) with emission; v_sharpness (N,) with sharpness; v_softnesses shaped
+ * like softnesses. */
+HX_API int hx_hexels2d_backward(
+    unsigned img_width, unsigned img_height, int channels, int num_points, const float* xys,
+    const float* scales, const float* rotation, const float* affines, const float* colors,
+    const float* color_grads, float color_grad_scale, const float* emission,
+    const float* v_output, const float* v_weights_sum, const float* v_entropy,
+    const int32_t* pixel_topk, float aa_kernel_size, const float* softnesses, int softness_stride,
+    float softness_default, const float* sharpness, float* v_xy, float* v_scale, float* v_rot,
+    float* v_affines, float* v_colors, float* v_color_grads, float* v_emission,
+    float* v_sharpness, float* v_softnesses, cudaStream_t stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -252,6 +252,24 @@ def _sigma(xy, conic, px, py):
             dx, dy)
 
 
+FLT_MIN = 1.1754943508222875e-38
+
+
+def _ftz(x):
+    """Flush subnormal results to zero, as the reference's fast-math build
+    (-ftz=true) does for every single-precision result."""
+    if x.dtype != torch.float32:
+        return x
+    return torch.where(x.abs() < FLT_MIN, torch.zeros_like(x), x)
+
+
+def _fexp(x):
+    """exp() with the reference's flush-to-zero of subnormal results: weights
+    of far-away primitives become exactly 0, which decides which of them fill
+    empty top-K slots."""
+    return _ftz(torch.exp(x))
+
+
 def _bad(sigma):
     return (sigma < 0) | torch.isnan(sigma) | torch.isinf(sigma)
 
@@ -324,7 +342,7 @@ def rasterize_topk_forward(xys, conics, colors, ids_sorted, tile_bins, img_h, im
     def cands():
         for g, sigma in _candidates(tl, ids_sorted, xys, conics):
             ok = (g >= 0) & ~_bad(sigma)
-            alpha = torch.exp(-sigma)
+            alpha = _fexp(-sigma)
             yield torch.where(ok, g, torch.full_like(g, -1)), alpha
 
     ids, vals = _topk_select(cands(), npix)
@@ -370,7 +388,7 @@ def rasterize_topk_backward(xys, conics, colors, v_output, pixel_topk, img_h, im
     xy = xys.to(f32)[g]        # (P,K,2)
     cn = conics.to(f32)[g]     # (P,K,3)
     sigma, dx, dy = _sigma(xy, cn, px[:, None], py[:, None])
-    d = torch.where(valid, torch.exp(-sigma), 0.0)
+    d = torch.where(valid, _fexp(-sigma), 0.0)
     denom = torch.full((P,), float(np.float32(eps)), dtype=f32)
     for k in range(TOP_K):
         denom = denom + torch.where(valid[:, k], d[:, k], 0.0)
@@ -421,7 +439,7 @@ def rasterize_sum_forward(xys, conics, colors, ids_sorted, tile_bins, img_h, img
     out = torch.zeros((tl.i.size, colors.shape[1]), dtype=f32)
     for g, sigma in _candidates(tl, ids_sorted, xys, conics):
         ok = (g >= 0) & ~_bad(sigma)
-        vis = torch.exp(-sigma)
+        vis = _fexp(-sigma)
         out = out + torch.where(ok[:, None], colors[g.clamp(min=0)] * vis[:, None], 0.0)
     return _scatter((img_h, img_w, colors.shape[1]), tl, out)
 
@@ -450,7 +468,7 @@ def rasterize_sum_backward(xys, conics, colors, ids_sorted, tile_bins, v_output,
         pos = torch.where(has, start + jj, torch.zeros_like(start))
         g = torch.where(has, ids_sorted[pos], torch.zeros_like(pos))
         sigma, dx, dy = _sigma(xys[g], conics[g], tl.px, tl.py)
-        d = torch.exp(-sigma)
+        d = _fexp(-sigma)
         valid = valid & ~(has & _bad(sigma))
         use = valid & has
         v_sigma = (colors[g] * vout).sum(1) * -d
@@ -478,7 +496,7 @@ def rasterize_no_tiles_forward(xys, conics, colors, img_h, img_w):
         for g in range(xys.shape[0]):
             sigma, _, _ = _sigma(xys[g], conics[g], px, py)
             ok = ~_bad(sigma)
-            yield torch.where(ok, torch.full((P,), g), torch.full((P,), -1)), torch.exp(-sigma)
+            yield torch.where(ok, torch.full((P,), g), torch.full((P,), -1)), _fexp(-sigma)
 
     ids, vals = _topk_select(cands(), P)
     valid = ids >= 0

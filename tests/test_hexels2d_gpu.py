@@ -1,0 +1,208 @@
+"""GPU parity of the sixteen 2D image-hexel entry points against the CPU
+oracle and, when built, the reference's own CUDA kernels (oracle/_ref).
+
+Tolerances: top-K ids bit-exact against the reference kernels; images and
+statistics 1e-5 absolute; gradients 1e-4 relative / 1e-6 absolute against the
+reference kernels (atomic order differs), 1e-3 relative against the CPU
+oracle (IEEE vs fast-math exp and division).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ref_module
+
+pytestmark = pytest.mark.gpu
+
+VARIANTS = [(aff, cg, soft) for aff in (False, True) for cg in (False, True)
+            for soft in (None, 1, 3)]
+
+
+@pytest.fixture(scope="module")
+def ref():
+    return ref_module("_ref_gsplat_csrc")
+
+
+def _name(aff, cg, soft_stride, direction):
+    n = f"nd_rasterize_{direction}_topk_norm_hexels"
+    if cg:
+        n += "_color_grad"
+    if aff:
+        n = n.replace("_hexels", "_hexels_affine") if not cg else \
+            f"nd_rasterize_{direction}_topk_norm_hexels_affine_color_grad"
+    if soft_stride:
+        n += "_softness"
+    return n
+
+
+def _scene(seed=3, H=40, W=56, n=60, extras=True):
+    import workloads
+    from gsplat.utils import bin_and_sort_gaussians, compute_cumulative_intersects, \
+        count_tiles_in_rows
+
+    w = workloads.hexels2d_tiny(seed, H, W, n)
+    dev = "cuda"
+    g = torch.Generator().manual_seed(seed)
+    d = dict(
+        xys=w.xys.to(dev), scales=w.scales.to(dev), rotation=w.rotation.to(dev),
+        colors=w.colors.to(dev),
+        affines=(torch.tensor([[0.3, 0.02], [-0.03, 0.28]]).repeat(n, 1, 1)
+                 * (0.8 + 0.4 * torch.rand((n, 1, 1), generator=g))).to(dev),
+        color_grads=(0.05 * torch.randn((n, 2, 3), generator=g)).to(dev),
+        soft1=(8 + 4 * torch.rand((n,), generator=g)).to(dev),
+        soft3=(8 + 4 * torch.rand((n, 3), generator=g)).to(dev),
+        sharpness=(0.02 + 0.05 * torch.rand((n,), generator=g)).to(dev) if extras else
+        torch.zeros(0, device=dev),
+        emission=(0.1 * torch.rand((n, 3), generator=g)).to(dev) if extras else
+        torch.zeros(0, device=dev),
+    )
+    tb = w.tile_bounds
+    radii = w.radii.to(dev)
+    nth = count_tiles_in_rows(d["xys"], radii, tb, (0, tb[1]))
+    ni, cum = compute_cumulative_intersects(nth)
+    _, _, _, ids, bins = bin_and_sort_gaussians(n, ni, d["xys"], radii, cum, tb)
+    return w, d, ids, bins
+
+
+def _fwd_args(aff, cg, soft, d, w, ids, bins, aa):
+    args = [w.tile_bounds, (16, 16, 1), (w.width, w.height, 1), ids, bins, d["xys"]]
+    args += [d["affines"]] if aff else [d["scales"], d["rotation"]]
+    args += [d["colors"]]
+    if cg:
+        args += [d["color_grads"], 0.7]
+    args += [aa]
+    if soft:
+        args += [d["soft1"] if soft == 1 else d["soft3"], w.softness]
+    else:
+        args += [w.softness]
+    args += [d["sharpness"], d["emission"]]
+    return args
+
+
+def _bwd_args(aff, cg, soft, d, w, ids, bins, aa, v_out, v_ws, v_en, topk):
+    args = [w.height, w.width, 16, 16, ids, bins, d["xys"]]
+    args += [d["affines"]] if aff else [d["scales"], d["rotation"]]
+    args += [d["colors"]]
+    if cg:
+        args += [d["color_grads"]]
+    if soft:
+        args += [d["soft1"] if soft == 1 else d["soft3"]]
+    if cg:
+        args += [0.7]
+    args += [v_out, v_ws, v_en, topk, aa]
+    args += [w.softness]
+    args += [d["sharpness"], d["emission"]]
+    return args
+
+
+def _oracle_params(aff, cg, soft, d, w, aa):
+    from oracle.hexels2d import HexParams
+
+    c = lambda t: t.detach().cpu()  # noqa: E731
+    p = HexParams(xys=c(d["xys"]), colors=c(d["colors"]), softness=w.softness, aa=aa)
+    if aff:
+        p.affines = c(d["affines"])
+    else:
+        p.scales, p.rotation = c(d["scales"]), c(d["rotation"])
+    if cg:
+        p.color_grads, p.color_grad_scale = c(d["color_grads"]), 0.7
+    if soft:
+        p.softnesses = c(d["soft1"] if soft == 1 else d["soft3"])
+    p.sharpness = c(d["sharpness"])
+    p.emission = c(d["emission"])
+    return p
+
+
+@pytest.mark.parametrize("aff,cg,soft", VARIANTS)
+@pytest.mark.parametrize("aa", [0.0, 0.3])
+def test_hexel_variant(ref, aff, cg, soft, aa):
+    from gsplat import csrc
+    from oracle import hexels2d as oh
+
+    w, d, ids, bins = _scene()
+    fwd = getattr(csrc, _name(aff, cg, soft, "forward"))
+    img, topk, ws, ent = fwd(*_fwd_args(aff, cg, soft, d, w, ids, bins, aa))
+    p = _oracle_params(aff, cg, soft, d, w, aa)
+    o_img, o_topk, o_ws, o_ent = oh.forward(p, ids.cpu(), bins.cpu().numpy(), w.height, w.width)
+    same = (topk.cpu() == o_topk).all(-1)
+    assert same.float().mean() > 0.999
+    torch.testing.assert_close(img.cpu()[same], o_img[same], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(ws.cpu()[same], o_ws[same], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(ent.cpu()[same], o_ent[same], rtol=1e-4, atol=1e-5)
+
+    g = torch.Generator().manual_seed(11)
+    v_out = (torch.rand(img.shape, generator=g) * 2 - 1).cuda()
+    v_ws = (0.1 * torch.randn(ws.shape, generator=g)).cuda()
+    v_en = (0.1 * torch.randn(ent.shape, generator=g)).cuda()
+    bwd = getattr(csrc, _name(aff, cg, soft, "backward"))
+    out = bwd(*_bwd_args(aff, cg, soft, d, w, ids, bins, aa, v_out, v_ws, v_en, topk))
+    og = oh.backward(p, v_out.cpu(), v_ws.cpu(), v_en.cpu(), topk.cpu(), w.height, w.width)
+    names = ["v_xy"] + (["v_affines"] if aff else ["v_scale", "v_rot"]) + ["v_colors"]
+    names += (["v_color_grads"] if cg else []) + ["v_emission", "v_sharpness"]
+    names += ["v_softnesses"] if soft else []
+    assert len(out) == len(names)
+    for name, t in zip(names, out):
+        if name in og:
+            torch.testing.assert_close(t.cpu().reshape(og[name].shape), og[name], rtol=1e-3,
+                                       atol=1e-5, msg=name)
+    if ref is not None:
+        r = getattr(ref, _name(aff, cg, soft, "forward"))(*_fwd_args(aff, cg, soft, d, w, ids,
+                                                                     bins, aa))
+        assert torch.equal(topk, r[1])
+        for a, b in zip((img, ws, ent), (r[0], r[2], r[3])):
+            torch.testing.assert_close(a, b, rtol=0, atol=1e-5)
+        rb = getattr(ref, _name(aff, cg, soft, "backward"))(
+            *_bwd_args(aff, cg, soft, d, w, ids, bins, aa, v_out, v_ws, v_en, topk))
+        assert len(rb) == len(out)
+        for name, a, b in zip(names, out, rb):
+            assert a.shape == b.shape, name
+            torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-6, msg=name)
+
+
+def test_hexel_empty_tiles_and_absent_extras(ref):
+    """Tiles with no primitives take the fast path (zeros, -1, EPS, 0); empty
+    sharpness/emission tensors mean absent."""
+    from gsplat import csrc
+
+    w, d, ids, bins = _scene(seed=5, H=64, W=80, n=6, extras=False)
+    img, topk, ws, ent = csrc.nd_rasterize_forward_topk_norm_hexels(
+        *_fwd_args(False, False, None, d, w, ids, bins, 0.0))
+    empty = (bins[:, 1] == bins[:, 0]).cpu()
+    assert bool(empty.any())
+    ty, tx = torch.nonzero(empty.view(w.tile_bounds[1], w.tile_bounds[0]))[0].tolist()
+    blk = (slice(ty * 16, ty * 16 + 16), slice(tx * 16, tx * 16 + 16))
+    assert float(img[blk].abs().sum()) == 0.0
+    assert bool((topk[blk] == -1).all())
+    assert torch.allclose(ws[blk], torch.tensor(1e-4, device="cuda"))
+    if ref is not None:
+        r = ref.nd_rasterize_forward_topk_norm_hexels(
+            *_fwd_args(False, False, None, d, w, ids, bins, 0.0))
+        assert torch.equal(topk, r[1]) and torch.equal(ws, r[2])
+
+
+def test_hexels_config3_properties():
+    """1024^2 / 50k hexels (the 2D-hexel benchmark configuration): finite,
+    deterministic, weights in range."""
+    import workloads
+    from gsplat import csrc
+    from gsplat.utils import bin_gaussians_fused, compute_cumulative_intersects, \
+        count_tiles_in_rows
+
+    w = workloads.hexels2d()
+    xys, radii = w.xys.cuda(), w.radii.cuda()
+    nth = count_tiles_in_rows(xys, radii, w.tile_bounds, (0, w.tile_bounds[1]))
+    ni, cum = compute_cumulative_intersects(nth)
+    ids, bins = bin_gaussians_fused(w.num_points, ni, xys, radii, cum, w.tile_bounds)
+    args = (w.tile_bounds, (16, 16, 1), (w.width, w.height, 1), ids, bins, xys, w.scales.cuda(),
+            w.rotation.cuda(), w.colors.cuda(), 0.0, w.softness, torch.zeros(0, device="cuda"),
+            torch.zeros(0, device="cuda"))
+    a = csrc.nd_rasterize_forward_topk_norm_hexels(*args)
+    b = csrc.nd_rasterize_forward_topk_norm_hexels(*args)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+    img, topk, ws, ent = a
+    assert torch.isfinite(img).all() and float(img.min()) >= 0 and float(img.max()) <= 1 + 1e-5
+    assert bool((topk[..., 0] >= 0).any())

@@ -176,6 +176,8 @@ __device__ __forceinline__ float hex_alpha(const HexPrim& p, float dx, float dy,
 
 struct HexFwdArgs {
     int tiles_x;
+    int num_points;
+    int num_intersects;
     unsigned img_w, img_h;
     int channels;
     const int* ids_sorted;
@@ -212,7 +214,9 @@ __global__ void __launch_bounds__(256) hexel_fwd_kernel(const HexFwdArgs a) {
     const bool inside = (i < a.img_h && j < a.img_w);
     const int C = a.channels;
 
-    const int2 range = a.tile_bins[tile_id];
+    int2 range = a.tile_bins[tile_id];
+    range.y = min(range.y, a.num_intersects);
+    range.x = max(0, min(range.x, range.y));
     if (range.x == range.y) {
         if (inside) {
             for (int c = 0; c < C; ++c) a.out_img[pix_id * C + c] = 0.f;
@@ -240,7 +244,8 @@ __global__ void __launch_bounds__(256) hexel_fwd_kernel(const HexFwdArgs a) {
         __syncthreads();
         const int idx = batch_start + tr;
         if (idx < range.y) {
-            s_prim[tr] = make_prim<AFFINE>(a.ids_sorted[idx], a.xys, a.scales, a.rotation,
+            const int g = min(max(a.ids_sorted[idx], 0), a.num_points - 1);
+            s_prim[tr] = make_prim<AFFINE>(g, a.xys, a.scales, a.rotation,
                                            a.affines, a.aa, a.softnesses, a.softness_stride,
                                            a.softness_default, a.sharpness);
         }
@@ -740,26 +745,28 @@ int launch_bwd(HexBwdArgs a, cudaStream_t stream) {
 
 extern "C" int hx_hexels2d_forward(
     int tiles_x, int tiles_y, unsigned img_width, unsigned img_height, int channels,
-    int num_points, const int32_t* gaussian_ids_sorted, const int32_t* tile_bins,
-    const float* xys, const float* scales, const float* rotation, const float* affines,
+    int num_points, int num_intersects, const int32_t* gaussian_ids_sorted,
+    const int32_t* tile_bins, const float* xys, const float* scales, const float* rotation, const float* affines,
     const float* colors, const float* color_grads, float color_grad_scale, float aa_kernel_size,
     const float* softnesses, int softness_stride, float softness_default, const float* sharpness,
     const float* emission, float* out_img, int32_t* pixel_topk, float* weights_sum,
     float* entropy, cudaStream_t stream) {
-    (void)num_points;
     HX_REQUIRE(channels >= 1, "hexels2d_forward: channels must be >= 1");
     HX_REQUIRE(softness_stride == 0 || softness_stride == 1 || softness_stride == 3,
                "hexels2d_forward: softness_stride must be 0, 1 or 3");
     if (tiles_x == 0 || tiles_y == 0 || img_width == 0 || img_height == 0) return HX_OK;
     const bool affine = affines != nullptr;
-    HX_REQUIRE(gaussian_ids_sorted && tile_bins && xys && colors && out_img && pixel_topk &&
-                   (affine || (scales && rotation)),
+    HX_REQUIRE(tile_bins && out_img && pixel_topk, "hexels2d_forward: null pointer");
+    HX_REQUIRE(num_intersects == 0 || (gaussian_ids_sorted && num_points > 0 && xys && colors &&
+                                       (affine || (scales && rotation))),
                "hexels2d_forward: null pointer");
     HX_REQUIRE((unsigned)ceil_div((int)img_width, kBlockX) <= (unsigned)tiles_x &&
                    (unsigned)ceil_div((int)img_height, kBlockY) <= (unsigned)tiles_y,
                "tile bounds do not cover the image");
     HexFwdArgs a;
     a.tiles_x = tiles_x;
+    a.num_points = num_points;
+    a.num_intersects = num_intersects;
     a.img_w = img_width;
     a.img_h = img_height;
     a.channels = channels;

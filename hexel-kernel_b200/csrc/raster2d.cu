@@ -22,6 +22,20 @@ namespace hx {
 constexpr double kEpsTopK = 1e-4;     // EPS (config.h:9)
 constexpr double kEpsNoTiles = 1e-7;  // EPS_no_tiles (config.h:10)
 
+// A tile's [start, end) range clipped to the intersection list, and a
+// primitive id clamped into [0, num_points): malformed bins or ids then read
+// valid memory instead of faulting (their output is unspecified, as in the
+// reference).
+__device__ __forceinline__ int2 clamp_range(int2 r, int num_intersects) {
+    r.y = min(r.y, num_intersects);
+    r.x = max(0, min(r.x, r.y));
+    return r;
+}
+
+__device__ __forceinline__ int clamp_id(int g, int num_points) {
+    return min(max(g, 0), num_points - 1);
+}
+
 // Gaussian falloff exponent at pixel offset delta = xy - pixel.
 __device__ __forceinline__ float gauss_sigma(const float3 conic, const float2 delta) {
     return 0.5f * (conic.x * delta.x * delta.x + conic.z * delta.y * delta.y) +
@@ -74,7 +88,7 @@ __device__ __forceinline__ void topk_insert(int (&ids)[K], float (&vals)[K], int
 // Top-K forward (forward.cu:172-320), one 16x16 tile per CTA.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) topk_fwd_kernel(
-    int tiles_x, unsigned img_w, unsigned img_h, int channels,
+    int tiles_x, unsigned img_w, unsigned img_h, int channels, int num_points, int num_intersects,
     const int* __restrict__ gaussian_ids_sorted, const int2* __restrict__ tile_bins,
     const float2* __restrict__ xys, const float3* __restrict__ conics,
     const float* __restrict__ colors, float* __restrict__ out_img, int* __restrict__ pixel_topk,
@@ -91,7 +105,7 @@ __global__ void __launch_bounds__(256) topk_fwd_kernel(
     const int pix_id = i * img_w + j;
     const bool inside = (i < img_h && j < img_w);
 
-    const int2 range = tile_bins[tile_id];
+    const int2 range = clamp_range(tile_bins[tile_id], num_intersects);
     int ids[kTopK];
     float vals[kTopK];
 #pragma unroll
@@ -106,7 +120,7 @@ __global__ void __launch_bounds__(256) topk_fwd_kernel(
         __syncthreads();
         const int idx = batch_start + tr;
         if (idx < range.y) {
-            const int g = gaussian_ids_sorted[idx];
+            const int g = clamp_id(gaussian_ids_sorted[idx], num_points);
             const float2 xy = xys[g];
             const float3 c = conics[g];
             s_a[tr] = make_float4(xy.x, xy.y, c.x, c.y);
@@ -165,7 +179,7 @@ __global__ void __launch_bounds__(256) topk_fwd_kernel(
 // ---------------------------------------------------------------------------
 template <int MAXC>
 __global__ void __launch_bounds__(256) sum_fwd_kernel(
-    int tiles_x, unsigned img_w, unsigned img_h, int channels,
+    int tiles_x, unsigned img_w, unsigned img_h, int channels, int num_points, int num_intersects,
     const int* __restrict__ gaussian_ids_sorted, const int2* __restrict__ tile_bins,
     const float2* __restrict__ xys, const float3* __restrict__ conics,
     const float* __restrict__ colors, float* __restrict__ out_img) {
@@ -179,7 +193,7 @@ __global__ void __launch_bounds__(256) sum_fwd_kernel(
     const float py = (float)i;
     const int pix_id = i * img_w + j;
     const bool inside = (i < img_h && j < img_w);
-    const int2 range = tile_bins[tile_id];
+    const int2 range = clamp_range(tile_bins[tile_id], num_intersects);
     float pix_out[MAXC];
 #pragma unroll
     for (int c = 0; c < MAXC; ++c) pix_out[c] = 0.f;
@@ -188,7 +202,7 @@ __global__ void __launch_bounds__(256) sum_fwd_kernel(
         __syncthreads();
         const int idx = batch_start + tr;
         if (idx < range.y) {
-            const int g = gaussian_ids_sorted[idx];
+            const int g = clamp_id(gaussian_ids_sorted[idx], num_points);
             const float2 xy = xys[g];
             const float3 c = conics[g];
             s_a[tr] = make_float4(xy.x, xy.y, c.x, c.y);
@@ -231,7 +245,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 template <int MAXC>
 __global__ void __launch_bounds__(256) sum_bwd_kernel(
-    int tiles_x, unsigned img_w, unsigned img_h, int channels,
+    int tiles_x, unsigned img_w, unsigned img_h, int channels, int num_points, int num_intersects,
     const int* __restrict__ gaussian_ids_sorted, const int2* __restrict__ tile_bins,
     const float2* __restrict__ xys, const float3* __restrict__ conics,
     const float* __restrict__ colors, const float* __restrict__ v_output,
@@ -251,7 +265,7 @@ __global__ void __launch_bounds__(256) sum_bwd_kernel(
     const float py = (float)i;
     const int pix_id = min(i * img_w + j, img_w * img_h - 1);
     const bool inside = (i < img_h && j < img_w);
-    const int2 range = tile_bins[tile_id];
+    const int2 range = clamp_range(tile_bins[tile_id], num_intersects);
 
     float v_out[MAXC];
 #pragma unroll
@@ -262,7 +276,7 @@ __global__ void __launch_bounds__(256) sum_bwd_kernel(
         __syncthreads();
         const int idx = batch_start + tr;
         if (idx < range.y) {
-            const int g = gaussian_ids_sorted[idx];
+            const int g = clamp_id(gaussian_ids_sorted[idx], num_points);
             const float2 xy = xys[g];
             const float3 c = conics[g];
             s_a[tr] = make_float4(xy.x, xy.y, c.x, c.y);
@@ -629,7 +643,8 @@ int launch_topk_bwd(unsigned img_w, unsigned img_h, int channels, int num_points
 using namespace hx;
 
 extern "C" int hx_nd_rasterize_forward(int tiles_x, int tiles_y, unsigned img_width,
-                                       unsigned img_height, int channels,
+                                       unsigned img_height, int channels, int num_points,
+                                       int num_intersects,
                                        const int32_t* gaussian_ids_sorted,
                                        const int32_t* tile_bins, const float* xys,
                                        const float* conics, const float* colors, float* out_img,
@@ -638,23 +653,28 @@ extern "C" int hx_nd_rasterize_forward(int tiles_x, int tiles_y, unsigned img_wi
                "nd_rasterize_forward supports 1..%d channels (got %d)", kMaxChannels, channels);
     HX_REQUIRE(tiles_x >= 0 && tiles_y >= 0, "bad tile bounds");
     if (tiles_x == 0 || tiles_y == 0 || img_width == 0 || img_height == 0) return HX_OK;
-    HX_REQUIRE(gaussian_ids_sorted && tile_bins && xys && conics && colors && out_img,
+    HX_REQUIRE(tile_bins && out_img, "nd_rasterize_forward: null pointer");
+    HX_REQUIRE(num_intersects == 0 || (gaussian_ids_sorted && num_points > 0 && xys && conics &&
+                                       colors),
                "nd_rasterize_forward: null pointer");
     dim3 grid(tiles_x, tiles_y), block(kBlockX, kBlockY);
     if (channels <= 3)
         sum_fwd_kernel<3><<<grid, block, 0, stream>>>(
-            tiles_x, img_width, img_height, channels, gaussian_ids_sorted, (const int2*)tile_bins,
+            tiles_x, img_width, img_height, channels, num_points, num_intersects,
+            gaussian_ids_sorted, (const int2*)tile_bins,
             (const float2*)xys, (const float3*)conics, colors, out_img);
     else
         sum_fwd_kernel<kMaxChannels><<<grid, block, 0, stream>>>(
-            tiles_x, img_width, img_height, channels, gaussian_ids_sorted, (const int2*)tile_bins,
+            tiles_x, img_width, img_height, channels, num_points, num_intersects,
+            gaussian_ids_sorted, (const int2*)tile_bins,
             (const float2*)xys, (const float3*)conics, colors, out_img);
     HX_LAUNCH_CHECK("sum_fwd_kernel");
     return HX_OK;
 }
 
 extern "C" int hx_nd_rasterize_backward(int tiles_x, int tiles_y, unsigned img_width,
-                                        unsigned img_height, int channels,
+                                        unsigned img_height, int channels, int num_points,
+                                        int num_intersects,
                                         const int32_t* gaussian_ids_sorted,
                                         const int32_t* tile_bins, const float* xys,
                                         const float* conics, const float* colors,
@@ -663,17 +683,20 @@ extern "C" int hx_nd_rasterize_backward(int tiles_x, int tiles_y, unsigned img_w
     HX_REQUIRE(channels >= 1 && channels <= kMaxChannels,
                "nd_rasterize_backward supports 1..%d channels (got %d)", kMaxChannels, channels);
     if (tiles_x == 0 || tiles_y == 0 || img_width == 0 || img_height == 0) return HX_OK;
+    if (num_intersects == 0 || num_points == 0) return HX_OK;
     HX_REQUIRE(gaussian_ids_sorted && tile_bins && xys && conics && colors && v_output && v_xy &&
                    v_conic && v_colors,
                "nd_rasterize_backward: null pointer");
     dim3 grid(tiles_x, tiles_y), block(kBlockX, kBlockY);
     if (channels <= 3)
         sum_bwd_kernel<3><<<grid, block, 0, stream>>>(
-            tiles_x, img_width, img_height, channels, gaussian_ids_sorted, (const int2*)tile_bins,
+            tiles_x, img_width, img_height, channels, num_points, num_intersects,
+            gaussian_ids_sorted, (const int2*)tile_bins,
             (const float2*)xys, (const float3*)conics, colors, v_output, v_xy, v_conic, v_colors);
     else
         sum_bwd_kernel<kMaxChannels><<<grid, block, 0, stream>>>(
-            tiles_x, img_width, img_height, channels, gaussian_ids_sorted, (const int2*)tile_bins,
+            tiles_x, img_width, img_height, channels, num_points, num_intersects,
+            gaussian_ids_sorted, (const int2*)tile_bins,
             (const float2*)xys, (const float3*)conics, colors, v_output, v_xy, v_conic, v_colors);
     HX_LAUNCH_CHECK("sum_bwd_kernel");
     return HX_OK;
@@ -681,19 +704,23 @@ extern "C" int hx_nd_rasterize_backward(int tiles_x, int tiles_y, unsigned img_w
 
 extern "C" int hx_nd_rasterize_forward_topk_norm(
     int tiles_x, int tiles_y, unsigned img_width, unsigned img_height, int channels,
+    int num_points, int num_intersects,
     const int32_t* gaussian_ids_sorted, const int32_t* tile_bins, const float* xys,
     const float* conics, const float* colors, float* out_img, int32_t* pixel_topk,
     float* weights_sum, float* entropy, cudaStream_t stream) {
     HX_REQUIRE(channels >= 1, "nd_rasterize_forward_topk_norm: channels must be >= 1");
     if (tiles_x == 0 || tiles_y == 0 || img_width == 0 || img_height == 0) return HX_OK;
-    HX_REQUIRE(gaussian_ids_sorted && tile_bins && xys && conics && colors && out_img && pixel_topk,
+    HX_REQUIRE(tile_bins && out_img && pixel_topk, "nd_rasterize_forward_topk_norm: null pointer");
+    HX_REQUIRE(num_intersects == 0 || (gaussian_ids_sorted && num_points > 0 && xys && conics &&
+                                       colors),
                "nd_rasterize_forward_topk_norm: null pointer");
     HX_REQUIRE((unsigned)ceil_div((int)img_width, kBlockX) <= (unsigned)tiles_x &&
                    (unsigned)ceil_div((int)img_height, kBlockY) <= (unsigned)tiles_y,
                "tile bounds do not cover the image");
     dim3 grid(tiles_x, tiles_y), block(kBlockX, kBlockY);
     topk_fwd_kernel<<<grid, block, 0, stream>>>(
-        tiles_x, img_width, img_height, channels, gaussian_ids_sorted, (const int2*)tile_bins,
+        tiles_x, img_width, img_height, channels, num_points, num_intersects,
+        gaussian_ids_sorted, (const int2*)tile_bins,
         (const float2*)xys, (const float3*)conics, colors, out_img, pixel_topk, weights_sum,
         entropy);
     HX_LAUNCH_CHECK("topk_fwd_kernel");

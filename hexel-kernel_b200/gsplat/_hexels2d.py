@@ -83,7 +83,8 @@ def _forward(tile_bounds, block, img_size, ids, bins, xys, colors, *, scales=Non
     weights_sum = torch.zeros((h, w), dtype=torch.float32, device=dev)
     entropy = torch.zeros((h, w), dtype=torch.float32, device=dev)
     with torch.cuda.device(dev):
-        lib.call("hx_hexels2d_forward", tb[0], tb[1], w, h, channels, n, ptr(ids), ptr(bins),
+        lib.call("hx_hexels2d_forward", tb[0], tb[1], w, h, channels, n, ids.numel(), ptr(ids),
+                 ptr(bins),
                  ptr(xys), ptr(scales), ptr(rotation), ptr(affines), ptr(colors),
                  ptr(color_grads), float(color_grad_scale), float(aa_kernel_size), ptr(soft),
                  stride, float(softness_default), ptr(sh), ptr(em), ptr(out_img),

@@ -147,8 +147,8 @@ def nd_rasterize_forward(tile_bounds, block, img_size, gaussian_ids_sorted, tile
     dev = xys.device
     out_img = torch.zeros((h, w, channels), dtype=torch.float32, device=dev)
     with torch.cuda.device(dev):
-        lib.call("hx_nd_rasterize_forward", tb[0], tb[1], w, h, channels,
-                 ptr(gaussian_ids_sorted), ptr(tile_bins), ptr(xys), ptr(conics), ptr(colors),
+        lib.call("hx_nd_rasterize_forward", tb[0], tb[1], w, h, channels, xys.size(0),
+                 gaussian_ids_sorted.numel(), ptr(gaussian_ids_sorted), ptr(tile_bins), ptr(xys), ptr(conics), ptr(colors),
                  ptr(out_img), stream(dev))
     return (out_img,)
 
@@ -181,7 +181,7 @@ def nd_rasterize_backward(img_height, img_width, BLOCK_H, BLOCK_W, gaussians_ids
     v_output = v_output.contiguous()
     with torch.cuda.device(dev):
         lib.call("hx_nd_rasterize_backward", tx, ty, int(img_width), int(img_height), channels,
-                 ptr(gaussians_ids_sorted.contiguous()), ptr(tile_bins.contiguous()), ptr(xys),
+                 n, gaussians_ids_sorted.numel(), ptr(gaussians_ids_sorted.contiguous()), ptr(tile_bins.contiguous()), ptr(xys),
                  ptr(conics.contiguous()), ptr(colors), ptr(v_output), ptr(v_xy), ptr(v_conic),
                  ptr(v_colors), stream(dev))
     return v_xy, v_conic, v_colors
@@ -207,8 +207,8 @@ def _topk_forward(tile_bounds, block, img_size, gaussian_ids_sorted, tile_bins, 
     weights_sum = torch.zeros((h, w), dtype=torch.float32, device=dev) if stats else None
     entropy = torch.zeros((h, w), dtype=torch.float32, device=dev) if stats else None
     with torch.cuda.device(dev):
-        lib.call("hx_nd_rasterize_forward_topk_norm", tb[0], tb[1], w, h, channels,
-                 ptr(gaussian_ids_sorted), ptr(tile_bins), ptr(xys), ptr(conics), ptr(colors),
+        lib.call("hx_nd_rasterize_forward_topk_norm", tb[0], tb[1], w, h, channels, xys.size(0),
+                 gaussian_ids_sorted.numel(), ptr(gaussian_ids_sorted), ptr(tile_bins), ptr(xys), ptr(conics), ptr(colors),
                  ptr(out_img), ptr(pixel_topk), ptr(weights_sum), ptr(entropy), stream(dev))
     if stats:
         return out_img, pixel_topk, weights_sum, entropy

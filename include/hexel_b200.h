@@ -141,13 +141,17 @@ HX_API int hx_count_tiles_2d(int num_points, const float* xys, const int32_t* ra
 
 /* ---- S3: Image-GS compositing ------------------------------------------ */
 
+/* Compositing kernels take num_points (N) and num_intersects (length of
+ * gaussian_ids_sorted): tile ranges are clipped to the list and ids clamped
+ * into [0, N), so malformed bins cannot make a kernel read out of bounds. */
+
 /* Replaces nd_rasterize_forward_tensor (gsplat/cuda/csrc/bindings.cu:175-232;
  * kernel forward.cu:76-170) and rasterize_forward_tensor (bindings.cu:118-173,
  * channels == 3).  Plain sum of colour * exp(-sigma) per pixel.  channels <= 12.
  * out_img (H,W,C). */
 HX_API int hx_nd_rasterize_forward(
     int tiles_x, int tiles_y, unsigned img_width, unsigned img_height, int channels,
-    const int32_t* gaussian_ids_sorted, const int32_t* tile_bins, const float* xys,
+    int num_points, int num_intersects, const int32_t* gaussian_ids_sorted, const int32_t* tile_bins, const float* xys,
     const float* conics, const float* colors, float* out_img, cudaStream_t stream);
 
 /* Replaces nd_rasterize_backward_tensor (bindings.cu:234-308; kernel
@@ -156,7 +160,7 @@ HX_API int hx_nd_rasterize_forward(
  * first. */
 HX_API int hx_nd_rasterize_backward(
     int tiles_x, int tiles_y, unsigned img_width, unsigned img_height, int channels,
-    const int32_t* gaussian_ids_sorted, const int32_t* tile_bins, const float* xys,
+    int num_points, int num_intersects, const int32_t* gaussian_ids_sorted, const int32_t* tile_bins, const float* xys,
     const float* conics, const float* colors, const float* v_output,
     float* v_xy, float* v_conic, float* v_colors, cudaStream_t stream);
 
@@ -166,7 +170,7 @@ HX_API int hx_nd_rasterize_backward(
  * weights_sum (H,W) and entropy (H,W) are optional. */
 HX_API int hx_nd_rasterize_forward_topk_norm(
     int tiles_x, int tiles_y, unsigned img_width, unsigned img_height, int channels,
-    const int32_t* gaussian_ids_sorted, const int32_t* tile_bins, const float* xys,
+    int num_points, int num_intersects, const int32_t* gaussian_ids_sorted, const int32_t* tile_bins, const float* xys,
     const float* conics, const float* colors, float* out_img, int32_t* pixel_topk,
     float* weights_sum, float* entropy, cudaStream_t stream);
 
@@ -208,7 +212,7 @@ HX_API int hx_nd_rasterize_backward_no_tiles(
  * if given, weights_sum and entropy (H,W). */
 HX_API int hx_hexels2d_forward(
     int tiles_x, int tiles_y, unsigned img_width, unsigned img_height, int channels,
-    int num_points, const int32_t* gaussian_ids_sorted, const int32_t* tile_bins,
+    int num_points, int num_intersects, const int32_t* gaussian_ids_sorted, const int32_t* tile_bins,
     const float* xys, const float* scales, const float* rotation, const float* affines,
     const float* colors, const float* color_grads, float color_grad_scale, float aa_kernel_size,
     const float* softnesses, int softness_stride, float softness_default, const float* sharpness,

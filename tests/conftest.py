@@ -33,6 +33,37 @@ def pytest_collection_modifyitems(config, items):
             item.add_marker(skip)
 
 
+def assert_grad_parity(mine, ref, exact=None, name: str = ""):
+    """Gradient parity against the reference kernels.
+
+    Both sides sum per-pixel contributions with fp32 atomics in different
+    orders, so entries that cancel to near zero carry absolute noise
+    proportional to the magnitude of the summed terms.  Criterion, per entry:
+        |mine - ref| <= 1e-4 * |ref| + 1e-5 * max|ref|
+    and, when the float64 oracle `exact` is given, ours must be at least as
+    accurate as the reference (up to a 1e-7 * max|exact| slack):
+        max|mine - exact| <= 2 * max|ref - exact| + 1e-7 * max|exact|.
+    """
+    import torch
+
+    a = mine.detach().double().cpu().reshape(-1)
+    b = ref.detach().double().cpu().reshape(-1)
+    assert a.shape == b.shape, name
+    scale = float(b.abs().max()) if b.numel() else 0.0
+    bound = 1e-4 * b.abs() + 1e-5 * scale
+    bad = (a - b).abs() > bound
+    assert not bool(bad.any()), (
+        f"{name}: {int(bad.sum())}/{b.numel()} entries differ; max |diff| "
+        f"{float((a - b).abs().max()):.3e}, scale {scale:.3e}")
+    if exact is not None:
+        e = exact.detach().double().cpu().reshape(-1)
+        err_mine = float((a - e).abs().max()) if e.numel() else 0.0
+        err_ref = float((b - e).abs().max()) if e.numel() else 0.0
+        emax = float(e.abs().max()) if e.numel() else 0.0
+        assert err_mine <= 2 * err_ref + 1e-7 * emax, (
+            f"{name}: error vs float64 oracle {err_mine:.3e} exceeds reference's {err_ref:.3e}")
+
+
 def ref_module(name: str):
     """The reference's CUDA extension built from its sources into oracle/_ref
     (see oracle/build_ref.py), or None when it was not built."""

@@ -1,0 +1,938 @@
+// S8 backward: reverse traversal of the front-to-back compositing and the VJP
+// to the ray-splat transforms and appearance parameters (reference
+// gsplat/cuda_hexels3d/csrc/hexels3d_forward.cu:1749-2492), and the VJP from
+// transforms to geometry (hexels3d_forward.cu:2494-2664).
+//
+// Per-pixel arithmetic is the reference's.  The schedule is B200-specific:
+//   * one CTA per 16x16 tile walks the tile's list back to front in lock step
+//     (pixel p is active for list index i < its own last index), with the
+//     surfels of each 256-entry batch staged in shared memory instead of
+//     re-read from global memory by every pixel;
+//   * the per-(pixel, surfel) gradient vector (up to 64 components) is summed
+//     over the warp with a butterfly reduce-scatter (N - N/32 shuffles, each
+//     lane ends with N/32 component sums), added into a per-batch
+//     shared-memory accumulator, and flushed with one global atomic per
+//     (surfel, component) per tile — instead of ~33 global atomics per
+//     (pixel, surfel);
+//   * gradients that factor through per-surfel constants (linear view-model
+//     gradients and the matching view-direction gradient) are formed once per
+//     surfel at flush time from the accumulated colour gradient;
+//   * with surface outputs the forward's saved per-pixel state replaces the
+//     reference's forward re-walk.
+#include "hx_cmat.cuh"
+#include "hx_hexmath3d.cuh"
+
+namespace hx {
+
+struct BwdLayout {
+    int ncomp;
+    int off_cg, off_cq, off_op, off_soft, off_tm, off_vd, off_n, off_ks, off_ls, off_abs, off_ctr;
+    bool derive_vg, derive_vd;
+};
+
+// Fixed slot layout of the common configurations (flat or linear colour,
+// no or linear view model): colour 0-2, colour gradients 3-8, opacity 9,
+// softness 10-12, transform 13-21, normal 22-24, screen-gradient norm 25,
+// prefilter centre 26-27, explicit view direction 28-30.
+constexpr int kFixCg = 3, kFixOp = 9, kFixSoft = 10, kFixTm = 13, kFixN = 22, kFixAbs = 25,
+              kFixCtr = 26, kFixVd = 28, kFixComp = 31;
+
+template <int N>
+__device__ __forceinline__ int warp_reduce_scatter(float (&v)[N], const int lane) {
+    int start = 0;
+#pragma unroll
+    for (int o = 16, n = N; o >= 1; o >>= 1, n >>= 1) {
+        const int half = n / 2;
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+        if (upper) start += half;
+    }
+    return start;
+}
+
+template <bool SURF, bool PREFILTER, int N>
+__global__ void __launch_bounds__(256) render3d_bwd_kernel(const Backward3DArgs a,
+                                                           const BwdLayout L) {
+    extern __shared__ __align__(16) unsigned char s_raw[];
+    Surfel3D* s_prim = reinterpret_cast<Surfel3D*>(s_raw);
+    float* s_acc = reinterpret_cast<float*>(s_raw + sizeof(Surfel3D) * k3BlockSize);
+    __shared__ int s_max_visit;
+
+    // N == 32 uses the fixed slot layout below (compile-time indices keep
+    // the per-pixel gradient vector in registers); N == 64 takes the
+    // host-computed layout for the quadratic colour and lobe view models.
+    constexpr bool FIX = (N == 32);
+    const int O_cg = FIX ? kFixCg : L.off_cg;
+    const int O_cq = FIX ? 0 : L.off_cq;
+    const int O_op = FIX ? kFixOp : L.off_op;
+    const int O_soft = FIX ? kFixSoft : L.off_soft;
+    const int O_tm = FIX ? kFixTm : L.off_tm;
+    const int O_vd = FIX ? kFixVd : L.off_vd;
+    const int O_n = FIX ? kFixN : L.off_n;
+    const int O_ks = FIX ? 0 : L.off_ks;
+    const int O_ls = FIX ? 0 : L.off_ls;
+    const int O_abs = FIX ? kFixAbs : L.off_abs;
+    const int O_ctr = FIX ? kFixCtr : L.off_ctr;
+
+    const int W = a.W, H = a.H;
+    const unsigned hblocks = (W + k3BlockX - 1) / k3BlockX;
+    const unsigned px_i = blockIdx.x * k3BlockX + threadIdx.x;
+    const unsigned py_i = blockIdx.y * k3BlockY + threadIdx.y;
+    const bool inside = px_i < (unsigned)W && py_i < (unsigned)H;
+    const unsigned pix_id = inside ? (unsigned)(W * (int)py_i + (int)px_i) : 0u;
+    const float px = (float)px_i;
+    const float py = (float)py_i;
+    const int tr = threadIdx.y * k3BlockX + threadIdx.x;
+    const int lane = tr & 31;
+    const int HW = H * W;
+
+    uint2 range = a.ranges[blockIdx.y * hblocks + blockIdx.x];
+    range.y = min(range.y, (unsigned)a.num_rendered);
+    range.x = min(range.x, range.y);
+    const int range_len = (int)(range.y - range.x);
+    if (range_len <= 0) return;  // uniform across the CTA
+
+    float v_out_r = 0.f, v_out_g = 0.f, v_out_b = 0.f, v_overdraw = 0.f;
+    float v_surf_depth = 0.f, v_surf_alpha = 0.f, v_surf_dist = 0.f, v_surf_median = 0.f;
+    float3 v_surf_normal = {0.f, 0.f, 0.f};
+    float T_after = 1.f, T_after_surf = 1.f, M1 = 0.f, M2 = 0.f;
+    int n_color = 0, n_surf = 0, median_index = -1;
+    if (inside) {
+        v_out_r = a.grad_out_color[pix_id];
+        v_out_g = a.grad_out_color[HW + pix_id];
+        v_out_b = a.grad_out_color[2 * HW + pix_id];
+        if (a.grad_out_overdraw) v_overdraw = a.grad_out_overdraw[pix_id];
+        T_after = a.final_T[pix_id];
+        n_color = min(a.last_index[pix_id], range_len);
+        if (SURF) {
+            if (a.grad_out_surf_depth) v_surf_depth = a.grad_out_surf_depth[pix_id];
+            if (a.grad_out_surf_alpha) v_surf_alpha = a.grad_out_surf_alpha[pix_id];
+            if (a.grad_out_surf_normals) {
+                v_surf_normal = {a.grad_out_surf_normals[pix_id],
+                                 a.grad_out_surf_normals[HW + pix_id],
+                                 a.grad_out_surf_normals[2 * HW + pix_id]};
+                v_surf_dist = a.grad_out_surf_normals[3 * HW + pix_id];
+                if (a.has_median_grad) v_surf_median = a.grad_out_surf_normals[4 * HW + pix_id];
+            }
+            T_after_surf = a.final_T_surf[pix_id];
+            n_surf = min(a.last_index_surf[pix_id], range_len);
+            M1 = a.m1_surf[pix_id];
+            M2 = a.m2_surf[pix_id];
+            median_index = a.median_index[pix_id];
+        }
+    }
+    const int n_max = SURF ? max(n_color, n_surf) : n_color;
+    if (tr == 0) s_max_visit = 0;
+    __syncthreads();
+    if (n_max > 0) atomicMax(&s_max_visit, n_max);
+    __syncthreads();
+    const int block_max = s_max_visit;
+
+    float3 behind = {a.bg[0], a.bg[1], a.bg[2]};
+    float behind_depth = 0.f, behind_alpha = 0.f;
+    float3 behind_normal = {0.f, 0.f, 0.f};
+    float last_dist_vjp = 0.f;
+    const float final_alpha_surf = 1.0f - T_after_surf;
+    const float bg0 = behind.x;
+    (void)bg0;
+
+    const int nb = (block_max + k3BlockSize - 1) / k3BlockSize;
+    for (int b = nb - 1; b >= 0; --b) {
+        const int bstart = b * k3BlockSize;
+        const int bend = min(bstart + k3BlockSize, block_max);
+        __syncthreads();
+        if (bstart + tr < bend) {
+            int g = a.point_list[range.x + bstart + tr];
+            g = min(max(g, 0), a.P - 1);
+            Surfel3D& s = s_prim[tr];
+            s.id = g;
+            const float* Tm = a.transMats + 9 * g;
+#pragma unroll
+            for (int q = 0; q < 3; ++q) {
+                s.tu[q] = Tm[q];
+                s.tv[q] = Tm[3 + q];
+                s.tw[q] = Tm[6 + q];
+            }
+            s.opacity = a.opacities[g];
+            if (a.softness_stride == 3) {
+                s.s0 = a.softnesses[3 * g];
+                s.s1 = a.softnesses[3 * g + 1];
+                s.s2 = a.softnesses[3 * g + 2];
+            } else {
+                s.s0 = s.s1 = s.s2 = a.softnesses[g];
+            }
+#pragma unroll
+            for (int q = 0; q < 3; ++q) s.cb[q] = a.colors[3 * g + q];
+            if (a.color_model >= kColorLinear) {
+#pragma unroll
+                for (int q = 0; q < 3; ++q) {
+                    s.gu[q] = a.color_grads[6 * g + q];
+                    s.gv[q] = a.color_grads[6 * g + 3 + q];
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < 3; ++q) s.gu[q] = s.gv[q] = 0.f;
+            }
+            if (a.use_view_grads) {
+                const float* vd = a.view_dirs + 3 * g;
+                const float* vg = a.view_grads + 9 * g;
+                s.cv[0] = vd[0] * vg[0] + vd[1] * vg[1] + vd[2] * vg[2];
+                s.cv[1] = vd[0] * vg[3] + vd[1] * vg[4] + vd[2] * vg[5];
+                s.cv[2] = vd[0] * vg[6] + vd[1] * vg[7] + vd[2] * vg[8];
+            } else {
+                s.cv[0] = s.cv[1] = s.cv[2] = 0.f;
+            }
+            if (SURF && a.normals) {
+                float3 n = {a.normals[3 * g], a.normals[3 * g + 1], a.normals[3 * g + 2]};
+                const float sg = normal_sign(n, a.view_dirs + 3 * g);
+                s.n[0] = sg * n.x;
+                s.n[1] = sg * n.y;
+                s.n[2] = sg * n.z;
+                s.nsign = sg;
+            } else {
+                s.n[0] = s.n[1] = s.n[2] = 0.f;
+                s.nsign = 1.f;
+            }
+            if (PREFILTER) {
+                const float2 c = a.points_xy_center[g];
+                s.cx = c.x;
+                s.cy = c.y;
+            }
+        }
+        for (int q = tr; q < k3BlockSize * L.ncomp; q += k3BlockSize) s_acc[q] = 0.f;
+        __syncthreads();
+
+        for (int idx = bend - 1; idx >= bstart; --idx) {
+            const Surfel3D& s = s_prim[idx - bstart];
+            float acc[N];
+#pragma unroll
+            for (int q = 0; q < N; ++q) acc[q] = 0.f;
+            bool contributed = false;
+            const int g_id = s.id;
+            const bool is_base = g_id < a.overdraw_base;
+            const bool active_color = idx < n_color;
+            const bool active_surf = SURF && is_base && idx < n_surf;
+            HexHit h;
+            const float3 Tu = {s.tu[0], s.tu[1], s.tu[2]};
+            const float3 Tv = {s.tv[0], s.tv[1], s.tv[2]};
+            const float3 Tw = {s.tw[0], s.tw[1], s.tw[2]};
+            const float3 soft3 = {s.s0, s.s1, s.s2};
+            if ((active_color || active_surf) &&
+                hexel_hit(px, py, Tu, Tv, Tw, s.opacity, soft3, h)) {
+                float alpha = h.alpha;
+                bool use_filter = false, clamped_filter = false;
+                float G = 0.f, dxf = 0.f, dyf = 0.f;
+                if (PREFILTER) {
+                    dxf = px - s.cx;
+                    dyf = py - s.cy;
+                    G = __expf(-0.5f * k3FilterInvSquare * (dxf * dxf + dyf * dyf));
+                    const float arf = s.opacity * G;
+                    clamped_filter = arf > 0.99f;
+                    const float af = clamped_filter ? 0.99f : arf;
+                    use_filter = af > h.alpha;
+                    alpha = use_filter ? af : h.alpha;
+                }
+                if (alpha >= 1.0f / 255.0f) {
+                    contributed = true;
+                    const float u = h.u, v = h.v;
+                    const float depth = use_filter ? Tw.z : h.depth;
+                    const float inv_1ma = 1.f / (1.f - alpha);
+                    float3 c = {0.f, 0.f, 0.f};
+                    float v_alpha_total = 0.f, v_u = 0.f, v_v = 0.f, v_depth_direct = 0.f;
+                    float T_before = 0.f, w = 0.f;
+                    if (active_color) {
+                        T_before = T_after * inv_1ma;
+                        w = alpha * T_before;
+                        const float ua = use_filter ? 0.f : u;
+                        const float va = use_filter ? 0.f : v;
+                        c = {s.cb[0], s.cb[1], s.cb[2]};
+                        if (a.color_model >= kColorLinear) {
+                            c.x += ua * s.gu[0] + va * s.gv[0];
+                            c.y += ua * s.gu[1] + va * s.gv[1];
+                            c.z += ua * s.gu[2] + va * s.gv[2];
+                        }
+                        const float* cq = nullptr;
+                        float ub = ua, vb = va;
+                        if (a.color_model == kColorQuadratic || a.color_model == kColorQuadBounded) {
+                            cq = a.color_quads + 9 * g_id;
+                            if (a.color_model == kColorQuadBounded) bounded_coords(ua, va, ub, vb);
+                            const float u2 = ub * ub, uv = ub * vb, v2 = vb * vb;
+                            c.x += u2 * cq[0] + uv * cq[3] + v2 * cq[6];
+                            c.y += u2 * cq[1] + uv * cq[4] + v2 * cq[7];
+                            c.z += u2 * cq[2] + uv * cq[5] + v2 * cq[8];
+                        }
+                        if (a.use_view_grads) {
+                            c.x += s.cv[0];
+                            c.y += s.cv[1];
+                            c.z += s.cv[2];
+                        }
+                        float spec = 0.f, cos_nv = 0.f, s_exp = 0.f;
+                        bool log_s_clamped = false;
+                        const float* vd = a.view_dirs + 3 * g_id;
+                        float3 nr = {0.f, 0.f, 0.f};
+                        if (a.view_model == kViewLobe) {
+                            if (a.normals)
+                                nr = {a.normals[3 * g_id], a.normals[3 * g_id + 1],
+                                      a.normals[3 * g_id + 2]};
+                            cos_nv = fmaxf(-(nr.x * vd[0] + nr.y * vd[1] + nr.z * vd[2]), 0.f);
+                            const float log_s = a.specular_log_s[g_id];
+                            log_s_clamped = (log_s < 0.f) || (log_s > 5.0f);
+                            s_exp = __expf(fminf(fmaxf(log_s, 0.f), 5.0f));
+                            spec = (cos_nv > 0.f) ? __powf(cos_nv, s_exp) : 0.f;
+                            c.x += a.specular_ks[3 * g_id] * spec;
+                            c.y += a.specular_ks[3 * g_id + 1] * spec;
+                            c.z += a.specular_ks[3 * g_id + 2] * spec;
+                        }
+                        acc[0] = w * v_out_r;
+                        acc[1] = w * v_out_g;
+                        acc[2] = w * v_out_b;
+                        if (L.off_cg >= 0) {
+                            acc[O_cg + 0] = w * v_out_r * ua;
+                            acc[O_cg + 1] = w * v_out_g * ua;
+                            acc[O_cg + 2] = w * v_out_b * ua;
+                            acc[O_cg + 3] = w * v_out_r * va;
+                            acc[O_cg + 4] = w * v_out_g * va;
+                            acc[O_cg + 5] = w * v_out_b * va;
+                        }
+                        if (L.off_cq >= 0 && cq) {
+                            const float u2 = ub * ub, uv = ub * vb, v2 = vb * vb;
+                            const float q3[3] = {u2, uv, v2};
+#pragma unroll
+                            for (int r = 0; r < 3; ++r) {
+                                acc[O_cq + 3 * r + 0] = w * v_out_r * q3[r];
+                                acc[O_cq + 3 * r + 1] = w * v_out_g * q3[r];
+                                acc[O_cq + 3 * r + 2] = w * v_out_b * q3[r];
+                            }
+                        }
+                        if (a.use_view_grads && L.off_vd >= 0 && !use_filter) {
+                            const float* vg = a.view_grads + 9 * g_id;
+                            acc[O_vd + 0] += w * (v_out_r * vg[0] + v_out_g * vg[3] + v_out_b * vg[6]);
+                            acc[O_vd + 1] += w * (v_out_r * vg[1] + v_out_g * vg[4] + v_out_b * vg[7]);
+                            acc[O_vd + 2] += w * (v_out_r * vg[2] + v_out_g * vg[5] + v_out_b * vg[8]);
+                        }
+                        if (a.view_model == kViewLobe) {
+                            if (L.off_ks >= 0) {
+                                acc[O_ks + 0] = w * v_out_r * spec;
+                                acc[O_ks + 1] = w * v_out_g * spec;
+                                acc[O_ks + 2] = w * v_out_b * spec;
+                            }
+                            const float v_spec = w * (v_out_r * a.specular_ks[3 * g_id] +
+                                                      v_out_g * a.specular_ks[3 * g_id + 1] +
+                                                      v_out_b * a.specular_ks[3 * g_id + 2]);
+                            if (L.off_ls >= 0 && !log_s_clamped && cos_nv > 0.f)
+                                acc[O_ls] = v_spec * (spec * logf(cos_nv) * s_exp);
+                            if (!use_filter && v_spec != 0.f && cos_nv > 0.f) {
+                                const float v_cos = v_spec * (s_exp * spec / cos_nv);
+                                if (L.off_vd >= 0) {
+                                    acc[O_vd + 0] += -v_cos * nr.x;
+                                    acc[O_vd + 1] += -v_cos * nr.y;
+                                    acc[O_vd + 2] += -v_cos * nr.z;
+                                }
+                                if (L.off_n >= 0) {
+                                    acc[O_n + 0] += -v_cos * vd[0];
+                                    acc[O_n + 1] += -v_cos * vd[1];
+                                    acc[O_n + 2] += -v_cos * vd[2];
+                                }
+                            }
+                        }
+                        v_alpha_total += T_before * (v_out_r * (c.x - behind.x) +
+                                                     v_out_g * (c.y - behind.y) +
+                                                     v_out_b * (c.z - behind.z));
+                        if (!use_filter && a.color_model >= kColorLinear) {
+                            v_u += w * (v_out_r * s.gu[0] + v_out_g * s.gu[1] + v_out_b * s.gu[2]);
+                            v_v += w * (v_out_r * s.gv[0] + v_out_g * s.gv[1] + v_out_b * s.gv[2]);
+                        }
+                        if (!use_filter && a.color_model == kColorQuadratic) {
+                            const float du_r = 2.f * u * cq[0] + v * cq[3];
+                            const float du_g = 2.f * u * cq[1] + v * cq[4];
+                            const float du_b = 2.f * u * cq[2] + v * cq[5];
+                            const float dv_r = u * cq[3] + 2.f * v * cq[6];
+                            const float dv_g = u * cq[4] + 2.f * v * cq[7];
+                            const float dv_b = u * cq[5] + 2.f * v * cq[8];
+                            v_u += w * (v_out_r * du_r + v_out_g * du_g + v_out_b * du_b);
+                            v_v += w * (v_out_r * dv_r + v_out_g * dv_g + v_out_b * dv_b);
+                        } else if (!use_filter && a.color_model == kColorQuadBounded) {
+                            float ubb, vbb;
+                            bounded_coords(u, v, ubb, vbb);
+                            const float du_r = 2.f * ubb * cq[0] + vbb * cq[3];
+                            const float du_g = 2.f * ubb * cq[1] + vbb * cq[4];
+                            const float du_b = 2.f * ubb * cq[2] + vbb * cq[5];
+                            const float dv_r = ubb * cq[3] + 2.f * vbb * cq[6];
+                            const float dv_g = ubb * cq[4] + 2.f * vbb * cq[7];
+                            const float dv_b = ubb * cq[5] + 2.f * vbb * cq[8];
+                            bounded_coords_vjp(u, v,
+                                               w * (v_out_r * du_r + v_out_g * du_g + v_out_b * du_b),
+                                               w * (v_out_r * dv_r + v_out_g * dv_g + v_out_b * dv_b),
+                                               v_u, v_v);
+                        }
+                    }
+                    float T_before_surf = 0.f, w_surf = 0.f;
+                    float3 n_surf = {0.f, 0.f, 0.f};
+                    if (SURF && active_surf) {
+                        T_before_surf = T_after_surf * inv_1ma;
+                        w_surf = alpha * T_before_surf;
+                        if (v_surf_depth != 0.f) {
+                            v_alpha_total += T_before_surf * v_surf_depth * (depth - behind_depth);
+                            if (!use_filter) {
+                                v_depth_direct += w_surf * v_surf_depth;
+                                v_u += v_depth_direct * Tw.x;
+                                v_v += v_depth_direct * Tw.y;
+                            }
+                        }
+                        if (v_surf_dist != 0.f) {
+                            const float m = k3FarPlane / (k3FarPlane - k3NearPlane) *
+                                            (1.0f - k3NearPlane / depth);
+                            const float weight_vjp =
+                                (M2 + m * m * final_alpha_surf - 2.0f * m * M1) * v_surf_dist;
+                            v_alpha_total += T_before_surf * (weight_vjp - last_dist_vjp);
+                            last_dist_vjp = alpha * weight_vjp + (1.0f - alpha) * last_dist_vjp;
+                            if (!use_filter) {
+                                const float m_vjp =
+                                    2.0f * w_surf * (m * final_alpha_surf - M1) * v_surf_dist;
+                                const float depth_vjp = m_vjp * (k3FarPlane * k3NearPlane) /
+                                                        ((k3FarPlane - k3NearPlane) * depth * depth);
+                                v_depth_direct += depth_vjp;
+                                v_u += depth_vjp * Tw.x;
+                                v_v += depth_vjp * Tw.y;
+                            }
+                        }
+                        if (idx == median_index && v_surf_median != 0.f) {
+                            if (use_filter) {
+                                acc[O_tm + 8] += v_surf_median;
+                            } else {
+                                v_depth_direct += v_surf_median;
+                                v_u += v_surf_median * Tw.x;
+                                v_v += v_surf_median * Tw.y;
+                            }
+                        }
+                        if (v_surf_alpha != 0.f)
+                            v_alpha_total += T_before_surf * v_surf_alpha * (1.f - behind_alpha);
+                        if (a.grad_out_surf_normals && a.normals) {
+                            n_surf = {s.n[0], s.n[1], s.n[2]};
+                            v_alpha_total += T_before_surf *
+                                             (v_surf_normal.x * (n_surf.x - behind_normal.x) +
+                                              v_surf_normal.y * (n_surf.y - behind_normal.y) +
+                                              v_surf_normal.z * (n_surf.z - behind_normal.z));
+                            if (!use_filter && L.off_n >= 0) {
+                                acc[O_n + 0] += s.nsign * w_surf * v_surf_normal.x;
+                                acc[O_n + 1] += s.nsign * w_surf * v_surf_normal.y;
+                                acc[O_n + 2] += s.nsign * w_surf * v_surf_normal.z;
+                            }
+                        }
+                    }
+                    // opacity
+                    float v_op = 0.f;
+                    if (use_filter) {
+                        if (!clamped_filter) {
+                            v_op += v_alpha_total * G;
+                            if (PREFILTER && L.off_ctr >= 0) {
+                                const float factor = v_alpha_total * s.opacity * G * k3FilterInvSquare;
+                                acc[O_ctr + 0] = factor * dxf;
+                                acc[O_ctr + 1] = factor * dyf;
+                            }
+                        }
+                    } else if (!h.clamped) {
+                        v_op += v_alpha_total * h.boundary;
+                    }
+                    const bool alpha_sdf_ok = h.alpha >= (1.0f / 255.0f);
+                    const bool has_overdraw =
+                        (v_overdraw != 0.f) && active_color && is_base && alpha_sdf_ok;
+                    if (has_overdraw) v_op += v_overdraw * h.boundary;
+                    acc[O_op] = v_op;
+                    if (L.off_soft >= 0) {
+                        const float sig = h.boundary;
+                        float v_soft = 0.f;
+                        if (!use_filter && !h.clamped)
+                            v_soft += v_alpha_total * s.opacity * (-h.dist) * sig * (1.f - sig);
+                        if (has_overdraw)
+                            v_soft += v_overdraw * s.opacity * (-h.dist) * sig * (1.f - sig);
+                        if (a.softness_stride == 3) {
+                            acc[O_soft + 0] = h.edge == 0 ? v_soft : 0.f;
+                            acc[O_soft + 1] = h.edge == 1 ? v_soft : 0.f;
+                            acc[O_soft + 2] = h.edge == 2 ? v_soft : 0.f;
+                        } else {
+                            acc[O_soft] = v_soft;
+                        }
+                    }
+                    if ((!use_filter && !h.clamped) || has_overdraw) {
+                        float dist_g, ddu, ddv;
+                        int edge_g;
+                        hex_sdf3_grad(u, v, dist_g, ddu, ddv, edge_g);
+                        const float soft_g = (edge_g == 0) ? soft3.x : ((edge_g == 1) ? soft3.y : soft3.z);
+                        const float d_sig = -soft_g * h.boundary * (1.f - h.boundary);
+                        float v_ad = has_overdraw ? (v_overdraw * s.opacity * d_sig) : 0.f;
+                        if (!use_filter && !h.clamped) v_ad += v_alpha_total * s.opacity * d_sig;
+                        v_u += v_ad * ddu;
+                        v_v += v_ad * ddv;
+                    }
+                    const float3 k = {px * Tw.x - Tu.x, px * Tw.y - Tu.y, px * Tw.z - Tu.z};
+                    const float3 l = {py * Tw.x - Tv.x, py * Tw.y - Tv.y, py * Tw.z - Tv.z};
+                    const float3 p = cross3(k, l);
+                    if (p.z != 0.f) {
+                        const float inv_pz = 1.f / p.z;
+                        const float dsx = v_u * inv_pz;
+                        const float dsy = v_v * inv_pz;
+                        const float3 v_p = {dsx, dsy, -(dsx * u + dsy * v)};
+                        const float3 v_k = cross3(l, v_p);
+                        const float3 v_l = cross3(v_p, k);
+                        float3 v_Tw = {px * v_k.x + py * v_l.x, px * v_k.y + py * v_l.y,
+                                       px * v_k.z + py * v_l.z};
+                        if (SURF && active_surf && v_depth_direct != 0.f) {
+                            v_Tw.x += u * v_depth_direct;
+                            v_Tw.y += v * v_depth_direct;
+                            v_Tw.z += v_depth_direct;
+                        }
+                        if (L.off_abs >= 0) {
+                            const float gx = -v_k.z * Tw.z * 0.5f * (float)W;
+                            const float gy = -v_l.z * Tw.z * 0.5f * (float)H;
+                            acc[O_abs] = sqrtf(gx * gx + gy * gy);
+                        }
+                        acc[O_tm + 0] += -v_k.x;
+                        acc[O_tm + 1] += -v_k.y;
+                        acc[O_tm + 2] += -v_k.z;
+                        acc[O_tm + 3] += -v_l.x;
+                        acc[O_tm + 4] += -v_l.y;
+                        acc[O_tm + 5] += -v_l.z;
+                        acc[O_tm + 6] += v_Tw.x;
+                        acc[O_tm + 7] += v_Tw.y;
+                        acc[O_tm + 8] += v_Tw.z;
+                    }
+                    if (active_color) {
+                        behind = {alpha * c.x + (1.f - alpha) * behind.x,
+                                  alpha * c.y + (1.f - alpha) * behind.y,
+                                  alpha * c.z + (1.f - alpha) * behind.z};
+                        T_after = T_before;
+                    }
+                    if (SURF && active_surf) {
+                        behind_depth = alpha * depth + (1.f - alpha) * behind_depth;
+                        behind_alpha = alpha * 1.0f + (1.f - alpha) * behind_alpha;
+                        if (a.grad_out_surf_normals && a.normals) {
+                            behind_normal = {alpha * n_surf.x + (1.f - alpha) * behind_normal.x,
+                                             alpha * n_surf.y + (1.f - alpha) * behind_normal.y,
+                                             alpha * n_surf.z + (1.f - alpha) * behind_normal.z};
+                        }
+                        T_after_surf = T_before_surf;
+                    }
+                }
+            }
+            if (__any_sync(0xffffffffu, contributed)) {
+                const int start = warp_reduce_scatter<N>(acc, lane);
+                float* dst = s_acc + (idx - bstart) * L.ncomp;
+#pragma unroll
+                for (int q = 0; q < N / 32; ++q) {
+                    const int comp = start + q;
+                    if (comp < L.ncomp && acc[q] != 0.f) atomicAdd(dst + comp, acc[q]);
+                }
+            }
+        }
+        __syncthreads();
+        // Flush this batch: one global atomic per (surfel, non-zero component).
+        if (bstart + tr < bend) {
+            const Surfel3D& s = s_prim[tr];
+            const int g = s.id;
+            const float* sa = s_acc + tr * L.ncomp;
+            auto put = [](float* p, float v) {
+                if (v != 0.f) atomicAdd(p, v);
+            };
+            put(a.grad_colors + 3 * g + 0, sa[0]);
+            put(a.grad_colors + 3 * g + 1, sa[1]);
+            put(a.grad_colors + 3 * g + 2, sa[2]);
+            if (L.off_cg >= 0 && a.grad_color_grads)
+                for (int q = 0; q < 6; ++q) put(a.grad_color_grads + 6 * g + q, sa[L.off_cg + q]);
+            if (L.off_cq >= 0 && a.grad_color_quads)
+                for (int q = 0; q < 9; ++q) put(a.grad_color_quads + 9 * g + q, sa[L.off_cq + q]);
+            put(a.grad_opacities + g, sa[L.off_op]);
+            if (L.off_soft >= 0) {
+                if (a.softness_stride == 3)
+                    for (int q = 0; q < 3; ++q) put(a.grad_softnesses + 3 * g + q, sa[L.off_soft + q]);
+                else
+                    put(a.grad_softnesses + g, sa[L.off_soft]);
+            }
+            for (int q = 0; q < 9; ++q) put(a.grad_transMats + 9 * g + q, sa[L.off_tm + q]);
+            if (L.off_n >= 0)
+                for (int q = 0; q < 3; ++q) put(a.grad_normals + 3 * g + q, sa[L.off_n + q]);
+            if (L.off_ks >= 0)
+                for (int q = 0; q < 3; ++q) put(a.grad_specular_ks + 3 * g + q, sa[L.off_ks + q]);
+            if (L.off_ls >= 0) put(a.grad_specular_log_s + g, sa[L.off_ls]);
+            if (L.off_abs >= 0) put(a.abs_means2d + 4 * g + 3, sa[L.off_abs]);
+            if (L.off_ctr >= 0) {
+                put(&a.grad_points_xy_center[g].x, sa[L.off_ctr]);
+                put(&a.grad_points_xy_center[g].y, sa[L.off_ctr + 1]);
+            }
+            float vd_acc[3] = {0.f, 0.f, 0.f};
+            if (L.off_vd >= 0)
+                for (int q = 0; q < 3; ++q) vd_acc[q] = sa[L.off_vd + q];
+            if (L.derive_vg || L.derive_vd) {
+                const float* vd = a.view_dirs + 3 * g;
+                const float* vg = a.view_grads + 9 * g;
+                if (L.derive_vg) {
+                    for (int c = 0; c < 3; ++c)
+                        for (int q = 0; q < 3; ++q)
+                            put(a.grad_view_grads + 9 * g + 3 * c + q, sa[c] * vd[q]);
+                }
+                if (L.derive_vd) {
+                    for (int q = 0; q < 3; ++q)
+                        vd_acc[q] += sa[0] * vg[q] + sa[1] * vg[3 + q] + sa[2] * vg[6 + q];
+                }
+            }
+            if (L.off_vd >= 0 || L.derive_vd)
+                for (int q = 0; q < 3; ++q) put(a.grad_view_dirs + 3 * g + q, vd_acc[q]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Geometry VJPs (hexels3d_forward.cu:2494-2664)
+// ---------------------------------------------------------------------------
+namespace {
+
+__device__ __forceinline__ Cmat<4, 4> w2n_of(const float* pm) {
+    Cmat<4, 4> m;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) m.m[c][r] = pm[4 * r + c];
+    return m;
+}
+
+__device__ __forceinline__ Cmat<3, 4> n2p_of(int W, int H) {
+    Cmat<3, 4> m;
+    m.m[0][0] = (float)W / 2.0f; m.m[0][1] = 0.0f; m.m[0][2] = 0.0f;
+    m.m[0][3] = ((float)W - 1.0f) / 2.0f;
+    m.m[1][0] = 0.0f; m.m[1][1] = (float)H / 2.0f; m.m[1][2] = 0.0f;
+    m.m[1][3] = ((float)H - 1.0f) / 2.0f;
+    m.m[2][0] = 0.0f; m.m[2][1] = 0.0f; m.m[2][2] = 0.0f; m.m[2][3] = 1.0f;
+    return m;
+}
+
+// Quaternion VJP through the normalised rotation matrix; the result is
+// projected onto the tangent space of the normalisation.
+__device__ __forceinline__ float4 quat_vjp(const float4 q, const Cmat<3, 3>& vR) {
+    const float s = rsqrtf(q.w * q.w + q.x * q.x + q.y * q.y + q.z * q.z);
+    const float w = q.x * s, x = q.y * s, y = q.z * s, z = q.w * s;
+    float4 g;
+    g.x = 2.f * (x * (vR.m[1][2] - vR.m[2][1]) + y * (vR.m[2][0] - vR.m[0][2]) +
+                 z * (vR.m[0][1] - vR.m[1][0]));
+    g.y = 2.f * (-2.f * x * (vR.m[1][1] + vR.m[2][2]) + y * (vR.m[0][1] + vR.m[1][0]) +
+                 z * (vR.m[0][2] + vR.m[2][0]) + w * (vR.m[1][2] - vR.m[2][1]));
+    g.z = 2.f * (x * (vR.m[0][1] + vR.m[1][0]) - 2.f * y * (vR.m[0][0] + vR.m[2][2]) +
+                 z * (vR.m[1][2] + vR.m[2][1]) + w * (vR.m[2][0] - vR.m[0][2]));
+    g.w = 2.f * (x * (vR.m[0][2] + vR.m[2][0]) + y * (vR.m[1][2] + vR.m[2][1]) -
+                 2.f * z * (vR.m[0][0] + vR.m[1][1]) + w * (vR.m[0][1] - vR.m[1][0]));
+    const float4 qu = {q.x * s, q.y * s, q.z * s, q.w * s};
+    const float dq = qu.x * g.x + qu.y * g.y + qu.z * g.z + qu.w * g.w;
+    return {s * (g.x - qu.x * dq), s * (g.y - qu.y * dq), s * (g.z - qu.z * dq),
+            s * (g.w - qu.w * dq)};
+}
+
+__device__ __forceinline__ float3 dnormvdv3(const float3 v, const float3 dv) {
+    const float sum2 = v.x * v.x + v.y * v.y + v.z * v.z + 1e-8f;
+    const float invsum32 = rsqrtf(sum2 * sum2 * sum2);
+    return {((sum2 - v.x * v.x) * dv.x - v.y * v.x * dv.y - v.z * v.x * dv.z) * invsum32,
+            (-v.x * v.y * dv.x + (sum2 - v.y * v.y) * dv.y - v.z * v.y * dv.z) * invsum32,
+            (-v.x * v.z * dv.x - v.y * v.z * dv.y + (sum2 - v.z * v.z) * dv.z) * invsum32};
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(256) geometry3d_bwd_kernel(
+    int P, const float* __restrict__ means3d, const float2* __restrict__ scales, float mod,
+    const float4* __restrict__ rotations, const float* __restrict__ projmatrix,
+    const float* __restrict__ campos, int W, int H, const int* __restrict__ radii,
+    const float* __restrict__ grad_T, const float* __restrict__ grad_view_dirs,
+    const float* __restrict__ grad_normals, float* __restrict__ grad_means3d,
+    float2* __restrict__ grad_scales, float4* __restrict__ grad_rotations) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= P) return;
+    if (radii[idx] <= 0) return;
+    const float3 p = {means3d[3 * idx], means3d[3 * idx + 1], means3d[3 * idx + 2]};
+    const float4 q = rotations[idx];
+    const float2 sc = scales[idx];
+    const Cmat<3, 3> R = quat_to_rotmat_wxyz(q);
+    const Cmat<3, 4> Pm = mmul<3, 4, 4>(w2n_of(projmatrix), n2p_of(W, H));
+    Cmat<3, 3> vT;
+#pragma unroll
+    for (int c = 0; c < 3; ++c)
+#pragma unroll
+        for (int r = 0; r < 3; ++r) vT.m[c][r] = grad_T[9 * idx + 3 * c + r];
+    const Cmat<3, 4> vM = mmul<3, 3, 4>(Pm, mtranspose<3, 3>(vT));
+    float3 v_mean = {vM.m[2][0], vM.m[2][1], vM.m[2][2]};
+    const float3 d = {p.x - campos[0], p.y - campos[1], p.z - campos[2]};
+    const float3 vvd = {grad_view_dirs[3 * idx], grad_view_dirs[3 * idx + 1],
+                        grad_view_dirs[3 * idx + 2]};
+    const float3 v_d = dnormvdv3(d, vvd);
+    v_mean.x += v_d.x;
+    v_mean.y += v_d.y;
+    v_mean.z += v_d.z;
+    grad_means3d[3 * idx] = v_mean.x;
+    grad_means3d[3 * idx + 1] = v_mean.y;
+    grad_means3d[3 * idx + 2] = v_mean.z;
+    float3 vR2 = {0.f, 0.f, 0.f};
+    if (grad_normals) {
+        vR2.x += grad_normals[3 * idx];
+        vR2.y += grad_normals[3 * idx + 1];
+        vR2.z += grad_normals[3 * idx + 2];
+    }
+    Cmat<3, 3> vR;
+    const float s0 = mod * sc.x, s1 = mod * sc.y;
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+        vR.m[0][r] = vM.m[0][r] * s0;
+        vR.m[1][r] = vM.m[1][r] * s1;
+    }
+    vR.m[2][0] = vR2.x;
+    vR.m[2][1] = vR2.y;
+    vR.m[2][2] = vR2.z;
+    grad_rotations[idx] = quat_vjp(q, vR);
+    grad_scales[idx] = {(vM.m[0][0] * R.m[0][0] + vM.m[0][1] * R.m[0][1] + vM.m[0][2] * R.m[0][2]) * mod,
+                        (vM.m[1][0] * R.m[1][0] + vM.m[1][1] * R.m[1][1] + vM.m[1][2] * R.m[1][2]) * mod};
+}
+
+__global__ void __launch_bounds__(256) means2d3d_bwd_kernel(int P, int W, int H, int stride,
+                                                            const int* __restrict__ radii,
+                                                            const float* __restrict__ transMats,
+                                                            const float* __restrict__ grad_T,
+                                                            float* __restrict__ grad_means2d) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= P) return;
+    if (radii[idx] <= 0) return;
+    const float depth = transMats[9 * idx + 8];
+    grad_means2d[idx * stride + 0] = grad_T[9 * idx + 2] * depth * 0.5f * (float)W;
+    grad_means2d[idx * stride + 1] = grad_T[9 * idx + 5] * depth * 0.5f * (float)H;
+    grad_means2d[idx * stride + 2] = 0.f;
+}
+
+__global__ void __launch_bounds__(256) center3d_bwd_kernel(int P, const float* __restrict__ means3d,
+                                                           const float* __restrict__ pm, int W,
+                                                           int H, const float2* __restrict__ gc,
+                                                           float* __restrict__ grad_means3d) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= P) return;
+    const float2 v_pix = gc[idx];
+    if (v_pix.x == 0.f && v_pix.y == 0.f) return;
+    const float x = means3d[3 * idx], y = means3d[3 * idx + 1], z = means3d[3 * idx + 2];
+    const float clip_x = pm[0] * x + pm[4] * y + pm[8] * z + pm[12];
+    const float clip_y = pm[1] * x + pm[5] * y + pm[9] * z + pm[13];
+    const float clip_w = pm[3] * x + pm[7] * y + pm[11] * z + pm[15];
+    const float inv_w = 1.0f / (clip_w + 1e-8f);
+    const float inv_w2 = inv_w * inv_w;
+    const float vx = v_pix.x * ((float)W / 2.0f);
+    const float vy = v_pix.y * ((float)H / 2.0f);
+    const float common = (vx * clip_x + vy * clip_y) * inv_w2;
+    grad_means3d[3 * idx + 0] += (vx * inv_w * pm[0]) + (vy * inv_w * pm[1]) - (common * pm[3]);
+    grad_means3d[3 * idx + 1] += (vx * inv_w * pm[4]) + (vy * inv_w * pm[5]) - (common * pm[7]);
+    grad_means3d[3 * idx + 2] += (vx * inv_w * pm[8]) + (vy * inv_w * pm[9]) - (common * pm[11]);
+}
+
+}  // namespace hx
+
+using namespace hx;
+
+namespace {
+
+template <bool SURF, bool PREFILTER, int N>
+int launch_bwd3d(const Backward3DArgs& a, const BwdLayout& L, cudaStream_t stream) {
+    const size_t smem = sizeof(Surfel3D) * k3BlockSize + sizeof(float) * k3BlockSize * L.ncomp;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    HX_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        HX_CUDA_TRY(cudaFuncSetAttribute(render3d_bwd_kernel<SURF, PREFILTER, N>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(sizeof(Surfel3D) * k3BlockSize +
+                                               sizeof(float) * k3BlockSize * N)));
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    dim3 grid(ceil_div(a.W, k3BlockX), ceil_div(a.H, k3BlockY)), block(k3BlockX, k3BlockY);
+    render3d_bwd_kernel<SURF, PREFILTER, N><<<grid, block, smem, stream>>>(a, L);
+    HX_LAUNCH_CHECK("render3d_bwd_kernel");
+    return HX_OK;
+}
+
+template <bool SURF, bool PREFILTER>
+int launch_bwd3d_n(const Backward3DArgs& a, const BwdLayout& L, bool generic,
+                   cudaStream_t stream) {
+    if (!generic) return launch_bwd3d<SURF, PREFILTER, 32>(a, L, stream);
+    return launch_bwd3d<SURF, PREFILTER, 64>(a, L, stream);
+}
+
+}  // namespace
+
+extern "C" int hx_hexels3d_render_backward(
+    int P, int num_rendered, const int32_t* ranges, const int32_t* point_list,
+    const float* points_xy_center, float* grad_points_xy_center, int image_width,
+    int image_height, const float* colors, const float* color_grads, const float* color_quads,
+    const float* view_grads, const float* specular_ks, const float* specular_log_s,
+    int view_model, const float* view_dirs, const float* transMats, const float* opacities,
+    const float* softnesses, int softness_stride, const float* background,
+    const float* grad_out_color, const float* grad_out_overdraw,
+    const float* grad_out_surf_depth, const float* grad_out_surf_alpha,
+    const float* grad_out_surf_normals, int has_median_grad, const float* normals,
+    float* grad_colors, float* grad_color_grads, float* grad_color_quads, float* grad_view_grads,
+    float* grad_specular_ks, float* grad_specular_log_s, float* grad_opacities,
+    float* grad_softnesses, float* grad_transMats, float* abs_means2d, float* grad_view_dirs,
+    float* grad_normals, int overdraw_base_count, int color_model, int use_view_grads,
+    const float* final_T, const int32_t* last_index, const float* final_T_surf,
+    const int32_t* last_index_surf, const float* m1_surf, const float* m2_surf,
+    const int32_t* median_index, cudaStream_t stream) {
+    HX_REQUIRE(image_width > 0 && image_height > 0, "invalid image dimensions");
+    HX_REQUIRE(color_model >= 0 && color_model <= 3, "color_model must be 0..3");
+    HX_REQUIRE(view_model >= 0 && view_model <= 2, "view_model must be 0..2");
+    HX_REQUIRE(softness_stride == 1 || softness_stride == 3, "softness_stride must be 1 or 3");
+    if (num_rendered == 0 || P == 0) return HX_OK;
+    HX_REQUIRE(ranges && point_list && colors && view_dirs && transMats && opacities &&
+                   softnesses && background && grad_out_color && grad_colors &&
+                   grad_opacities && grad_transMats && grad_view_dirs && final_T && last_index,
+               "hexels3d_render_backward: null pointer");
+    const bool surf = grad_out_surf_depth || grad_out_surf_alpha || grad_out_surf_normals;
+    HX_REQUIRE(!surf || (final_T_surf && last_index_surf && m1_surf && m2_surf && median_index),
+               "surface gradients need the forward's saved surface state");
+    const bool prefilter = points_xy_center != nullptr;
+    HX_REQUIRE(!prefilter || grad_points_xy_center, "prefilter needs grad_points_xy_center");
+    Backward3DArgs a = {};
+    a.ranges = (const uint2*)ranges;
+    a.point_list = point_list;
+    a.num_rendered = num_rendered;
+    a.P = P;
+    a.points_xy_center = (const float2*)points_xy_center;
+    a.grad_points_xy_center = (float2*)grad_points_xy_center;
+    a.W = image_width;
+    a.H = image_height;
+    a.colors = colors;
+    a.color_grads = color_grads;
+    a.color_quads = color_quads;
+    a.view_grads = view_grads;
+    a.specular_ks = specular_ks;
+    a.specular_log_s = specular_log_s;
+    a.view_model = view_model;
+    a.view_dirs = view_dirs;
+    a.transMats = transMats;
+    a.opacities = opacities;
+    a.softnesses = softnesses;
+    a.softness_stride = softness_stride;
+    a.bg = background;
+    a.grad_out_color = grad_out_color;
+    a.grad_out_overdraw = grad_out_overdraw;
+    a.grad_out_surf_depth = grad_out_surf_depth;
+    a.grad_out_surf_alpha = grad_out_surf_alpha;
+    a.grad_out_surf_normals = grad_out_surf_normals;
+    a.has_median_grad = has_median_grad != 0;
+    a.normals = normals;
+    a.grad_colors = grad_colors;
+    a.grad_color_grads = grad_color_grads;
+    a.grad_color_quads = grad_color_quads;
+    a.grad_view_grads = grad_view_grads;
+    a.grad_specular_ks = grad_specular_ks;
+    a.grad_specular_log_s = grad_specular_log_s;
+    a.grad_opacities = grad_opacities;
+    a.grad_softnesses = grad_softnesses;
+    a.grad_transMats = grad_transMats;
+    a.abs_means2d = abs_means2d;
+    a.grad_view_dirs = grad_view_dirs;
+    a.grad_normals = grad_normals;
+    a.overdraw_base = (overdraw_base_count <= 0 || overdraw_base_count > P) ? P : overdraw_base_count;
+    a.color_model = color_model;
+    a.use_view_grads = use_view_grads != 0;
+    a.final_T = final_T;
+    a.last_index = last_index;
+    a.final_T_surf = final_T_surf;
+    a.last_index_surf = last_index_surf;
+    a.m1_surf = m1_surf;
+    a.m2_surf = m2_surf;
+    a.median_index = median_index;
+
+    BwdLayout L;
+    const bool explicit_vd = view_model == 2 || (use_view_grads && prefilter);
+    const bool generic = color_model >= 2 || view_model == 2;
+    if (!generic) {
+        L.off_cg = (color_model >= 1 && grad_color_grads) ? kFixCg : -1;
+        L.off_cq = -1;
+        L.off_op = kFixOp;
+        L.off_soft = grad_softnesses ? kFixSoft : -1;
+        L.off_tm = kFixTm;
+        L.off_vd = explicit_vd ? kFixVd : -1;
+        L.off_n = grad_normals ? kFixN : -1;
+        L.off_ks = -1;
+        L.off_ls = -1;
+        L.off_abs = abs_means2d ? kFixAbs : -1;
+        L.off_ctr = prefilter ? kFixCtr : -1;
+        L.ncomp = kFixComp;
+    } else {
+        int off = 3;
+        L.off_cg = (color_model >= 1 && grad_color_grads) ? off : -1;
+        off += L.off_cg >= 0 ? 6 : 0;
+        L.off_cq = (color_model >= 2 && grad_color_quads) ? off : -1;
+        off += L.off_cq >= 0 ? 9 : 0;
+        L.off_op = off++;
+        L.off_soft = grad_softnesses ? off : -1;
+        off += grad_softnesses ? 3 : 0;
+        L.off_tm = off;
+        off += 9;
+        L.off_vd = explicit_vd ? off : -1;
+        off += explicit_vd ? 3 : 0;
+        L.off_n = grad_normals ? off : -1;
+        off += grad_normals ? 3 : 0;
+        L.off_ks = (view_model == 2 && grad_specular_ks) ? off : -1;
+        off += L.off_ks >= 0 ? 3 : 0;
+        L.off_ls = (view_model == 2 && grad_specular_log_s) ? off : -1;
+        off += L.off_ls >= 0 ? 1 : 0;
+        L.off_abs = abs_means2d ? off : -1;
+        off += abs_means2d ? 1 : 0;
+        L.off_ctr = prefilter ? off : -1;
+        off += prefilter ? 2 : 0;
+        L.ncomp = off;
+    }
+    L.derive_vg = use_view_grads && grad_view_grads;
+    L.derive_vd = use_view_grads && !prefilter;
+    HX_REQUIRE(L.ncomp <= 64, "internal: too many gradient components");
+    HX_REQUIRE(!use_view_grads || view_grads, "view_grads required with use_view_grads");
+    HX_REQUIRE(color_model < 1 || color_grads, "color_grads required for color_model >= 1");
+    HX_REQUIRE(color_model < 2 || color_quads, "color_quads required for quadratic models");
+    HX_REQUIRE(view_model != 2 || (specular_ks && specular_log_s), "lobe needs specular params");
+    if (surf) return prefilter ? launch_bwd3d_n<true, true>(a, L, generic, stream)
+                               : launch_bwd3d_n<true, false>(a, L, generic, stream);
+    return prefilter ? launch_bwd3d_n<false, true>(a, L, generic, stream)
+                     : launch_bwd3d_n<false, false>(a, L, generic, stream);
+}
+
+extern "C" int hx_hexels3d_geometry_backward(
+    int P, int num_rendered, const float* means3d, const float* scales, float scale_modifier,
+    const float* rotations, const float* projmatrix, const float* campos, int image_width,
+    int image_height, const int32_t* radii, const float* transMats, const float* grad_transMats,
+    const float* grad_view_dirs, const float* grad_normals, const float* grad_points_xy_center,
+    float* grad_means3d, float* grad_means2d, int means2d_stride, float* grad_scales,
+    float* grad_rotations, cudaStream_t stream) {
+    HX_REQUIRE(P >= 0, "hexels3d_geometry_backward: bad P");
+    if (P == 0 || num_rendered == 0) return HX_OK;
+    HX_REQUIRE(means3d && scales && rotations && projmatrix && campos && radii &&
+                   grad_transMats && grad_view_dirs && grad_means3d && grad_scales &&
+                   grad_rotations,
+               "hexels3d_geometry_backward: null pointer");
+    const int blocks = ceil_div(P, 256);
+    if (grad_means2d) {
+        HX_REQUIRE(transMats && (means2d_stride == 3 || means2d_stride == 4),
+                   "means2d stride must be 3 or 4");
+        means2d3d_bwd_kernel<<<blocks, 256, 0, stream>>>(P, image_width, image_height,
+                                                         means2d_stride, radii, transMats,
+                                                         grad_transMats, grad_means2d);
+        HX_LAUNCH_CHECK("means2d3d_bwd_kernel");
+    }
+    geometry3d_bwd_kernel<<<blocks, 256, 0, stream>>>(
+        P, means3d, (const float2*)scales, scale_modifier, (const float4*)rotations, projmatrix,
+        campos, image_width, image_height, radii, grad_transMats, grad_view_dirs, grad_normals,
+        grad_means3d, (float2*)grad_scales, (float4*)grad_rotations);
+    HX_LAUNCH_CHECK("geometry3d_bwd_kernel");
+    if (grad_points_xy_center) {
+        center3d_bwd_kernel<<<blocks, 256, 0, stream>>>(P, means3d, projmatrix, image_width,
+                                                        image_height,
+                                                        (const float2*)grad_points_xy_center,
+                                                        grad_means3d);
+        HX_LAUNCH_CHECK("center3d_bwd_kernel");
+    }
+    return HX_OK;
+}

@@ -1,0 +1,152 @@
+// Per-pixel math of the 3D hexel compositing kernels (forward and backward),
+// restating gsplat/cuda_hexels3d/csrc/hexels3d_forward.cu:260-371,1030-1067.
+#pragma once
+
+#include "hx_hexels3d.cuh"
+
+namespace hx {
+
+// Per-surfel record staged in shared memory by the compositing kernels.
+struct __align__(16) Surfel3D {
+    float tu[3], tv[3], tw[3];
+    float opacity;
+    float s0, s1, s2;
+    float cb[3];     // base colour
+    float cv[3];     // view_dir . view_grads (linear view model), else 0
+    float gu[3], gv[3];
+    float n[3];      // viewer-facing normal (surface outputs), else 0
+    float nsign;     // the sign applied to that normal
+    float cx, cy;    // prefilter centre
+    int id;
+};
+
+__device__ __forceinline__ float3 cross3(const float3 a, const float3 b) {
+    return make_float3(a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x);
+}
+
+__device__ __forceinline__ float sigmoid_neg(const float dist, const float softness) {
+    const float x = dist * softness;
+    return 1.f / (1.f + __expf(x));
+}
+
+// Hexagon SDF max(|v|, |a u + b v|, |a u - b v|) - 1 and the active edge;
+// slanted edges win ties with |v|, edge 2 wins ties with edge 1.
+__device__ __forceinline__ float hex_sdf3(const float u, const float v, int& edge) {
+    constexpr float k = 1.7320508f;
+    constexpr float a = 0.5f * k;
+    constexpr float b = 0.5f;
+    const float d0 = fabsf(v);
+    const float t1 = a * u + b * v;
+    const float t2 = a * u - b * v;
+    const float d1 = fabsf(t1);
+    const float d2 = fabsf(t2);
+    float m = d1;
+    edge = 1;
+    if (d2 >= m) {
+        m = d2;
+        edge = 2;
+    }
+    if (d0 > m) {
+        edge = 0;
+        return d0 - 1.f;
+    }
+    return m - 1.f;
+}
+
+// SDF with its (sub)gradient; here |x| uses sign(0) = +1.
+__device__ __forceinline__ void hex_sdf3_grad(const float u, const float v, float& dist,
+                                              float& ddu, float& ddv, int& edge) {
+    constexpr float k = 1.7320508f;
+    constexpr float a = 0.5f * k;
+    constexpr float b = 0.5f;
+    const float d0 = fabsf(v);
+    const float t1 = a * u + b * v;
+    const float t2 = a * u - b * v;
+    const float d1 = fabsf(t1);
+    const float d2 = fabsf(t2);
+    float m = d1;
+    edge = 1;
+    if (d2 >= m) {
+        m = d2;
+        edge = 2;
+    }
+    if (d0 > m) {
+        edge = 0;
+        dist = d0 - 1.f;
+        ddu = 0.f;
+        ddv = (v >= 0.f) ? 1.f : -1.f;
+        return;
+    }
+    dist = m - 1.f;
+    if (edge == 1) {
+        const float s = (t1 >= 0.f) ? 1.f : -1.f;
+        ddu = a * s;
+        ddv = b * s;
+        return;
+    }
+    const float s = (t2 >= 0.f) ? 1.f : -1.f;
+    ddu = a * s;
+    ddv = -b * s;
+}
+
+// (u, v) scaled back onto the hexagon when outside it (quadratic_bounded).
+__device__ __forceinline__ void bounded_coords(const float u, const float v, float& ub,
+                                               float& vb) {
+    int edge;
+    const float rho = hex_sdf3(u, v, edge) + 1.f;
+    const float inv = (rho > 1.f) ? (1.f / rho) : 1.f;
+    ub = u * inv;
+    vb = v * inv;
+}
+
+__device__ __forceinline__ void bounded_coords_vjp(const float u, const float v, const float gub,
+                                                   const float gvb, float& gu, float& gv) {
+    float dist, dru, drv;
+    int edge;
+    hex_sdf3_grad(u, v, dist, dru, drv, edge);
+    const float rho = dist + 1.f;
+    if (rho <= 1.f) {
+        gu += gub;
+        gv += gvb;
+        return;
+    }
+    const float inv = 1.f / rho;
+    const float radial = (gub * u + gvb * v) * inv * inv;
+    gu += gub * inv - radial * dru;
+    gv += gvb * inv - radial * drv;
+}
+
+__device__ __forceinline__ float normal_sign(const float3 n, const float* vd) {
+    return n.x * vd[0] + n.y * vd[1] + n.z * vd[2] > 0.f ? -1.f : 1.f;
+}
+
+// Ray-splat intersection of pixel (px, py) with a surfel of transform rows
+// Tu, Tv, Tw: returns false when the ray is parallel or the hit is in front
+// of the near plane; otherwise (u, v), depth, SDF, boundary weight and alpha.
+struct HexHit {
+    float u, v, depth, dist, soft, boundary, alpha_raw, alpha;
+    int edge;
+    bool clamped;
+};
+
+__device__ __forceinline__ bool hexel_hit(const float px, const float py, const float3 Tu,
+                                          const float3 Tv, const float3 Tw, const float opacity,
+                                          const float3 soft3, HexHit& h) {
+    const float3 k = {px * Tw.x - Tu.x, px * Tw.y - Tu.y, px * Tw.z - Tu.z};
+    const float3 l = {py * Tw.x - Tv.x, py * Tw.y - Tv.y, py * Tw.z - Tv.z};
+    const float3 p = cross3(k, l);
+    if (p.z == 0.0f) return false;
+    h.u = p.x / p.z;
+    h.v = p.y / p.z;
+    h.depth = (h.u * Tw.x + h.v * Tw.y) + Tw.z;
+    if (h.depth < k3NearPlane) return false;
+    h.dist = hex_sdf3(h.u, h.v, h.edge);
+    h.soft = (h.edge == 0) ? soft3.x : ((h.edge == 1) ? soft3.y : soft3.z);
+    h.boundary = sigmoid_neg(h.dist, h.soft);
+    h.alpha_raw = opacity * h.boundary;
+    h.clamped = h.alpha_raw > 0.99f;
+    h.alpha = h.clamped ? 0.99f : h.alpha_raw;
+    return true;
+}
+
+}  // namespace hx

@@ -1,0 +1,478 @@
+"""``gsplat.cuda_hexels3d._C`` — the 3D hexel surfel rasteriser module.
+
+Same function names, positional arguments, return tuples and checks as the
+reference's extension (gsplat/cuda_hexels3d/csrc/ext.cpp:5-23,
+hexels3d_forward.h, hexels3d_backward.h); each function drives the sm_100a
+kernels of ``libhexel_b200.so`` through its C-ABI on PyTorch's current stream:
+
+  preprocess -> prefix sum (one 8-byte read-back of the intersection count,
+  as the reference) -> emit (tile|depth) keys -> stable radix sort -> tile
+  ranges -> compositing; backward: reverse traversal -> geometry VJP.
+
+The cached forward returns the reference's eleven saved buffers, and the
+cached backward accepts them.  The diagnostic exact-sort / pixel-risk oracles
+of the reference are not part of the training or render path and are not
+provided by this build.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .._lib import check_input, lib, ptr, stream, workspace
+
+kNumChannels = 3
+_EMPTY_CACHE: dict = {}
+
+
+def _empty(x: torch.Tensor, dtype=None) -> torch.Tensor:
+    return torch.empty((0,), device=x.device, dtype=dtype or x.dtype)
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _checks(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
+            specular_ks, specular_log_s, opacities, softnesses, viewmatrix, projmatrix, campos,
+            background, image_width, image_height, softness, color_model, view_model,
+            use_view_grads):
+    """The reference's argument checks (hexels3d_forward.cu:2724-2857)."""
+    names = ("means3d", "scales", "rotations", "colors", "color_grads", "color_quads",
+             "view_grads", "specular_ks", "specular_log_s", "opacities", "softnesses",
+             "viewmatrix", "projmatrix", "campos", "background")
+    tensors = (means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
+               specular_ks, specular_log_s, opacities, softnesses, viewmatrix, projmatrix,
+               campos, background)
+    for t, n in zip(tensors, names):
+        check_input(t, n)
+    _check(means3d.ndimension() == 2 and means3d.size(1) == 3, "means3d must have shape (P,3)")
+    _check(scales.ndimension() == 2 and scales.size(1) == 2, "scales must have shape (P,2)")
+    _check(rotations.ndimension() == 2 and rotations.size(1) == 4,
+           "rotations must have shape (P,4)")
+    _check(colors.ndimension() == 2 and colors.size(1) == 3, "colors must have shape (P,3)")
+    _check(0 <= color_model <= 3,
+           "color_model must be one of: 0 (flat), 1 (linear), 2 (quadratic), 3 (quadratic_bounded)")
+    _check(0 <= view_model <= 2, "view_model must be one of: 0 (none), 1 (linear), 2 (lobe)")
+    P = means3d.size(0)
+    want_linear = color_model >= 1
+    want_quad = color_model in (2, 3)
+    cg_ok = color_grads.ndimension() == 3 and color_grads.size(1) == 2 and color_grads.size(2) == 3
+    if want_linear:
+        _check(cg_ok, "color_grads must have shape (P,2,3)")
+        _check(color_grads.size(0) == P, "color_grads must have shape (P,2,3)")
+    else:
+        _check(color_grads.numel() == 0 or cg_ok, "color_grads must have shape (P,2,3) or be empty")
+    cq_ok = color_quads.ndimension() == 3 and color_quads.size(1) == 3 and color_quads.size(2) == 3
+    if want_quad:
+        _check(cq_ok, "color_quads must have shape (P,3,3)")
+        _check(color_quads.size(0) == P, "color_quads must have shape (P,3,3)")
+    else:
+        _check(color_quads.numel() == 0 or cq_ok, "color_quads must have shape (P,3,3) or be empty")
+    vg_ok = view_grads.ndimension() == 3 and view_grads.size(1) == 3 and view_grads.size(2) == 3
+    if use_view_grads:
+        _check(vg_ok, "view_grads must have shape (P,3,3)")
+        _check(view_grads.size(0) == P, "view_grads must have shape (P,3,3)")
+    else:
+        _check(view_grads.numel() == 0 or vg_ok, "view_grads must have shape (P,3,3) or be empty")
+    if view_model == 2:
+        _check(specular_ks.ndimension() == 2 and specular_ks.size(1) == 3,
+               "specular_ks must have shape (P,3)")
+        _check(specular_log_s.ndimension() == 1, "specular_log_s must have shape (P,)")
+        _check(specular_ks.size(0) == P, "specular_ks must have shape (P,3)")
+        _check(specular_log_s.numel() == P, "specular_log_s must have shape (P,)")
+    _check(opacities.ndimension() == 1, "opacities must have shape (P,)")
+    _check(softnesses.ndimension() in (1, 2), "softnesses must have shape (P,), (P,3) or (0,)")
+    _check(viewmatrix.numel() == 16, "viewmatrix must have 16 elements")
+    _check(projmatrix.numel() == 16, "projmatrix must have 16 elements")
+    _check(campos.numel() == 3, "campos must have 3 elements")
+    _check(background.numel() == 3, "background must have 3 elements")
+    _check(softness > 0.0, "softness must be > 0")
+    _check(image_width > 0 and image_height > 0, "invalid image dimensions")
+    for t, n in zip(tensors, names):
+        _check(t.dtype == torch.float32, f"{n} must be float32")
+    if softnesses.numel() == 0:
+        stride = 1
+    elif softnesses.ndimension() == 1:
+        _check(softnesses.numel() == P, "softnesses must have shape (P,), (P,3) or (0,)")
+        stride = 1
+    else:
+        _check(softnesses.size(0) == P and softnesses.size(1) == 3,
+               "softnesses must have shape (P,3)")
+        stride = 3
+    return P, stride
+
+
+def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
+                  specular_ks, specular_log_s, opacities, softnesses, viewmatrix, projmatrix,
+                  campos, background, image_width, image_height, tan_fovx, tan_fovy, softness,
+                  scale_modifier, color_model, view_model, use_view_grads, prefilter_edge_on,
+                  conservative_bounds, debug, *, return_contrib=False, return_overdraw=False,
+                  return_overdraw_hits=False, return_surface=False, overdraw_base_count=-1,
+                  owner=False, return_median_depth=False, save=False, save_surface=False):
+    """rasterize_hexels3d_forward_impl (hexels3d_forward.cu:2679-3481)."""
+    W, H = int(image_width), int(image_height)
+    P, stride = _checks(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
+                        specular_ks, specular_log_s, opacities, softnesses, viewmatrix,
+                        projmatrix, campos, background, W, H, float(softness), int(color_model),
+                        int(view_model), bool(use_view_grads))
+    dev = means3d.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    need_normals = return_surface or view_model == 2
+    radii = torch.empty((P,), **i32)
+    tile_radii = torch.empty((P, 2), **i32)
+    points_xy_image = torch.empty((P, 2), **f32)
+    points_xy_center = torch.empty((P, 2), **f32) if prefilter_edge_on else torch.empty((0,), **f32)
+    depths = torch.empty((P,), **f32)
+    transMats = torch.empty((P, 9), **f32)
+    tiles_touched = torch.empty((P,), **i32)
+    opacities_out = torch.empty((P,), **f32)
+    softnesses_out = torch.empty((P, 3) if stride == 3 else (P,), **f32)
+    view_dirs = torch.empty((P, 3), **f32)
+    normals = torch.empty((P, 3), **f32) if need_normals else torch.empty((0,), **f32)
+    soft_in = softnesses if softnesses.numel() > 0 else None
+    with torch.cuda.device(dev):
+        s = stream(dev)
+        lib.call("hx_hexels3d_preprocess", P, ptr(means3d), ptr(scales), float(scale_modifier),
+                 ptr(rotations), ptr(opacities), ptr(soft_in), float(softness), stride,
+                 ptr(viewmatrix), ptr(projmatrix), ptr(campos), W, H, int(bool(prefilter_edge_on)),
+                 int(bool(conservative_bounds)), ptr(radii), ptr(tile_radii),
+                 ptr(points_xy_image), ptr(points_xy_center) if prefilter_edge_on else None,
+                 ptr(depths), ptr(transMats), ptr(tiles_touched), ptr(opacities_out),
+                 ptr(softnesses_out), ptr(view_dirs), ptr(normals) if need_normals else None, s)
+        offsets = torch.empty((P,), **i32)
+        total = torch.zeros((1,), dtype=torch.int64, device=dev)
+        ws = workspace(lib.query("hx_scan_workspace_bytes", P), dev)
+        lib.call("hx_inclusive_scan_i32", ptr(tiles_touched), ptr(offsets), P, ptr(total),
+                 ptr(ws), ws.numel(), s)
+        num_rendered = int(total.item()) if P > 0 else 0
+        _check(num_rendered <= 2**31 - 1, "number of rendered intersections overflows int32")
+        tx, ty = (W + 15) // 16, (H + 15) // 16
+        ranges = torch.empty((tx * ty, 2), **i32)
+        values_sorted = torch.empty((num_rendered,), **i32)
+        keys_sorted = torch.empty((num_rendered,), dtype=torch.int64, device=dev)
+        ws = workspace(lib.query("hx_hexels3d_bin_workspace_bytes", num_rendered), dev)
+        lib.call("hx_hexels3d_bin", P, num_rendered, W, H, ptr(points_xy_image), ptr(depths),
+                 ptr(offsets), ptr(radii), ptr(tile_radii), ptr(keys_sorted),
+                 ptr(values_sorted), ptr(ranges), ptr(ws), ws.numel(), s)
+
+        out_color = torch.zeros((kNumChannels, H, W), **f32)
+        contrib = torch.zeros((P,), **f32) if return_contrib else torch.empty((0,), **f32)
+        overdraw = torch.zeros((H, W), **f32) if return_overdraw else torch.empty((0,), **f32)
+        overdraw_hits = (torch.zeros((H, W), **f32) if return_overdraw_hits
+                         else torch.empty((0,), **f32))
+        if return_surface:
+            surf_depth = torch.zeros((H, W), **f32)
+            surf_alpha = torch.zeros((H, W), **f32)
+            surf_maps = torch.zeros((kNumChannels + 1 + int(return_median_depth), H, W), **f32)
+        else:
+            surf_depth = surf_alpha = surf_maps = torch.empty((0,), **f32)
+        final_T = torch.empty((H, W), **f32) if save else torch.empty((0,), **f32)
+        last_index = torch.empty((H, W), **i32) if save else torch.empty((0,), **i32)
+        surf_state = None
+        if save_surface and return_surface:
+            surf_state = (torch.empty((H, W), **f32), torch.empty((H, W), **i32),
+                          torch.empty((H, W), **f32), torch.empty((H, W), **f32),
+                          torch.empty((H, W), **i32))
+        own = None
+        if owner:
+            own = (torch.full((H, W), -1, dtype=torch.int64, device=dev),
+                   torch.zeros((H, W), **f32), torch.zeros((2, H, W), **f32),
+                   torch.zeros((H, W), **f32), torch.zeros((H, W), **f32),
+                   torch.zeros((H, W), **f32))
+        if num_rendered > 0:
+            lib.call("hx_hexels3d_render_forward", P, num_rendered, ptr(ranges),
+                     ptr(values_sorted), ptr(points_xy_center) if prefilter_edge_on else None,
+                     W, H, ptr(colors), ptr(color_grads) if color_model >= 1 else None,
+                     ptr(color_quads) if color_model >= 2 else None,
+                     ptr(view_grads) if use_view_grads else None,
+                     ptr(specular_ks) if view_model == 2 else None,
+                     ptr(specular_log_s) if view_model == 2 else None, ptr(view_dirs),
+                     ptr(transMats), ptr(opacities_out), ptr(softnesses_out), stride,
+                     ptr(background), ptr(normals) if need_normals else None,
+                     int(overdraw_base_count), int(color_model), int(view_model),
+                     int(bool(use_view_grads)), int(bool(return_median_depth)),
+                     ptr(out_color), ptr(contrib) if return_contrib else None,
+                     ptr(overdraw) if return_overdraw else None,
+                     ptr(overdraw_hits) if return_overdraw_hits else None,
+                     ptr(surf_depth) if return_surface else None,
+                     ptr(surf_alpha) if return_surface else None,
+                     ptr(surf_maps) if return_surface else None,
+                     *(ptr(t) for t in own) if own else (None,) * 6,
+                     ptr(final_T) if save else None, ptr(last_index) if save else None,
+                     *(ptr(t) for t in surf_state) if surf_state else (None,) * 5, s)
+        elif save:
+            final_T.fill_(1.0)
+            last_index.zero_()
+            if surf_state:
+                surf_state[0].fill_(1.0)
+                for t in surf_state[1:4]:
+                    t.zero_()
+                surf_state[4].fill_(-1)
+        if debug:
+            torch.cuda.synchronize(dev)
+    saved = None
+    if save:
+        saved = [radii, transMats, opacities_out, softnesses_out, view_dirs,
+                 normals if view_model == 2 else torch.empty((0,), **f32),
+                 points_xy_center, ranges, values_sorted, final_T, last_index]
+    return dict(out_color=out_color, radii=radii, contrib=contrib, overdraw=overdraw,
+                overdraw_hits=overdraw_hits, surf_depth=surf_depth, surf_alpha=surf_alpha,
+                surf_maps=surf_maps, saved=saved, surf_state=surf_state, normals=normals,
+                owner=own, num_rendered=num_rendered)
+
+
+def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, color_quads,
+                   view_grads, specular_ks, specular_log_s, opacities, softnesses, viewmatrix,
+                   projmatrix, campos, background, grad_out_color, grad_out_overdraw,
+                   grad_out_surf_depth, grad_out_surf_alpha, grad_out_surf_normals, image_width,
+                   image_height, tan_fovx, tan_fovy, softness, scale_modifier, color_model,
+                   view_model, use_view_grads, overdraw_base_count, prefilter_edge_on,
+                   conservative_bounds, debug, saved, surf_state=None, surf_normals=None):
+    """rasterize_hexels3d_backward_impl (hexels3d_forward.cu:4882-5582) on the
+    forward's saved state."""
+    W, H = int(image_width), int(image_height)
+    P, stride = _checks(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
+                        specular_ks, specular_log_s, opacities, softnesses, viewmatrix,
+                        projmatrix, campos, background, W, H, float(softness), int(color_model),
+                        int(view_model), bool(use_view_grads))
+    for t, n in ((means2d, "means2d"), (grad_out_color, "grad_out_color"),
+                 (grad_out_overdraw, "grad_out_overdraw"),
+                 (grad_out_surf_depth, "grad_out_surf_depth"),
+                 (grad_out_surf_alpha, "grad_out_surf_alpha"),
+                 (grad_out_surf_normals, "grad_out_surf_normals")):
+        check_input(t, n)
+        _check(t.dtype == torch.float32, f"{n} must be float32")
+    _check(means2d.numel() == 0 or (means2d.ndimension() == 2 and means2d.size(0) == P and
+                                    means2d.size(1) in (3, 4)),
+           "means2d must have shape (P,3), (P,4) or be empty")
+    _check(grad_out_color.ndimension() == 3 and grad_out_color.size(0) == 3 and
+           grad_out_color.size(1) == H and grad_out_color.size(2) == W,
+           "grad_out_color must have shape (3,H,W)")
+    for t, n in ((grad_out_overdraw, "grad_out_overdraw"),
+                 (grad_out_surf_depth, "grad_out_surf_depth"),
+                 (grad_out_surf_alpha, "grad_out_surf_alpha")):
+        _check(t.numel() == 0 or tuple(t.shape) == (H, W), f"{n} must have shape (H,W) or be empty")
+    _check(grad_out_surf_normals.numel() == 0 or (
+        grad_out_surf_normals.ndimension() == 3 and grad_out_surf_normals.size(0) in (4, 5) and
+        grad_out_surf_normals.size(1) == H and grad_out_surf_normals.size(2) == W),
+        "grad_out_surf_normals must have shape (4,H,W), (5,H,W) or be empty")
+    dev = means3d.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    (radii, transMats, opacities_out, softnesses_out, view_dirs, normals_saved, points_xy_center,
+     ranges, values_sorted, final_T, last_index) = saved
+    num_rendered = values_sorted.numel()
+    grad_means3d = torch.zeros((P, 3), **f32)
+    grad_means2d = torch.zeros_like(means2d)
+    stride2d = means2d.size(1) if means2d.numel() > 0 else 3
+    grad_scales = torch.zeros((P, 2), **f32)
+    grad_rotations = torch.zeros((P, 4), **f32)
+    grad_colors = torch.zeros((P, 3), **f32)
+    grad_color_grads = torch.zeros_like(color_grads)
+    grad_color_quads = torch.zeros_like(color_quads)
+    grad_view_grads = torch.zeros_like(view_grads)
+    grad_specular_ks = torch.zeros_like(specular_ks)
+    grad_specular_log_s = torch.zeros_like(specular_log_s)
+    grad_opacities = torch.zeros((P,), **f32)
+    grad_softnesses = torch.zeros_like(softnesses, dtype=torch.float32)
+    has_surface = (grad_out_surf_depth.numel() > 0 or grad_out_surf_alpha.numel() > 0 or
+                   grad_out_surf_normals.numel() > 0)
+    need_normals = view_model == 2 or grad_out_surf_normals.numel() > 0
+    normals = surf_normals if (surf_normals is not None and surf_normals.numel() > 0) \
+        else normals_saved
+    _check(not need_normals or normals.numel() == 3 * P, "normals are required by this backward")
+    grad_normals = torch.zeros((P, 3), **f32) if need_normals else None
+    grad_transMats = torch.zeros((P, 9), **f32)
+    grad_view_dirs = torch.zeros((P, 3), **f32)
+    grad_center = torch.zeros((P, 2), **f32) if prefilter_edge_on else None
+    _check(not has_surface or surf_state is not None,
+           "surface gradients need a forward run with surface outputs")
+    nz = lambda t: ptr(t) if t.numel() > 0 else None  # noqa: E731
+    with torch.cuda.device(dev):
+        s = stream(dev)
+        if num_rendered > 0:
+            lib.call("hx_hexels3d_render_backward", P, num_rendered, ptr(ranges),
+                     ptr(values_sorted), ptr(points_xy_center) if prefilter_edge_on else None,
+                     ptr(grad_center), W, H, ptr(colors),
+                     ptr(color_grads) if color_model >= 1 else None,
+                     ptr(color_quads) if color_model >= 2 else None,
+                     ptr(view_grads) if use_view_grads else None,
+                     ptr(specular_ks) if view_model == 2 else None,
+                     ptr(specular_log_s) if view_model == 2 else None, int(view_model),
+                     ptr(view_dirs), ptr(transMats), ptr(opacities_out), ptr(softnesses_out),
+                     stride, ptr(background), ptr(grad_out_color), nz(grad_out_overdraw),
+                     nz(grad_out_surf_depth) if has_surface else None,
+                     nz(grad_out_surf_alpha) if has_surface else None,
+                     nz(grad_out_surf_normals) if has_surface else None,
+                     int(has_surface and grad_out_surf_normals.numel() > 0 and
+                         grad_out_surf_normals.size(0) == 5),
+                     ptr(normals) if need_normals else None, ptr(grad_colors),
+                     ptr(grad_color_grads) if color_model >= 1 else None,
+                     ptr(grad_color_quads) if color_model >= 2 else None,
+                     ptr(grad_view_grads) if use_view_grads else None,
+                     ptr(grad_specular_ks) if view_model == 2 else None,
+                     ptr(grad_specular_log_s) if view_model == 2 else None,
+                     ptr(grad_opacities),
+                     ptr(grad_softnesses) if softnesses.numel() > 0 else None,
+                     ptr(grad_transMats), ptr(grad_means2d) if stride2d == 4 and
+                     means2d.numel() > 0 else None, ptr(grad_view_dirs), ptr(grad_normals),
+                     int(overdraw_base_count), int(color_model), int(bool(use_view_grads)),
+                     ptr(final_T), ptr(last_index),
+                     *(ptr(t) for t in surf_state) if has_surface else (None,) * 5, s)
+            lib.call("hx_hexels3d_geometry_backward", P, num_rendered, ptr(means3d), ptr(scales),
+                     float(scale_modifier), ptr(rotations), ptr(projmatrix), ptr(campos), W, H,
+                     ptr(radii), ptr(transMats), ptr(grad_transMats), ptr(grad_view_dirs),
+                     ptr(grad_normals), ptr(grad_center), ptr(grad_means3d),
+                     ptr(grad_means2d) if means2d.numel() > 0 else None, int(stride2d),
+                     ptr(grad_scales), ptr(grad_rotations), s)
+        if debug:
+            torch.cuda.synchronize(dev)
+    return (grad_means3d, grad_means2d, grad_scales, grad_rotations, grad_colors,
+            grad_color_grads, grad_color_quads, grad_view_grads, grad_specular_ks,
+            grad_specular_log_s, grad_opacities, grad_softnesses)
+
+
+# ---------------------------------------------------------------------------
+# the reference's entry points (ext.cpp:6-22)
+# ---------------------------------------------------------------------------
+def rasterize_hexels3d_forward(*args):
+    o = _forward_core(*args)
+    return o["out_color"], o["radii"]
+
+
+def rasterize_hexels3d_forward_cached(*args):
+    o = _forward_core(*args, save=True)
+    return o["out_color"], o["radii"], o["saved"]
+
+
+def rasterize_hexels3d_owner_forward(*args):
+    o = _forward_core(*args, owner=True)
+    return (o["out_color"], o["radii"], *o["owner"])
+
+
+def rasterize_hexels3d_forward_with_contrib(*args):
+    o = _forward_core(*args, return_contrib=True)
+    return o["out_color"], o["radii"], o["contrib"]
+
+
+def _split_overdraw(args):
+    # (..., use_view_grads, overdraw_base_count, prefilter, conservative, debug)
+    base = list(args[:24])
+    odb, pre, cons, dbg = args[24:28]
+    return base + [pre, cons, dbg], int(odb)
+
+
+def rasterize_hexels3d_forward_with_overdraw(*args):
+    a, odb = _split_overdraw(args)
+    o = _forward_core(*a, return_overdraw=True, overdraw_base_count=odb)
+    return o["out_color"], o["radii"], o["overdraw"]
+
+
+def rasterize_hexels3d_forward_with_contrib_overdraw(*args):
+    a, odb = _split_overdraw(args)
+    o = _forward_core(*a, return_contrib=True, return_overdraw=True, overdraw_base_count=odb)
+    return o["out_color"], o["radii"], o["contrib"], o["overdraw"]
+
+
+def rasterize_hexels3d_forward_with_overdraw_hits(*args):
+    a, odb = _split_overdraw(args)
+    o = _forward_core(*a, return_overdraw=True, return_overdraw_hits=True,
+                      overdraw_base_count=odb)
+    return o["out_color"], o["radii"], o["overdraw"], o["overdraw_hits"]
+
+
+def rasterize_hexels3d_forward_with_contrib_overdraw_hits(*args):
+    a, odb = _split_overdraw(args)
+    o = _forward_core(*a, return_contrib=True, return_overdraw=True, return_overdraw_hits=True,
+                      overdraw_base_count=odb)
+    return o["out_color"], o["radii"], o["contrib"], o["overdraw"], o["overdraw_hits"]
+
+
+def _all(args, median: bool):
+    base = list(args[:24])
+    (ret_contrib, ret_overdraw, ret_hits, ret_surface, odb, pre, cons, dbg) = args[24:32]
+    o = _forward_core(*base, pre, cons, dbg, return_contrib=bool(ret_contrib),
+                      return_overdraw=bool(ret_overdraw), return_overdraw_hits=bool(ret_hits),
+                      return_surface=bool(ret_surface), overdraw_base_count=int(odb),
+                      return_median_depth=median)
+    return (o["out_color"], o["radii"], o["contrib"], o["overdraw"], o["overdraw_hits"],
+            o["surf_depth"], o["surf_alpha"], o["surf_maps"])
+
+
+def rasterize_hexels3d_forward_all(*args):
+    return _all(args, False)
+
+
+def rasterize_hexels3d_forward_median(*args):
+    return _all(args, True)
+
+
+def rasterize_hexels3d_backward_cached(*args):
+    if len(args) != 35:
+        raise TypeError("rasterize_hexels3d_backward_cached takes 35 arguments")
+    saved = list(args[34])
+    _check(len(saved) == 11, "Expected eleven saved rasterizer buffers")
+    for t in saved:
+        check_input(t, "saved")
+    gs = args[17:21]
+    _check(all(t.numel() == 0 for t in gs),
+           "Cached RGB backward does not accept auxiliary gradients")
+    return _backward_core(*args[:34], saved)
+
+
+def rasterize_hexels3d_backward(*args):
+    """Uncached backward: re-runs the forward (preprocess, binning and, for
+    surface gradients, the surface state) and then the cached backward."""
+    if len(args) != 34:
+        raise TypeError("rasterize_hexels3d_backward takes 34 arguments")
+    (means3d, means2d, scales, rotations, colors, color_grads, color_quads, view_grads,
+     specular_ks, specular_log_s, opacities, softnesses, viewmatrix, projmatrix, campos,
+     background, g_color, g_overdraw, g_depth, g_alpha, g_normals, W, H, tfx, tfy, softness,
+     mod, cm, vm, uvg, odb, pre, cons, dbg) = args
+    surface = g_depth.numel() > 0 or g_alpha.numel() > 0 or g_normals.numel() > 0
+    median = surface and g_normals.numel() > 0 and g_normals.size(0) == 5
+    o = _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
+                      specular_ks, specular_log_s, opacities, softnesses, viewmatrix, projmatrix,
+                      campos, background, W, H, tfx, tfy, softness, mod, cm, vm, uvg, pre, cons,
+                      False, return_surface=surface, overdraw_base_count=odb,
+                      return_median_depth=median, save=True, save_surface=surface)
+    return _backward_core(*args, o["saved"], surf_state=o["surf_state"],
+                          surf_normals=o["normals"] if surface else None)
+
+
+def _not_provided(name: str):
+    def fn(*args, **kwargs):
+        raise NotImplementedError(
+            f"{name} is a diagnostic exact-sort replay of the reference, off the render and "
+            "training path; it is not provided by the B200 build.")
+
+    fn.__name__ = name
+    return fn
+
+
+rasterize_hexels3d_exact_sort_forward = _not_provided("rasterize_hexels3d_exact_sort_forward")
+rasterize_hexels3d_pixel_risk_forward = _not_provided("rasterize_hexels3d_pixel_risk_forward")
+
+
+def _sig(name, n_tensor, n_total, returns):
+    types = ["torch.Tensor"] * n_tensor + ["int", "int", "float", "float", "float", "float",
+                                           "int", "int", "bool", "bool", "bool",
+                                           "bool"][: n_total - n_tensor]
+    params = ", ".join(f"arg{i}: {t}" for i, t in enumerate(types))
+    return f"{name}({params}) -> tuple[{', '.join(['torch.Tensor'] * returns)}]\n"
+
+
+# pybind-style signatures, so callers that validate the extension's arity by
+# its docstrings (gsplat/cuda_hexels3d/__init__.py of the reference) accept it.
+rasterize_hexels3d_forward.__doc__ = _sig("rasterize_hexels3d_forward", 15, 27, 2)
+rasterize_hexels3d_backward.__doc__ = (
+    "rasterize_hexels3d_backward("
+    + ", ".join([f"arg{i}: torch.Tensor" for i in range(21)]
+                + [f"arg{21 + i}: {t}" for i, t in enumerate(
+                    ["int", "int", "float", "float", "float", "float", "int", "int", "bool",
+                     "int", "bool", "bool", "bool"])])
+    + ") -> tuple[" + ", ".join(["torch.Tensor"] * 12) + "]\n")

@@ -235,6 +235,103 @@ HX_API int hx_hexels2d_backward(
     float* v_affines, float* v_colors, float* v_color_grads, float* v_emission,
     float* v_sharpness, float* v_softnesses, cudaStream_t stream);
 
+/* ---- S6-S8: 3D hexel surfels ------------------------------------------- */
+
+/* Per-surfel preprocessing; replaces the kernel preprocess_hexels3d and its
+ * launch (gsplat/cuda_hexels3d/csrc/hexels3d_forward.cu:372-551, 2940-2972).
+ * rotations are WXYZ quaternions (P,4); softnesses (P,) or (P,3) with
+ * softness_stride 1 or 3, or NULL to use softness_default (stride 1).
+ * Writes radii (P,), tile_radii (P,2), points_xy_image (P,2),
+ * points_xy_center (P,2; only with prefilter_edge_on, else may be NULL),
+ * depths (P,), transMats (P,9), tiles_touched (P,), opacities_out (P,),
+ * softnesses_out (P,) or (P,3), view_dirs (P,3) and, if not NULL, normals
+ * (P,3).  Every element is written (zeros for culled surfels). */
+HX_API int hx_hexels3d_preprocess(
+    int P, const float* means3d, const float* scales, float scale_modifier,
+    const float* rotations, const float* opacities, const float* softnesses,
+    float softness_default, int softness_stride, const float* viewmatrix,
+    const float* projmatrix, const float* campos, int image_width, int image_height,
+    int prefilter_edge_on, int conservative_bounds, int32_t* radii, int32_t* tile_radii,
+    float* points_xy_image, float* points_xy_center, float* depths, float* transMats,
+    int32_t* tiles_touched, float* opacities_out, float* softnesses_out, float* view_dirs,
+    float* normals, cudaStream_t stream);
+
+/* Intersection emission, stable sort and tile ranges; replaces
+ * duplicate_with_keys + cub::DeviceRadixSort::SortPairs + identify_tile_ranges
+ * (hexels3d_forward.cu:553-604, 2990-3043).  offsets = inclusive scan of
+ * tiles_touched; num_rendered its total.  Writes keys_sorted (I,) int64
+ * (tile << 32 | depth bits), point_list (I,) and ranges (tiles,2) (zeros for
+ * empty tiles). */
+HX_API size_t hx_hexels3d_bin_workspace_bytes(int num_rendered);
+HX_API int hx_hexels3d_bin(int P, int num_rendered, int image_width, int image_height,
+                           const float* points_xy_image, const float* depths,
+                           const int32_t* offsets, const int32_t* radii,
+                           const int32_t* tile_radii, int64_t* keys_sorted,
+                           int32_t* point_list, int32_t* ranges, void* workspace,
+                           size_t workspace_bytes, cudaStream_t stream);
+
+/* Front-to-back compositing; replaces render_hexels3d<S,F,O> and its launches
+ * (hexels3d_forward.cu:610-1011, 3047-3467).  out_color (3,H,W).  Optional
+ * outputs (NULL = not requested): contrib (P,), overdraw and overdraw_hits
+ * (H,W); surface outputs out_depth, out_alpha (H,W) and out_surface (4 or 5,
+ * H,W) (needs normals); owner outputs (owner_id int64, weight, uv (2,H,W),
+ * sdf, depth, total alpha); final_T and last_index (H,W) for the RGB
+ * backward; final_T_surf, last_index_surf, m1_surf, m2_surf, median_index
+ * (H,W) for the surface backward.  points_xy_center non-NULL selects the
+ * prefilter path. */
+HX_API int hx_hexels3d_render_forward(
+    int P, int num_rendered, const int32_t* ranges, const int32_t* point_list,
+    const float* points_xy_center, int image_width, int image_height, const float* colors,
+    const float* color_grads, const float* color_quads, const float* view_grads,
+    const float* specular_ks, const float* specular_log_s, const float* view_dirs,
+    const float* transMats, const float* opacities, const float* softnesses,
+    int softness_stride, const float* background, const float* normals, int overdraw_base_count,
+    int color_model, int view_model, int use_view_grads, int return_median_depth,
+    float* out_color, float* contrib, float* overdraw, float* overdraw_hits, float* out_depth,
+    float* out_alpha, float* out_surface, int64_t* owner_id, float* owner_weight,
+    float* owner_uv, float* owner_sdf, float* owner_depth, float* total_alpha, float* final_T,
+    int32_t* last_index, float* final_T_surf, int32_t* last_index_surf, float* m1_surf,
+    float* m2_surf, int32_t* median_index, cudaStream_t stream);
+
+/* Reverse traversal VJP; replaces render_hexels3d_backward<S,F> and its
+ * launches (hexels3d_forward.cu:1749-2492, 5323-5505).  Uses the forward's
+ * saved final_T/last_index (and the surface state when surface gradients are
+ * given).  All gradient outputs are ACCUMULATED (clear them first);
+ * grad_transMats (P,9), grad_view_dirs (P,3) and grad_normals (P,3) are
+ * intermediates for hx_hexels3d_geometry_backward. */
+HX_API int hx_hexels3d_render_backward(
+    int P, int num_rendered, const int32_t* ranges, const int32_t* point_list,
+    const float* points_xy_center, float* grad_points_xy_center, int image_width,
+    int image_height, const float* colors, const float* color_grads, const float* color_quads,
+    const float* view_grads, const float* specular_ks, const float* specular_log_s,
+    int view_model, const float* view_dirs, const float* transMats, const float* opacities,
+    const float* softnesses, int softness_stride, const float* background,
+    const float* grad_out_color, const float* grad_out_overdraw,
+    const float* grad_out_surf_depth, const float* grad_out_surf_alpha,
+    const float* grad_out_surf_normals, int has_median_grad, const float* normals,
+    float* grad_colors, float* grad_color_grads, float* grad_color_quads, float* grad_view_grads,
+    float* grad_specular_ks, float* grad_specular_log_s, float* grad_opacities,
+    float* grad_softnesses, float* grad_transMats, float* abs_means2d, float* grad_view_dirs,
+    float* grad_normals, int overdraw_base_count, int color_model, int use_view_grads,
+    const float* final_T, const int32_t* last_index, const float* final_T_surf,
+    const int32_t* last_index_surf, const float* m1_surf, const float* m2_surf,
+    const int32_t* median_index, cudaStream_t stream);
+
+/* VJP from transforms (and view directions / normals) to means3d, scales and
+ * WXYZ rotations, plus the screen-gradient proxy for means2d and the
+ * prefilter-centre VJP; replaces transmat_to_geometry_backward,
+ * transmat_to_means2d_backward and points_xy_center_to_means3d_backward
+ * (hexels3d_forward.cu:2494-2664).  grad_means3d, grad_scales and
+ * grad_rotations are written for visible surfels and must be zeroed first;
+ * grad_means2d (P, means2d_stride) may be NULL. */
+HX_API int hx_hexels3d_geometry_backward(
+    int P, int num_rendered, const float* means3d, const float* scales, float scale_modifier,
+    const float* rotations, const float* projmatrix, const float* campos, int image_width,
+    int image_height, const int32_t* radii, const float* transMats, const float* grad_transMats,
+    const float* grad_view_dirs, const float* grad_normals, const float* grad_points_xy_center,
+    float* grad_means3d, float* grad_means2d, int means2d_stride, float* grad_scales,
+    float* grad_rotations, cudaStream_t stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

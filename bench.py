@@ -402,6 +402,399 @@ def run_e2e(w, args, world, rank):
 
 
 # ---------------------------------------------------------------------------
+# 3D hexel surfels: multi-view fit step
+# ---------------------------------------------------------------------------
+# Synthetic loss of one view (the reference's depth/normal outputs all get a
+# gradient): mean((rgb - target)^2) + LAMBDA_DEPTH mean(depth)
+# + LAMBDA_ALPHA mean(1 - alpha) + LAMBDA_NORMAL mean(1 - normal . n_ref)
+# + LAMBDA_DIST mean(distortion).
+LAMBDA_DEPTH, LAMBDA_ALPHA, LAMBDA_NORMAL, LAMBDA_DIST = 1e-3, 1e-2, 5e-2, 1e-2
+N_REF = (0.0, 0.0, 1.0)
+# Modelled FP32 work of one evaluated (pixel, surfel) pair in the forward
+# compositing (ray-splat intersection 21, projection divides 4, depth 5,
+# hexagon SDF 10, sigmoid 5, alpha and transmittance 5, colour 22).
+FWD_FLOP_PER_PAIR = 72.0
+
+
+def view_split(num_views: int, world: int, rank: int):
+    b = num_views * rank // world
+    e = num_views * (rank + 1) // world
+    return list(range(b, e))
+
+
+def make_targets(w, views, device):
+    """Seeded U[0,1) target image per view (3,H,W)."""
+    cam = w.cameras[0]
+    out = []
+    for v in views:
+        g = torch.Generator().manual_seed(20261201 + 7919 * (v + 1))
+        out.append(torch.rand((3, cam.height, cam.width), generator=g).to(device))
+    return out
+
+
+def surface_grad_constants(H, W, device):
+    hw = float(H * W)
+    gd = torch.full((H, W), LAMBDA_DEPTH / hw, device=device)
+    ga = torch.full((H, W), -LAMBDA_ALPHA / hw, device=device)
+    gn = torch.empty((4, H, W), device=device)
+    for c in range(3):
+        gn[c].fill_(-LAMBDA_NORMAL * N_REF[c] / hw)
+    gn[3].fill_(LAMBDA_DIST / hw)
+    return gd, ga, gn
+
+
+class Hexels3DStep:
+    """Device-resident multi-view step through the same kernels as the public
+    autograd API (cuda_hexels3d._C forward with surface state saved, cached
+    backward), CUDA events between stages."""
+
+    STAGES = ("preprocess", "scan", "bin", "render_fwd", "loss", "render_bwd", "geometry_bwd",
+              "accumulate", "allreduce")
+
+    def __init__(self, w, world: int, rank: int):
+        from gsplat.cuda_hexels3d import _C
+
+        self.C = _C
+        self.w = w
+        self.world, self.rank = world, rank
+        self.views = view_split(len(w.cameras), world, rank)
+        dev = torch.device("cuda")
+        self.dev = dev
+        self.params = [t.to(dev) for t in (w.means3d, w.scales, w.rotations, w.colors,
+                                           w.color_grads, w.view_grads, w.opacities)]
+        self.bg = w.background.to(dev)
+        self.cams = [w.cameras[v].to(dev) for v in self.views]
+        self.targets = make_targets(w, self.views, dev)
+        cam = w.cameras[0]
+        self.H, self.W = cam.height, cam.width
+        self.gd, self.ga, self.gn = surface_grad_constants(self.H, self.W, dev)
+        self.empty = torch.empty(0, device=dev)
+        self.numel = 3 * self.H * self.W
+        self.acc = None
+        self.marks: list = []
+        self.stage_ms = {k: 0.0 for k in self.STAGES}
+        self.info: dict = {}
+
+    def _mark(self, name):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.marks.append((name, ev))
+
+    def _view(self, cam, target, keep_info):
+        C, e = self.C, self.empty
+        m3, sc, rot, col, cg, vg, op = self.params
+        o = C._forward_core(m3, sc, rot, col, cg, e, vg, e, e, op, e, cam.viewmatrix,
+                            cam.projmatrix, cam.campos, self.bg, self.W, self.H, cam.tan_fovx,
+                            cam.tan_fovy, self.w.softness, 1.0, 1, 1, True, False, False, False,
+                            return_surface=True, save=True, save_surface=True)
+        diff = o["out_color"] - target
+        loss = (diff * diff).sum() / self.numel
+        g_color = diff * (2.0 / self.numel)
+        self._mark("loss")
+        grads = C._backward_core(m3, e, sc, rot, col, cg, e, vg, e, e, op, e, cam.viewmatrix,
+                                 cam.projmatrix, cam.campos, self.bg, g_color, e, self.gd,
+                                 self.ga, self.gn, self.W, self.H, cam.tan_fovx, cam.tan_fovy,
+                                 self.w.softness, 1.0, 1, 1, True, -1, False, False, False,
+                                 o["saved"], surf_state=o["surf_state"],
+                                 surf_normals=o["normals"])
+        if keep_info:
+            saved = o["saved"]
+            self.info.setdefault("num_rendered", []).append(o["num_rendered"])
+            self.info.setdefault("evaluated_pairs", []).append(
+                int(saved[10].to(torch.int64).sum().item()))
+        return loss, grads
+
+    def run(self, timed: bool, keep_info: bool = False):
+        self.marks = []
+        self.C.stage_hook = self._mark
+        try:
+            self._mark("start")
+            total = torch.zeros((), device=self.dev)
+            if self.acc is None:
+                self.acc = [torch.zeros_like(p) for p in self.params]
+            for a in self.acc:
+                a.zero_()
+            for cam, tgt in zip(self.cams, self.targets):
+                loss, g = self._view(cam, tgt, keep_info)
+                # grads: means3d, means2d, scales, rotations, colors, color_grads,
+                # color_quads, view_grads, specular_ks, specular_log_s, opacities, softnesses
+                for a, gi in zip(self.acc, (g[0], g[2], g[3], g[4], g[5], g[7], g[10])):
+                    a.add_(gi)
+                total = total + loss
+                self._mark("accumulate")
+            if self.world > 1:
+                import torch.distributed as dist
+
+                packed = torch.cat([a.view(-1) for a in self.acc] + [total.view(1)])
+                dist.all_reduce(packed)
+                total = packed[-1]
+            self._mark("allreduce")
+        finally:
+            self.C.stage_hook = None
+        return total
+
+    def collect(self):
+        for (_, a), (name, b) in zip(self.marks[:-1], self.marks[1:]):
+            self.stage_ms[name] += a.elapsed_time(b)
+
+
+def run_ours_3d(args, world, rank, local):
+    import workloads
+    from gsplat._lib import lib
+
+    w = workload_3d(args.config)
+    step = Hexels3DStep(w, world, rank)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    for i in range(args.warmup):
+        step.run(False, keep_info=(i == 0))
+    torch.cuda.synchronize()
+    step.stage_ms = {k: 0.0 for k in step.STAGES}
+    clocks = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    launches0 = lib.dll.hx_launch_count()
+    total_ms = 0.0
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(args.steps):
+        flush.zero_()
+        st.record()
+        step.run(True)
+        en.record()
+        torch.cuda.synchronize()
+        step.collect()
+        total_ms += st.elapsed_time(en)
+    launches = lib.dll.hx_launch_count() - launches0
+    barrier(world)
+    clk = clocks.stop()
+    total_ms = max_over_ranks(total_ms, world)
+    ms_per_step = total_ms / args.steps
+    stage_ms = {k: max_over_ranks(v / args.steps, world) for k, v in step.stage_ms.items()}
+    pairs_rank = sum(step.info.get("evaluated_pairs", [0]))
+    rendered_rank = sum(step.info.get("num_rendered", [0]))
+    e2e = run_e2e_3d(w, args, world, rank)
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    nviews = len(w.cameras)
+    mpix = nviews * step.H * step.W / 1e6
+    value = mpix / (ms_per_step / 1e3)
+    fp32_peak = NUM_SMS * FP32_LANES_PER_SM * 2 * peaks["sm_max_mhz"] * 1e6 / 1e12
+    fwd_ms = stage_ms["render_fwd"]
+    nv_rank = len(step.views)
+    fwd_flops = pairs_rank * FWD_FLOP_PER_PAIR
+    achieved = fwd_flops / (fwd_ms / 1e3) / 1e12 if fwd_ms > 0 else 0.0
+    roofline = {
+        "kernel": "render3d_fwd_kernel (rasterize_hexels3d forward, surface outputs)",
+        "bound": "fp32",
+        "achieved": round(achieved, 3),
+        "peak": round(fp32_peak, 2),
+        "unit": "TFLOP/s",
+        "frac": round(achieved / fp32_peak, 4),
+        "traffic": None,
+        "peak_source": "nominal FP32 FMA rate, 148 SMs x 128 lanes x 2 x max SM clock "
+                       "(no measured FP32 peak in MEASURED_PEAKS.json)",
+        "work": f"{pairs_rank} evaluated (pixel, surfel) pairs on rank 0 over {nv_rank} views "
+                f"(sum of per-pixel last indices) x {FWD_FLOP_PER_PAIR:.0f} FLOP",
+    }
+    line = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "frames_per_s": round(nviews / (ms_per_step / 1e3), 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded; the reference publishes no dataset)",
+        "config": {
+            "workload": w.name,
+            "views": nviews, "height": step.H, "width": step.W, "num_surfels": w.num_points,
+            "outputs": "rgb + depth + alpha + normal + distortion",
+            "color_model": "linear", "view_model": "linear",
+            "intersections_per_view_rank0": round(rendered_rank / max(1, nv_rank)),
+            "parallelism": f"views split over {world} GPUs, surfels replicated, gradients "
+                           "NCCL all-reduced" if world > 1 else "single GPU",
+            "l2": "flushed between timed steps (256 MB write)",
+        },
+        "stages_ms": {k: round(v, 4) for k, v in stage_ms.items()},
+        "roofline": roofline,
+        "e2e": e2e,
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+    if world == 1:
+        cpu = cpu_baseline_3d(args, w)
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        ref = ref_cuda_timing_3d(args, w)
+        if ref is not None:
+            line["ref_cuda_sm100a"] = ref
+    return line
+
+
+def run_e2e_3d(w, args, world, rank):
+    """The multi-view step through gsplat.rasterize_hexels3d (autograd), the
+    surfel parameters and this rank's target images copied from pinned host
+    memory every step and the loss read back."""
+    import gsplat
+
+    views = view_split(len(w.cameras), world, rank)
+    host_params = [t.pin_memory() for t in (w.means3d, w.scales, w.rotations, w.colors,
+                                           w.color_grads, w.view_grads, w.opacities)]
+    host_targets = [t.pin_memory() for t in make_targets(w, views, "cpu")]
+    cams = [w.cameras[v].to("cuda") for v in views]
+    h2d = sum(t.numel() * t.element_size() for t in host_params + host_targets)
+    bg = w.background.to("cuda")
+    n_ref = torch.tensor(N_REF, device="cuda").view(3, 1, 1)
+
+    def one():
+        params = [t.to("cuda", non_blocking=True).requires_grad_(True) for t in host_params]
+        total = torch.zeros((), device="cuda")
+        for cam, ht in zip(cams, host_targets):
+            tgt = ht.to("cuda", non_blocking=True)
+            color, radii, depth, alpha, normals, dist_map = gsplat.rasterize_hexels3d(
+                *params[:7], cam.viewmatrix, cam.projmatrix, cam.campos, bg, cam.width,
+                cam.height, cam.tan_fovx, cam.tan_fovy, w.softness, return_surface=True,
+                return_distortion=True)
+            d = color - tgt
+            loss = ((d * d).mean() + LAMBDA_DEPTH * depth.mean() +
+                    LAMBDA_ALPHA * (1.0 - alpha).mean() +
+                    LAMBDA_NORMAL * (1.0 - (normals * n_ref).sum(0)).mean() +
+                    LAMBDA_DIST * dist_map.mean())
+            loss.backward()
+            total = total + loss.detach()
+        if world > 1:
+            import torch.distributed as dist
+
+            packed = torch.cat([p.grad.view(-1) for p in params] + [total.view(1)])
+            dist.all_reduce(packed)
+            total = packed[-1]
+        return float(total.item())
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        one()
+    torch.cuda.synchronize()
+    barrier(world)
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, min(args.steps, args.e2e_steps))
+    st.record()
+    for _ in range(steps):
+        one()
+    en.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(st.elapsed_time(en) / steps, world)
+    cam = w.cameras[0]
+    return {"value": round(len(w.cameras) * cam.height * cam.width / 1e6 / (ms / 1e3), 3),
+            "unit": UNIT, "ms_per_step": round(ms, 4), "steps": steps,
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
+            "path": "gsplat.rasterize_hexels3d(return_surface=True, return_distortion=True) per "
+                    "view + loss.backward()"}
+
+
+def ref_cuda_timing_3d(args, w):
+    """The reference's CUDA kernels (compiled from its sources) on the same
+    views, driven by the reference's own call sequence for surface outputs:
+    rasterize_hexels3d_forward_all, then the uncached rasterize_hexels3d_backward
+    (gsplat/rasterize_hexels3d.py:2294-2492)."""
+    path = os.path.join(ROOT, "oracle", "_ref", "_ref_hexels3d_C.so")
+    if not os.path.exists(path):
+        return None
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_ref_hexels3d_C", path)
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    dev = torch.device("cuda")
+    views = list(range(len(w.cameras)))
+    m3, sc, rot, col, cg, vg, op = (t.to(dev) for t in (w.means3d, w.scales, w.rotations,
+                                                        w.colors, w.color_grads, w.view_grads,
+                                                        w.opacities))
+    bg = w.background.to(dev)
+    cams = [w.cameras[v].to(dev) for v in views]
+    targets = make_targets(w, views, dev)
+    H, W = cams[0].height, cams[0].width
+    gd, ga, gn = surface_grad_constants(H, W, dev)
+    e = torch.empty(0, device=dev)
+    numel = 3 * H * W
+
+    def step():
+        for cam, tgt in zip(cams, targets):
+            scal = (W, H, cam.tan_fovx, cam.tan_fovy, w.softness, 1.0, 1, 1, True)
+            tens = (m3, sc, rot, col, cg, e, vg, e, e, op, e, cam.viewmatrix, cam.projmatrix,
+                    cam.campos, bg)
+            out = ref.rasterize_hexels3d_forward_all(*tens, *scal, False, False, False, True, -1,
+                                                     False, False, False)
+            g_color = (out[0] - tgt) * (2.0 / numel)
+            ref.rasterize_hexels3d_backward(m3, e, *tens[1:], g_color, e, gd, ga, gn, *scal, -1,
+                                            False, False, False)
+
+    steps = max(1, min(args.steps, args.ref_max_steps))
+    for _ in range(min(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    total = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        st.record()
+        step()
+        en.record()
+        torch.cuda.synchronize()
+        total += st.elapsed_time(en)
+    ms = total / steps
+    return {"value": round(len(views) * H * W / 1e6 / (ms / 1e3), 3), "unit": UNIT,
+            "ms_per_step": round(ms, 4), "steps": steps,
+            "what": "reference CUDA kernels compiled from its sources for sm_100a "
+                    "(-O3 --use_fast_math): forward_all with surface outputs + uncached "
+                    "backward per view, same inputs and upstream gradients"}
+
+
+def workload_3d(name):
+    import workloads
+
+    if name == "hexels3d_multiview":
+        return workloads.hexels3d_multiview(64)
+    if name == "hexels3d_single":
+        return workloads.hexels3d_single()
+    raise ValueError(name)
+
+
+def cpu_baseline_3d(args, w):
+    try:
+        from oracle import hexels3d  # noqa: F401
+    except ImportError:
+        return None
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    secs, mpix, desc = cpu_sample_run_3d(w, args.cpu_crop_tiles)
+    return {"value": round(mpix / secs, 5), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": desc, "seconds": round(secs, 3)}
+
+
+def cpu_sample_run_3d(w, crop_tiles: int):
+    """One fwd+bwd of the oracle over a crop_tiles x crop_tiles tile crop at
+    the centre of view 0: preprocess of all surfels, binning of those meeting
+    the crop, compositing with surface outputs and the backward."""
+    from oracle import hexels3d as o
+
+    cam = w.cameras[0]
+    t0 = time.perf_counter()
+    mpix = o.sample_fwd_bwd(w, cam, crop_tiles, make_targets(w, [0], "cpu")[0],
+                            (LAMBDA_DEPTH, LAMBDA_ALPHA, LAMBDA_NORMAL, LAMBDA_DIST), N_REF)
+    secs = time.perf_counter() - t0
+    desc = (f"one fwd+bwd over a {crop_tiles}x{crop_tiles}-tile ({mpix:.4f} Mpix) centre crop "
+            f"of view 0 of {w.name}: preprocess of all surfels, binning of those meeting the "
+            f"crop, compositing with depth/normal outputs and backward; {secs:.2f} s")
+    return secs, mpix, desc
+
+
+# ---------------------------------------------------------------------------
 # CPU baseline: the oracle (restated reference algorithm) on host cores
 # ---------------------------------------------------------------------------
 def cpu_sample_run(w, crop_tiles: int):
@@ -557,10 +950,12 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", default="imagegs_large",
-                    choices=["imagegs_large", "imagegs_small"])
+    ap.add_argument("--config", default="hexels3d_multiview",
+                    choices=["hexels3d_multiview", "hexels3d_single", "imagegs_large",
+                             "imagegs_small"])
     ap.add_argument("--cpu-crop-tiles", type=int, default=16)
     ap.add_argument("--ref-max-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=3)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -575,7 +970,10 @@ def main():
 
     world, rank, local = dist_setup(args.gpus)
     try:
-        line = run_ours(args, world, rank, local)
+        if args.config.startswith("hexels3d"):
+            line = run_ours_3d(args, world, rank, local)
+        else:
+            line = run_ours(args, world, rank, local)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

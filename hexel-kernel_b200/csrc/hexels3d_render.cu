@@ -255,17 +255,11 @@ __global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a)
         a.final_T[pix_id] = T;
         a.last_index[pix_id] = n_visited;
     }
-    if (a.num_rendered > 0) {
-        a.out_color[pix_id] = C0 + T * a.bg[0];
-        a.out_color[HW + pix_id] = C1 + T * a.bg[1];
-        a.out_color[2 * HW + pix_id] = C2 + T * a.bg[2];
-    } else {
-        // With nothing binned the reference launches no compositing and
-        // returns its zero-initialised image (no background).
-        a.out_color[pix_id] = 0.f;
-        a.out_color[HW + pix_id] = 0.f;
-        a.out_color[2 * HW + pix_id] = 0.f;
-    }
+    // With nothing binned every tile range is empty and the pixel is the
+    // background, as in the reference (hexels3d_forward.cu:3300-3470).
+    a.out_color[pix_id] = C0 + T * a.bg[0];
+    a.out_color[HW + pix_id] = C1 + T * a.bg[1];
+    a.out_color[2 * HW + pix_id] = C2 + T * a.bg[2];
     if (a.overdraw) a.overdraw[pix_id] = overdraw;
     if (a.overdraw_hits) a.overdraw_hits[pix_id] = overdraw_hits;
     if (SURF) {

@@ -26,6 +26,16 @@ from .._lib import check_input, lib, ptr, stream, workspace
 kNumChannels = 3
 _EMPTY_CACHE: dict = {}
 
+# Optional callable invoked with a stage name after each stage's launches
+# ("preprocess", "scan", "bin", "render_fwd", "render_bwd", "geometry_bwd"),
+# e.g. to record CUDA events between stages.  None in normal use.
+stage_hook = None
+
+
+def _mark(name: str) -> None:
+    if stage_hook is not None:
+        stage_hook(name)
+
 
 def _empty(x: torch.Tensor, dtype=None) -> torch.Tensor:
     return torch.empty((0,), device=x.device, dtype=dtype or x.dtype)
@@ -144,11 +154,13 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                  ptr(points_xy_image), ptr(points_xy_center) if prefilter_edge_on else None,
                  ptr(depths), ptr(transMats), ptr(tiles_touched), ptr(opacities_out),
                  ptr(softnesses_out), ptr(view_dirs), ptr(normals) if need_normals else None, s)
+        _mark("preprocess")
         offsets = torch.empty((P,), **i32)
         total = torch.zeros((1,), dtype=torch.int64, device=dev)
         ws = workspace(lib.query("hx_scan_workspace_bytes", P), dev)
         lib.call("hx_inclusive_scan_i32", ptr(tiles_touched), ptr(offsets), P, ptr(total),
                  ptr(ws), ws.numel(), s)
+        _mark("scan")
         num_rendered = int(total.item()) if P > 0 else 0
         _check(num_rendered <= 2**31 - 1, "number of rendered intersections overflows int32")
         tx, ty = (W + 15) // 16, (H + 15) // 16
@@ -160,6 +172,7 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                  ptr(offsets), ptr(radii), ptr(tile_radii), ptr(keys_sorted),
                  ptr(values_sorted), ptr(ranges), ptr(ws), ws.numel(), s)
 
+        _mark("bin")
         out_color = torch.zeros((kNumChannels, H, W), **f32)
         contrib = torch.zeros((P,), **f32) if return_contrib else torch.empty((0,), **f32)
         overdraw = torch.zeros((H, W), **f32) if return_overdraw else torch.empty((0,), **f32)
@@ -184,35 +197,28 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                    torch.zeros((H, W), **f32), torch.zeros((2, H, W), **f32),
                    torch.zeros((H, W), **f32), torch.zeros((H, W), **f32),
                    torch.zeros((H, W), **f32))
-        if num_rendered > 0:
-            lib.call("hx_hexels3d_render_forward", P, num_rendered, ptr(ranges),
-                     ptr(values_sorted), ptr(points_xy_center) if prefilter_edge_on else None,
-                     W, H, ptr(colors), ptr(color_grads) if color_model >= 1 else None,
-                     ptr(color_quads) if color_model >= 2 else None,
-                     ptr(view_grads) if use_view_grads else None,
-                     ptr(specular_ks) if view_model == 2 else None,
-                     ptr(specular_log_s) if view_model == 2 else None, ptr(view_dirs),
-                     ptr(transMats), ptr(opacities_out), ptr(softnesses_out), stride,
-                     ptr(background), ptr(normals) if need_normals else None,
-                     int(overdraw_base_count), int(color_model), int(view_model),
-                     int(bool(use_view_grads)), int(bool(return_median_depth)),
-                     ptr(out_color), ptr(contrib) if return_contrib else None,
-                     ptr(overdraw) if return_overdraw else None,
-                     ptr(overdraw_hits) if return_overdraw_hits else None,
-                     ptr(surf_depth) if return_surface else None,
-                     ptr(surf_alpha) if return_surface else None,
-                     ptr(surf_maps) if return_surface else None,
-                     *(ptr(t) for t in own) if own else (None,) * 6,
-                     ptr(final_T) if save else None, ptr(last_index) if save else None,
-                     *(ptr(t) for t in surf_state) if surf_state else (None,) * 5, s)
-        elif save:
-            final_T.fill_(1.0)
-            last_index.zero_()
-            if surf_state:
-                surf_state[0].fill_(1.0)
-                for t in surf_state[1:4]:
-                    t.zero_()
-                surf_state[4].fill_(-1)
+        # launched even with nothing binned: every pixel is then the background
+        lib.call("hx_hexels3d_render_forward", P, num_rendered, ptr(ranges),
+                 ptr(values_sorted), ptr(points_xy_center) if prefilter_edge_on else None,
+                 W, H, ptr(colors), ptr(color_grads) if color_model >= 1 else None,
+                 ptr(color_quads) if color_model >= 2 else None,
+                 ptr(view_grads) if use_view_grads else None,
+                 ptr(specular_ks) if view_model == 2 else None,
+                 ptr(specular_log_s) if view_model == 2 else None, ptr(view_dirs),
+                 ptr(transMats), ptr(opacities_out), ptr(softnesses_out), stride,
+                 ptr(background), ptr(normals) if need_normals else None,
+                 int(overdraw_base_count), int(color_model), int(view_model),
+                 int(bool(use_view_grads)), int(bool(return_median_depth)),
+                 ptr(out_color), ptr(contrib) if return_contrib else None,
+                 ptr(overdraw) if return_overdraw else None,
+                 ptr(overdraw_hits) if return_overdraw_hits else None,
+                 ptr(surf_depth) if return_surface else None,
+                 ptr(surf_alpha) if return_surface else None,
+                 ptr(surf_maps) if return_surface else None,
+                 *(ptr(t) for t in own) if own else (None,) * 6,
+                 ptr(final_T) if save else None, ptr(last_index) if save else None,
+                 *(ptr(t) for t in surf_state) if surf_state else (None,) * 5, s)
+        _mark("render_fwd")
         if debug:
             torch.cuda.synchronize(dev)
     saved = None
@@ -323,12 +329,14 @@ def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, col
                      int(overdraw_base_count), int(color_model), int(bool(use_view_grads)),
                      ptr(final_T), ptr(last_index),
                      *(ptr(t) for t in surf_state) if has_surface else (None,) * 5, s)
+            _mark("render_bwd")
             lib.call("hx_hexels3d_geometry_backward", P, num_rendered, ptr(means3d), ptr(scales),
                      float(scale_modifier), ptr(rotations), ptr(projmatrix), ptr(campos), W, H,
                      ptr(radii), ptr(transMats), ptr(grad_transMats), ptr(grad_view_dirs),
                      ptr(grad_normals), ptr(grad_center), ptr(grad_means3d),
                      ptr(grad_means2d) if means2d.numel() > 0 else None, int(stride2d),
                      ptr(grad_scales), ptr(grad_rotations), s)
+            _mark("geometry_bwd")
         if debug:
             torch.cuda.synchronize(dev)
     return (grad_means3d, grad_means2d, grad_scales, grad_rotations, grad_colors,

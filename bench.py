@@ -280,7 +280,7 @@ def run_ours(args, world, rank, local):
     stage_ms = {k: max_over_ranks(v / args.steps, world) for k, v in step.stage_ms.items()}
 
     # end-to-end: public autograd API from pinned host buffers, loss read back
-    e2e = run_e2e(w, args, world, rank)
+    e2e = None if args.skip_extras else run_e2e(w, args, world, rank)
 
     if rank != 0:
         return None
@@ -340,7 +340,7 @@ def run_ours(args, world, rank, local):
         "gpu_launches": int(launches),
         "clocks": clk,
     }
-    if world == 1:
+    if world == 1 and not args.skip_extras:
         line["cpu_baseline"] = cpu_baseline(args, w)
         ref = ref_cuda_timing(args, w)
         if ref is not None:
@@ -402,24 +402,24 @@ def run_e2e(w, args, world, rank):
 
 
 # ---------------------------------------------------------------------------
-# 3D hexel surfels: multi-view fit step
+# 3D hexel surfels
 # ---------------------------------------------------------------------------
-# Synthetic loss of one view (the reference's depth/normal outputs all get a
-# gradient): mean((rgb - target)^2) + LAMBDA_DEPTH mean(depth)
-# + LAMBDA_ALPHA mean(1 - alpha) + LAMBDA_NORMAL mean(1 - normal . n_ref)
-# + LAMBDA_DIST mean(distortion).
-LAMBDA_DEPTH, LAMBDA_ALPHA, LAMBDA_NORMAL, LAMBDA_DIST = 1e-3, 1e-2, 5e-2, 1e-2
-N_REF = (0.0, 0.0, 1.0)
-# Modelled FP32 work of one evaluated (pixel, surfel) pair in the forward
-# compositing (ray-splat intersection 21, projection divides 4, depth 5,
-# hexagon SDF 10, sigmoid 5, alpha and transmittance 5, colour 22).
-FWD_FLOP_PER_PAIR = 72.0
+# c5 (multi-view, default): 64 views of the 1M-surfel scene, the RGB-only
+# cached training path, loss per view mean((rgb - target)^2), views dealt
+# round-robin over the ranks, per-surfel gradients all-reduced once per step.
+# c4 (single view): the same scene from view 0 with depth/normal outputs,
+# loss mean((rgb - target)^2) + 0.1 mean(depth^2) + 0.1 mean(normal^2).
+LAMBDA_DEPTH2, LAMBDA_NORMAL2 = 0.1, 0.1
+# Algorithmic work per unit (FMA = 2 FLOP): forward compositing per
+# evaluated (pixel, surfel) pair, i.e. list entries visited before the
+# pixel terminates (sum of the per-pixel last index); backward compositing
+# per contributing (blended) pair.
+FWD_FLOP_PER_PAIR = 90.0
+BWD_FLOP_PER_PAIR = 260.0
 
 
 def view_split(num_views: int, world: int, rank: int):
-    b = num_views * rank // world
-    e = num_views * (rank + 1) // world
-    return list(range(b, e))
+    return [v for v in range(num_views) if v % world == rank]
 
 
 def make_targets(w, views, device):
@@ -432,30 +432,20 @@ def make_targets(w, views, device):
     return out
 
 
-def surface_grad_constants(H, W, device):
-    hw = float(H * W)
-    gd = torch.full((H, W), LAMBDA_DEPTH / hw, device=device)
-    ga = torch.full((H, W), -LAMBDA_ALPHA / hw, device=device)
-    gn = torch.empty((4, H, W), device=device)
-    for c in range(3):
-        gn[c].fill_(-LAMBDA_NORMAL * N_REF[c] / hw)
-    gn[3].fill_(LAMBDA_DIST / hw)
-    return gd, ga, gn
-
-
 class Hexels3DStep:
-    """Device-resident multi-view step through the same kernels as the public
-    autograd API (cuda_hexels3d._C forward with surface state saved, cached
-    backward), CUDA events between stages."""
+    """Device-resident fit step over this rank's views through the kernels of
+    the public autograd API (cuda_hexels3d._C forward with the backward's
+    state saved, then the cached backward), CUDA events between stages."""
 
     STAGES = ("preprocess", "scan", "bin", "render_fwd", "loss", "render_bwd", "geometry_bwd",
               "accumulate", "allreduce")
 
-    def __init__(self, w, world: int, rank: int):
+    def __init__(self, w, world: int, rank: int, surface: bool):
         from gsplat.cuda_hexels3d import _C
 
         self.C = _C
         self.w = w
+        self.surface = surface
         self.world, self.rank = world, rank
         self.views = view_split(len(w.cameras), world, rank)
         dev = torch.device("cuda")
@@ -467,10 +457,10 @@ class Hexels3DStep:
         self.targets = make_targets(w, self.views, dev)
         cam = w.cameras[0]
         self.H, self.W = cam.height, cam.width
-        self.gd, self.ga, self.gn = surface_grad_constants(self.H, self.W, dev)
         self.empty = torch.empty(0, device=dev)
+        self.zero_hw = torch.zeros((self.H, self.W), device=dev)
         self.numel = 3 * self.H * self.W
-        self.acc = None
+        self.acc = [torch.zeros_like(p) for p in self.params]
         self.marks: list = []
         self.stage_ms = {k: 0.0 for k in self.STAGES}
         self.info: dict = {}
@@ -486,32 +476,44 @@ class Hexels3DStep:
         o = C._forward_core(m3, sc, rot, col, cg, e, vg, e, e, op, e, cam.viewmatrix,
                             cam.projmatrix, cam.campos, self.bg, self.W, self.H, cam.tan_fovx,
                             cam.tan_fovy, self.w.softness, 1.0, 1, 1, True, False, False, False,
-                            return_surface=True, save=True, save_surface=True)
+                            return_surface=self.surface, save=True, save_surface=self.surface,
+                            count_contrib=keep_info)
         diff = o["out_color"] - target
         loss = (diff * diff).sum() / self.numel
         g_color = diff * (2.0 / self.numel)
+        gd = ga = gn = e
+        if self.surface:
+            hw = float(self.H * self.W)
+            depth, normals = o["surf_depth"], o["surf_maps"][:3]
+            loss = loss + LAMBDA_DEPTH2 * (depth * depth).sum() / hw + \
+                LAMBDA_NORMAL2 * (normals * normals).sum() / (3 * hw)
+            gd = depth * (2 * LAMBDA_DEPTH2 / hw)
+            ga = self.zero_hw
+            gn = torch.cat([normals * (2 * LAMBDA_NORMAL2 / (3 * hw)), self.zero_hw[None]])
         self._mark("loss")
         grads = C._backward_core(m3, e, sc, rot, col, cg, e, vg, e, e, op, e, cam.viewmatrix,
-                                 cam.projmatrix, cam.campos, self.bg, g_color, e, self.gd,
-                                 self.ga, self.gn, self.W, self.H, cam.tan_fovx, cam.tan_fovy,
-                                 self.w.softness, 1.0, 1, 1, True, -1, False, False, False,
-                                 o["saved"], surf_state=o["surf_state"],
-                                 surf_normals=o["normals"])
+                                 cam.projmatrix, cam.campos, self.bg, g_color, e, gd, ga, gn,
+                                 self.W, self.H, cam.tan_fovx, cam.tan_fovy, self.w.softness,
+                                 1.0, 1, 1, True, -1, False, False, False, o["saved"],
+                                 surf_state=o["surf_state"],
+                                 surf_normals=o["normals"] if self.surface else None)
         if keep_info:
             saved = o["saved"]
             self.info.setdefault("num_rendered", []).append(o["num_rendered"])
             self.info.setdefault("evaluated_pairs", []).append(
                 int(saved[10].to(torch.int64).sum().item()))
+            self.info.setdefault("blended_pairs", []).append(
+                int(o["contrib_count"].to(torch.int64).sum().item()))
         return loss, grads
 
-    def run(self, timed: bool, keep_info: bool = False):
+    def run(self, keep_info: bool = False):
+        if keep_info:
+            self.info = {}
         self.marks = []
         self.C.stage_hook = self._mark
         try:
             self._mark("start")
             total = torch.zeros((), device=self.dev)
-            if self.acc is None:
-                self.acc = [torch.zeros_like(p) for p in self.params]
             for a in self.acc:
                 a.zero_()
             for cam, tgt in zip(self.cams, self.targets):
@@ -538,65 +540,82 @@ class Hexels3DStep:
             self.stage_ms[name] += a.elapsed_time(b)
 
 
-def run_ours_3d(args, world, rank, local):
-    import workloads
+def time_step_3d(step, steps, warmup, world):
+    """Warm-up (the first one collects the work counts), then `steps` timed
+    steps between barriers, L2 flushed before each; returns (ms per step,
+    stage ms per step, this library's kernel launches in the timed steps),
+    times max over ranks."""
     from gsplat._lib import lib
 
-    w = workload_3d(args.config)
-    step = Hexels3DStep(w, world, rank)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
-    for i in range(args.warmup):
-        step.run(False, keep_info=(i == 0))
+    for i in range(warmup):
+        step.run(keep_info=(i == 0))
     torch.cuda.synchronize()
     step.stage_ms = {k: 0.0 for k in step.STAGES}
-    clocks = ClockSampler(local)
     barrier(world)
     torch.cuda.synchronize()
-    clocks.start()
-    launches0 = lib.dll.hx_launch_count()
     total_ms = 0.0
     st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for _ in range(args.steps):
+    launches0 = lib.dll.hx_launch_count()
+    for _ in range(steps):
         flush.zero_()
         st.record()
-        step.run(True)
+        step.run()
         en.record()
         torch.cuda.synchronize()
         step.collect()
         total_ms += st.elapsed_time(en)
     launches = lib.dll.hx_launch_count() - launches0
     barrier(world)
-    clk = clocks.stop()
-    total_ms = max_over_ranks(total_ms, world)
-    ms_per_step = total_ms / args.steps
-    stage_ms = {k: max_over_ranks(v / args.steps, world) for k, v in step.stage_ms.items()}
-    pairs_rank = sum(step.info.get("evaluated_pairs", [0]))
-    rendered_rank = sum(step.info.get("num_rendered", [0]))
-    e2e = run_e2e_3d(w, args, world, rank)
-    if rank != 0:
-        return None
+    ms = max_over_ranks(total_ms / steps, world)
+    stage = {k: max_over_ranks(v / steps, world) for k, v in step.stage_ms.items()}
+    return ms, stage, launches
+
+
+def roofline_3d(step, stage_ms):
     peaks = measured_peaks()
-    nviews = len(w.cameras)
-    mpix = nviews * step.H * step.W / 1e6
-    value = mpix / (ms_per_step / 1e3)
     fp32_peak = NUM_SMS * FP32_LANES_PER_SM * 2 * peaks["sm_max_mhz"] * 1e6 / 1e12
-    fwd_ms = stage_ms["render_fwd"]
-    nv_rank = len(step.views)
-    fwd_flops = pairs_rank * FWD_FLOP_PER_PAIR
-    achieved = fwd_flops / (fwd_ms / 1e3) / 1e12 if fwd_ms > 0 else 0.0
-    roofline = {
-        "kernel": "render3d_fwd_kernel (rasterize_hexels3d forward, surface outputs)",
+    nv = len(step.views)
+    blended = sum(step.info.get("blended_pairs", [0]))
+    evaluated = sum(step.info.get("evaluated_pairs", [0]))
+    bwd_ms, fwd_ms = stage_ms["render_bwd"], stage_ms["render_fwd"]
+    bwd = blended * BWD_FLOP_PER_PAIR / (bwd_ms / 1e3) / 1e12 if bwd_ms > 0 else 0.0
+    fwd = evaluated * FWD_FLOP_PER_PAIR / (fwd_ms / 1e3) / 1e12 if fwd_ms > 0 else 0.0
+    return {
+        "kernel": "render3d_bwd_kernel (rasterize_hexels3d backward compositing)",
         "bound": "fp32",
-        "achieved": round(achieved, 3),
+        "achieved": round(bwd, 3),
         "peak": round(fp32_peak, 2),
         "unit": "TFLOP/s",
-        "frac": round(achieved / fp32_peak, 4),
+        "frac": round(bwd / fp32_peak, 4),
         "traffic": None,
         "peak_source": "nominal FP32 FMA rate, 148 SMs x 128 lanes x 2 x max SM clock "
-                       "(no measured FP32 peak in MEASURED_PEAKS.json)",
-        "work": f"{pairs_rank} evaluated (pixel, surfel) pairs on rank 0 over {nv_rank} views "
-                f"(sum of per-pixel last indices) x {FWD_FLOP_PER_PAIR:.0f} FLOP",
+                       "(MEASURED_PEAKS.json has no FP32 figure)",
+        "work": f"{blended} blended (pixel, surfel) pairs over {nv} views x "
+                f"{BWD_FLOP_PER_PAIR:.0f} FLOP per step on rank 0",
+        "forward": {"kernel": "render3d_fwd_kernel", "achieved": round(fwd, 3),
+                    "frac": round(fwd / fp32_peak, 4),
+                    "work": f"{evaluated} evaluated pairs x {FWD_FLOP_PER_PAIR:.0f} FLOP"},
     }
+
+
+def run_ours_3d(args, world, rank, local):
+    w = workload_3d(args.config)
+    surface = args.config == "hexels3d_single"
+    step = Hexels3DStep(w, world, rank, surface)
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms_per_step, stage_ms, launches = time_step_3d(step, args.steps, args.warmup, world)
+    clk = clocks.stop()
+    nviews = len(w.cameras)
+    rendered_rank = sum(step.info.get("num_rendered", [0]))
+    e2e = None if args.skip_extras else run_e2e_3d(w, args, world, rank, surface)
+    secondary = None
+    if world == 1 and not args.skip_extras and not surface:
+        secondary = single_view_comparison(args)
+    if rank != 0:
+        return None
+    value = nviews * step.H * step.W / 1e6 / (ms_per_step / 1e3)
     line = {
         "metric": METRIC,
         "value": round(value, 3),
@@ -614,33 +633,54 @@ def run_ours_3d(args, world, rank, local):
         "config": {
             "workload": w.name,
             "views": nviews, "height": step.H, "width": step.W, "num_surfels": w.num_points,
-            "outputs": "rgb + depth + alpha + normal + distortion",
+            "outputs": "rgb + depth + alpha + normal + distortion" if surface else "rgb",
             "color_model": "linear", "view_model": "linear",
-            "intersections_per_view_rank0": round(rendered_rank / max(1, nv_rank)),
-            "parallelism": f"views split over {world} GPUs, surfels replicated, gradients "
-                           "NCCL all-reduced" if world > 1 else "single GPU",
+            "intersections_per_view": round(rendered_rank / max(1, len(step.views))),
+            "parallelism": (f"views dealt round-robin over {world} GPUs, surfels replicated, "
+                            "gradients NCCL all-reduced") if world > 1 else "single GPU",
             "l2": "flushed between timed steps (256 MB write)",
         },
         "stages_ms": {k: round(v, 4) for k, v in stage_ms.items()},
-        "roofline": roofline,
+        "roofline": roofline_3d(step, stage_ms),
         "e2e": e2e,
         "gpu_launches": int(launches),
         "clocks": clk,
     }
-    if world == 1:
+    if secondary is not None:
+        line["single_view_surface"] = secondary
+    if world == 1 and not args.skip_extras:
         cpu = cpu_baseline_3d(args, w)
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        ref = ref_cuda_timing_3d(args, w)
+        ref = ref_cuda_timing_3d(args, w, surface)
         if ref is not None:
             line["ref_cuda_sm100a"] = ref
     return line
 
 
-def run_e2e_3d(w, args, world, rank):
-    """The multi-view step through gsplat.rasterize_hexels3d (autograd), the
-    surfel parameters and this rank's target images copied from pinned host
-    memory every step and the loss read back."""
+def single_view_comparison(args):
+    """The 1080p / 1M-surfel single view with depth/normal outputs, ours and
+    the reference's CUDA kernels on the same inputs (device-resident, L2
+    flushed between steps)."""
+    w = workload_3d("hexels3d_single")
+    step = Hexels3DStep(w, 1, 0, True)
+    ms, stage, _ = time_step_3d(step, max(args.steps, 10), max(args.warmup, 3), 1)
+    H, W = step.H, step.W
+    out = {"workload": w.name, "ms_per_step": round(ms, 4),
+           "value": round(H * W / 1e6 / (ms / 1e3), 3), "unit": UNIT,
+           "stages_ms": {k: round(v, 4) for k, v in stage.items()},
+           "roofline": roofline_3d(step, stage)}
+    del step
+    ref = ref_cuda_timing_3d(args, w, True, steps=max(args.steps, 10))
+    if ref is not None:
+        out["ref_cuda_sm100a"] = ref
+    return out
+
+
+def run_e2e_3d(w, args, world, rank, surface):
+    """The step through gsplat.rasterize_hexels3d (autograd), the surfel
+    parameters and this rank's target images copied from pinned host memory
+    every step and the loss read back."""
     import gsplat
 
     views = view_split(len(w.cameras), world, rank)
@@ -650,22 +690,21 @@ def run_e2e_3d(w, args, world, rank):
     cams = [w.cameras[v].to("cuda") for v in views]
     h2d = sum(t.numel() * t.element_size() for t in host_params + host_targets)
     bg = w.background.to("cuda")
-    n_ref = torch.tensor(N_REF, device="cuda").view(3, 1, 1)
 
     def one():
         params = [t.to("cuda", non_blocking=True).requires_grad_(True) for t in host_params]
         total = torch.zeros((), device="cuda")
         for cam, ht in zip(cams, host_targets):
             tgt = ht.to("cuda", non_blocking=True)
-            color, radii, depth, alpha, normals, dist_map = gsplat.rasterize_hexels3d(
+            out = gsplat.rasterize_hexels3d(
                 *params[:7], cam.viewmatrix, cam.projmatrix, cam.campos, bg, cam.width,
-                cam.height, cam.tan_fovx, cam.tan_fovy, w.softness, return_surface=True,
-                return_distortion=True)
-            d = color - tgt
-            loss = ((d * d).mean() + LAMBDA_DEPTH * depth.mean() +
-                    LAMBDA_ALPHA * (1.0 - alpha).mean() +
-                    LAMBDA_NORMAL * (1.0 - (normals * n_ref).sum(0)).mean() +
-                    LAMBDA_DIST * dist_map.mean())
+                cam.height, cam.tan_fovx, cam.tan_fovy, w.softness, return_surface=surface)
+            d = out[0] - tgt
+            loss = (d * d).mean()
+            if surface:
+                depth, normals = out[2], out[4]
+                loss = loss + LAMBDA_DEPTH2 * (depth * depth).mean() + \
+                    LAMBDA_NORMAL2 * (normals * normals).mean()
             loss.backward()
             total = total + loss.detach()
         if world > 1:
@@ -692,15 +731,17 @@ def run_e2e_3d(w, args, world, rank):
     return {"value": round(len(w.cameras) * cam.height * cam.width / 1e6 / (ms / 1e3), 3),
             "unit": UNIT, "ms_per_step": round(ms, 4), "steps": steps,
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
-            "path": "gsplat.rasterize_hexels3d(return_surface=True, return_distortion=True) per "
-                    "view + loss.backward()"}
+            "path": "gsplat.rasterize_hexels3d(" + ("return_surface=True" if surface else "")
+                    + ") per view + loss.backward()"}
 
 
-def ref_cuda_timing_3d(args, w):
+def ref_cuda_timing_3d(args, w, surface, steps=None):
     """The reference's CUDA kernels (compiled from its sources) on the same
-    views, driven by the reference's own call sequence for surface outputs:
-    rasterize_hexels3d_forward_all, then the uncached rasterize_hexels3d_backward
-    (gsplat/rasterize_hexels3d.py:2294-2492)."""
+    views, driven by the reference's own call sequence: the cached RGB path
+    (rasterize_hexels3d_forward_cached + rasterize_hexels3d_backward_cached,
+    gsplat/rasterize_hexels3d.py:957-1035,1363-1517) or, with surface outputs,
+    rasterize_hexels3d_forward_all + the uncached rasterize_hexels3d_backward
+    (gsplat/rasterize_hexels3d.py:2294-2491)."""
     path = os.path.join(ROOT, "oracle", "_ref", "_ref_hexels3d_C.so")
     if not os.path.exists(path):
         return None
@@ -718,22 +759,32 @@ def ref_cuda_timing_3d(args, w):
     cams = [w.cameras[v].to(dev) for v in views]
     targets = make_targets(w, views, dev)
     H, W = cams[0].height, cams[0].width
-    gd, ga, gn = surface_grad_constants(H, W, dev)
     e = torch.empty(0, device=dev)
+    zero_hw = torch.zeros((H, W), device=dev)
     numel = 3 * H * W
+    hw = float(H * W)
 
     def step():
         for cam, tgt in zip(cams, targets):
             scal = (W, H, cam.tan_fovx, cam.tan_fovy, w.softness, 1.0, 1, 1, True)
             tens = (m3, sc, rot, col, cg, e, vg, e, e, op, e, cam.viewmatrix, cam.projmatrix,
                     cam.campos, bg)
-            out = ref.rasterize_hexels3d_forward_all(*tens, *scal, False, False, False, True, -1,
-                                                     False, False, False)
-            g_color = (out[0] - tgt) * (2.0 / numel)
-            ref.rasterize_hexels3d_backward(m3, e, *tens[1:], g_color, e, gd, ga, gn, *scal, -1,
-                                            False, False, False)
+            if surface:
+                out = ref.rasterize_hexels3d_forward_all(*tens, *scal, False, False, False, True,
+                                                         -1, False, False, False)
+                g_color = (out[0] - tgt) * (2.0 / numel)
+                gd = out[5] * (2 * LAMBDA_DEPTH2 / hw)
+                gn = torch.cat([out[7][:3] * (2 * LAMBDA_NORMAL2 / (3 * hw)), zero_hw[None]])
+                ref.rasterize_hexels3d_backward(m3, e, *tens[1:], g_color, e, gd, zero_hw, gn,
+                                                *scal, -1, False, False, False)
+            else:
+                img, radii, saved = ref.rasterize_hexels3d_forward_cached(*tens, *scal, False,
+                                                                          False, False)
+                g_color = (img - tgt) * (2.0 / numel)
+                ref.rasterize_hexels3d_backward_cached(m3, e, *tens[1:], g_color, e, e, e, e,
+                                                       *scal, -1, False, False, False, saved)
 
-    steps = max(1, min(args.steps, args.ref_max_steps))
+    steps = max(1, min(args.steps, args.ref_max_steps)) if steps is None else steps
     for _ in range(min(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
@@ -751,8 +802,10 @@ def ref_cuda_timing_3d(args, w):
     return {"value": round(len(views) * H * W / 1e6 / (ms / 1e3), 3), "unit": UNIT,
             "ms_per_step": round(ms, 4), "steps": steps,
             "what": "reference CUDA kernels compiled from its sources for sm_100a "
-                    "(-O3 --use_fast_math): forward_all with surface outputs + uncached "
-                    "backward per view, same inputs and upstream gradients"}
+                    "(-O3 --use_fast_math), its own call sequence "
+                    + ("(forward_all + uncached backward, surface outputs)" if surface
+                       else "(forward_cached + backward_cached)")
+                    + ", same inputs and loss"}
 
 
 def workload_3d(name):
@@ -766,13 +819,9 @@ def workload_3d(name):
 
 
 def cpu_baseline_3d(args, w):
-    try:
-        from oracle import hexels3d  # noqa: F401
-    except ImportError:
-        return None
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    secs, mpix, desc = cpu_sample_run_3d(w, args.cpu_crop_tiles)
+    secs, mpix, desc = cpu_sample_run_3d(w, args.cpu_crop_tiles_3d)
     return {"value": round(mpix / secs, 5), "unit": UNIT, "cores": threads, "kind": "port",
             "sample": desc, "seconds": round(secs, 3)}
 
@@ -780,17 +829,16 @@ def cpu_baseline_3d(args, w):
 def cpu_sample_run_3d(w, crop_tiles: int):
     """One fwd+bwd of the oracle over a crop_tiles x crop_tiles tile crop at
     the centre of view 0: preprocess of all surfels, binning of those meeting
-    the crop, compositing with surface outputs and the backward."""
+    the crop, RGB compositing and its backward through the geometry."""
     from oracle import hexels3d as o
 
     cam = w.cameras[0]
     t0 = time.perf_counter()
-    mpix = o.sample_fwd_bwd(w, cam, crop_tiles, make_targets(w, [0], "cpu")[0],
-                            (LAMBDA_DEPTH, LAMBDA_ALPHA, LAMBDA_NORMAL, LAMBDA_DIST), N_REF)
+    mpix = o.sample_fwd_bwd(w, cam, crop_tiles, make_targets(w, [0], "cpu")[0])
     secs = time.perf_counter() - t0
     desc = (f"one fwd+bwd over a {crop_tiles}x{crop_tiles}-tile ({mpix:.4f} Mpix) centre crop "
             f"of view 0 of {w.name}: preprocess of all surfels, binning of those meeting the "
-            f"crop, compositing with depth/normal outputs and backward; {secs:.2f} s")
+            f"crop, compositing, loss and backward to the surfel parameters; {secs:.2f} s")
     return secs, mpix, desc
 
 
@@ -954,8 +1002,12 @@ def main():
                     choices=["hexels3d_multiview", "hexels3d_single", "imagegs_large",
                              "imagegs_small"])
     ap.add_argument("--cpu-crop-tiles", type=int, default=16)
+    ap.add_argument("--cpu-crop-tiles-3d", type=int, default=8)
     ap.add_argument("--ref-max-steps", type=int, default=3)
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--skip-extras", action="store_true",
+                    help="time the device-resident step only (no e2e, CPU baseline or "
+                         "reference CUDA timing), e.g. under a profiler")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

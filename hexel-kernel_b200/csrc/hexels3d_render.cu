@@ -41,6 +41,7 @@ __global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a)
     const int tr = threadIdx.y * k3BlockX + threadIdx.x;
 
     int n_visited = 0;
+    int n_blended = 0;
     float T = 1.0f;
     float C0 = 0.f, C1 = 0.f, C2 = 0.f;
     float overdraw = 0.f, overdraw_hits = 0.f;
@@ -210,6 +211,7 @@ __global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a)
                     C2 += cz * w;
                     T = test_T;
                     n_visited = i * k3BlockSize + j + 1;
+                    ++n_blended;
                     if (a.contrib) atomicAdd(&s_contrib[j], w);
                 }
             }
@@ -255,6 +257,7 @@ __global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a)
         a.final_T[pix_id] = T;
         a.last_index[pix_id] = n_visited;
     }
+    if (a.contrib_count) a.contrib_count[pix_id] = n_blended;
     // With nothing binned every tile range is empty and the pixel is the
     // background, as in the reference (hexels3d_forward.cu:3300-3470).
     a.out_color[pix_id] = C0 + T * a.bg[0];
@@ -317,7 +320,7 @@ extern "C" int hx_hexels3d_render_forward(
     float* out_alpha, float* out_surface, int64_t* owner_id, float* owner_weight,
     float* owner_uv, float* owner_sdf, float* owner_depth, float* total_alpha, float* final_T,
     int32_t* last_index, float* final_T_surf, int32_t* last_index_surf, float* m1_surf,
-    float* m2_surf, int32_t* median_index, cudaStream_t stream) {
+    float* m2_surf, int32_t* median_index, int32_t* contrib_count, cudaStream_t stream) {
     HX_REQUIRE(image_width > 0 && image_height > 0, "invalid image dimensions");
     HX_REQUIRE(color_model >= 0 && color_model <= 3, "color_model must be 0..3");
     HX_REQUIRE(view_model >= 0 && view_model <= 2, "view_model must be 0..2");
@@ -386,6 +389,7 @@ extern "C" int hx_hexels3d_render_forward(
     a.m1_surf = m1_surf;
     a.m2_surf = m2_surf;
     a.median_index = median_index;
+    a.contrib_count = contrib_count;
     if (surf) return prefilter ? launch_render<true, true, false>(a, stream)
                                : launch_render<true, false, false>(a, stream);
     if (owner) return prefilter ? launch_render<false, true, true>(a, stream)

@@ -98,6 +98,8 @@ struct Render3DArgs {
     float* m1_surf;
     float* m2_surf;
     int* median_index;
+    // optional per-pixel count of blended (contributing) pairs, or null
+    int* contrib_count;
 };
 
 struct Backward3DArgs {

@@ -122,7 +122,8 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                   scale_modifier, color_model, view_model, use_view_grads, prefilter_edge_on,
                   conservative_bounds, debug, *, return_contrib=False, return_overdraw=False,
                   return_overdraw_hits=False, return_surface=False, overdraw_base_count=-1,
-                  owner=False, return_median_depth=False, save=False, save_surface=False):
+                  owner=False, return_median_depth=False, save=False, save_surface=False,
+                  count_contrib=False):
     """rasterize_hexels3d_forward_impl (hexels3d_forward.cu:2679-3481)."""
     W, H = int(image_width), int(image_height)
     P, stride = _checks(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
@@ -184,6 +185,7 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
             surf_maps = torch.zeros((kNumChannels + 1 + int(return_median_depth), H, W), **f32)
         else:
             surf_depth = surf_alpha = surf_maps = torch.empty((0,), **f32)
+        contrib_count = torch.empty((H, W), **i32) if count_contrib else None
         final_T = torch.empty((H, W), **f32) if save else torch.empty((0,), **f32)
         last_index = torch.empty((H, W), **i32) if save else torch.empty((0,), **i32)
         surf_state = None
@@ -217,7 +219,8 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                  ptr(surf_maps) if return_surface else None,
                  *(ptr(t) for t in own) if own else (None,) * 6,
                  ptr(final_T) if save else None, ptr(last_index) if save else None,
-                 *(ptr(t) for t in surf_state) if surf_state else (None,) * 5, s)
+                 *(ptr(t) for t in surf_state) if surf_state else (None,) * 5,
+                 ptr(contrib_count) if count_contrib else None, s)
         _mark("render_fwd")
         if debug:
             torch.cuda.synchronize(dev)
@@ -229,7 +232,7 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
     return dict(out_color=out_color, radii=radii, contrib=contrib, overdraw=overdraw,
                 overdraw_hits=overdraw_hits, surf_depth=surf_depth, surf_alpha=surf_alpha,
                 surf_maps=surf_maps, saved=saved, surf_state=surf_state, normals=normals,
-                owner=own, num_rendered=num_rendered)
+                owner=own, num_rendered=num_rendered, contrib_count=contrib_count)
 
 
 def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, color_quads,

@@ -278,7 +278,9 @@ HX_API int hx_hexels3d_bin(int P, int num_rendered, int image_width, int image_h
  * sdf, depth, total alpha); final_T and last_index (H,W) for the RGB
  * backward; final_T_surf, last_index_surf, m1_surf, m2_surf, median_index
  * (H,W) for the surface backward.  points_xy_center non-NULL selects the
- * prefilter path. */
+ * prefilter path.  contrib_count (H,W int32, may be NULL; no reference
+ * counterpart) receives the number of blended (pixel, surfel) pairs per pixel,
+ * the work unit of the backward traversal. */
 HX_API int hx_hexels3d_render_forward(
     int P, int num_rendered, const int32_t* ranges, const int32_t* point_list,
     const float* points_xy_center, int image_width, int image_height, const float* colors,
@@ -291,7 +293,7 @@ HX_API int hx_hexels3d_render_forward(
     float* out_alpha, float* out_surface, int64_t* owner_id, float* owner_weight,
     float* owner_uv, float* owner_sdf, float* owner_depth, float* total_alpha, float* final_T,
     int32_t* last_index, float* final_T_surf, int32_t* last_index_surf, float* m1_surf,
-    float* m2_surf, int32_t* median_index, cudaStream_t stream);
+    float* m2_surf, int32_t* median_index, int32_t* contrib_count, cudaStream_t stream);
 
 /* Reverse traversal VJP; replaces render_hexels3d_backward<S,F> and its
  * launches (hexels3d_forward.cu:1749-2492, 5323-5505).  Uses the forward's

@@ -152,3 +152,69 @@ extern "C" int hx_inclusive_scan_i32(const int32_t* in, int32_t* out, int n, int
     }
     return HX_OK;
 }
+
+// ---------------------------------------------------------------------------
+// No-allocation variant: the per-CTA partial sums live in a fixed file-scope
+// device array (kScanMaxPartials ints = 64 KiB, enough for n up to
+// kScanMaxPartials * kScanTile = 67,108,864 elements) instead of a caller
+// workspace.  Every call on a device shares that array; each call writes
+// every partial it reads before reading it, so nothing needs clearing, but
+// two calls that overlap on one device (concurrent streams or host threads)
+// race on the array and must be serialised by the caller.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+
+static __device__ __align__(256) int g_noalloc_partials[kScanMaxPartials];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+int* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Address of this device's copy of the array, looked up once per device (on
+// the first call with that device current) and cached.
+int noalloc_partials(int** out) {
+    int dev = -1;
+    HX_CUDA_TRY(cudaGetDevice(&dev));
+    HX_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, "scan_noalloc: device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+        if (e != cudaSuccess || p == nullptr)
+            return set_error(HX_ERR_CUDA, "scan_noalloc: cudaGetSymbolAddress failed: %s",
+                             cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = static_cast<int*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return HX_OK;
+}
+
+}  // namespace
+
+extern "C" int hx_inclusive_scan_i32_noalloc(const int32_t* in, int32_t* out, int n,
+                                             int64_t* total_out, cudaStream_t stream) {
+    HX_REQUIRE(n >= 0, "scan_noalloc: n must be non-negative (got %d)", n);
+    HX_REQUIRE(n <= kScanMaxPartials * kScanTile,
+               "scan_noalloc: n=%d exceeds the fixed scratch maximum of %d elements", n,
+               kScanMaxPartials * kScanTile);
+    int* partials = nullptr;
+    const int rc = noalloc_partials(&partials);
+    if (rc != HX_OK) return rc;
+    if (n == 0) {
+        if (total_out) HX_CUDA_TRY(cudaMemsetAsync(total_out, 0, sizeof(int64_t), stream));
+        return HX_OK;
+    }
+    HX_REQUIRE(in && out, "scan_noalloc: null pointer");
+    const int tiles = ceil_div(n, kScanTile);
+    scan_tiles_kernel<<<tiles, kScanThreads, 0, stream>>>(in, out, n, partials);
+    HX_LAUNCH_CHECK("scan_tiles_kernel");
+    scan_partials_kernel<<<1, 1024, 0, stream>>>(partials, tiles, (long long*)total_out);
+    HX_LAUNCH_CHECK("scan_partials_kernel");
+    if (tiles > 1) {
+        scan_add_kernel<<<tiles, 256, 0, stream>>>(out, n, partials);
+        HX_LAUNCH_CHECK("scan_add_kernel");
+    }
+    return HX_OK;
+}

@@ -89,6 +89,23 @@ HX_API size_t hx_scan_workspace_bytes(int n);
 HX_API int hx_inclusive_scan_i32(const int32_t* in, int32_t* out, int n, int64_t* total_out,
                           void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* hx_inclusive_scan_i32 without a workspace; it has no counterpart in the
+ * reference.  For callers that cannot allocate device memory at the call
+ * site: an FFI binding of this C-ABI that owns no device allocator, a process
+ * whose device memory is held by a caching allocator (a raw cudaMalloc can
+ * fail there although cached blocks are free), or code that must not
+ * synchronise the device (cudaMalloc/cudaFree do).  The per-block partial
+ * sums live in a fixed 64 KiB file-scope device array, so n is limited to
+ * 67,108,864; larger n is rejected with HX_ERR_INVALID_ARGUMENT.  The first
+ * call on each device (with that device current) looks the array's address
+ * up once with cudaGetSymbolAddress and caches it; make that first call
+ * before any stream capture.  All calls on a device share the array: calls
+ * that overlap on one device (other streams or host threads) race and must be
+ * serialised by the caller.  Nothing in the array needs clearing: each call
+ * writes every entry it reads. */
+HX_API int hx_inclusive_scan_i32_noalloc(const int32_t* in, int32_t* out, int n,
+                                         int64_t* total_out, cudaStream_t stream);
+
 /* Replaces map_gaussian_to_intersects_tensor (gsplat/cuda/csrc/bindings.cu:62-97;
  * kernel forward.cu:13-44).  Writes isect_ids (I,) = (tile << 32) | 0 and
  * gaussian_ids (I,) in Gaussian-major, tile-row-major order.  Writes are

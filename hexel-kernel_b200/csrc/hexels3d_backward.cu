@@ -55,40 +55,374 @@ __device__ __forceinline__ int warp_reduce_scatter(float (&v)[N], const int lane
     return start;
 }
 
+// Per-pixel state of the reverse traversal.  The surface fields are dead
+// (and eliminated) in the RGB-only instantiations.
+struct BwdPixel {
+    float px, py;
+    float v_r, v_g, v_b, v_overdraw;
+    float T_after;
+    float3 behind;
+    int n_color;
+    float v_depth, v_alpha, v_dist, v_median;
+    float3 v_normal;
+    float T_after_surf, M1, M2, final_alpha_surf, last_dist_vjp;
+    float behind_depth, behind_alpha;
+    float3 behind_normal;
+    int n_surf, median_index;
+};
+
+// Slot offsets of the per-pair gradient vector.
+struct BwdSlots {
+    int cg, cq, op, soft, tm, vd, n, ks, ls, abs, ctr;
+};
+
+// VJP of one (pixel, surfel) pair at list index idx, ADDED into acc; updates
+// the pixel's running state (transmittance and "behind" terms).  Returns
+// whether the pair blended.  Per-pair arithmetic restates
+// hexels3d_forward.cu:1983-2470.
 template <bool SURF, bool PREFILTER, int N>
-__global__ void __launch_bounds__(256) render3d_bwd_kernel(const Backward3DArgs a,
-                                                           const BwdLayout L) {
+__device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayout& L,
+                                         const BwdSlots& O, const Surfel3D& s, const int idx,
+                                         BwdPixel& q, float (&acc)[N]) {
+    const int g_id = s.id;
+    const bool is_base = g_id < a.overdraw_base;
+    const bool active_color = idx < q.n_color;
+    const bool active_surf = SURF && is_base && idx < q.n_surf;
+    if (!active_color && !active_surf) return false;
+    const float px = q.px, py = q.py;
+    const float3 Tu = {s.tu[0], s.tu[1], s.tu[2]};
+    const float3 Tv = {s.tv[0], s.tv[1], s.tv[2]};
+    const float3 Tw = {s.tw[0], s.tw[1], s.tw[2]};
+    const float3 soft3 = {s.s0, s.s1, s.s2};
+    HexHit h;
+    if (!hexel_hit(px, py, Tu, Tv, Tw, s.opacity, soft3, h)) return false;
+    float alpha = h.alpha;
+    bool use_filter = false, clamped_filter = false;
+    float G = 0.f, dxf = 0.f, dyf = 0.f;
+    if (PREFILTER) {
+        dxf = px - s.q.ctr.x;
+        dyf = py - s.q.ctr.y;
+        G = __expf(-0.5f * k3FilterInvSquare * (dxf * dxf + dyf * dyf));
+        const float arf = s.opacity * G;
+        clamped_filter = arf > 0.99f;
+        const float af = clamped_filter ? 0.99f : arf;
+        use_filter = af > h.alpha;
+        alpha = use_filter ? af : h.alpha;
+    }
+    if (alpha < 1.0f / 255.0f) return false;
+
+    const float u = h.u, v = h.v;
+    const float depth = use_filter ? Tw.z : h.depth;
+    const float inv_1ma = 1.f / (1.f - alpha);
+    float3 c = {0.f, 0.f, 0.f};
+    float v_alpha_total = 0.f, v_u = 0.f, v_v = 0.f, v_depth_direct = 0.f;
+    float T_before = 0.f;
+    const float v_out_r = q.v_r, v_out_g = q.v_g, v_out_b = q.v_b;
+    if (active_color) {
+        T_before = q.T_after * inv_1ma;
+        const float w = alpha * T_before;
+        const float ua = use_filter ? 0.f : u;
+        const float va = use_filter ? 0.f : v;
+        c = {s.cb[0], s.cb[1], s.cb[2]};
+        if (a.color_model >= kColorLinear) {
+            c.x += ua * s.gu[0] + va * s.gv[0];
+            c.y += ua * s.gu[1] + va * s.gv[1];
+            c.z += ua * s.gu[2] + va * s.gv[2];
+        }
+        const float* cq = nullptr;
+        float ub = ua, vb = va;
+        if (a.color_model == kColorQuadratic || a.color_model == kColorQuadBounded) {
+            cq = a.color_quads + 9 * g_id;
+            if (a.color_model == kColorQuadBounded) bounded_coords(ua, va, ub, vb);
+            const float u2 = ub * ub, uv = ub * vb, v2 = vb * vb;
+            c.x += u2 * cq[0] + uv * cq[3] + v2 * cq[6];
+            c.y += u2 * cq[1] + uv * cq[4] + v2 * cq[7];
+            c.z += u2 * cq[2] + uv * cq[5] + v2 * cq[8];
+        }
+        if (a.use_view_grads) {
+            c.x += s.cv[0];
+            c.y += s.cv[1];
+            c.z += s.cv[2];
+        }
+        float spec = 0.f, cos_nv = 0.f, s_exp = 0.f;
+        bool log_s_clamped = false;
+        const float* vd = a.view_dirs + 3 * g_id;
+        float3 nr = {0.f, 0.f, 0.f};
+        if (a.view_model == kViewLobe) {
+            if (a.normals)
+                nr = {a.normals[3 * g_id], a.normals[3 * g_id + 1], a.normals[3 * g_id + 2]};
+            cos_nv = fmaxf(-(nr.x * vd[0] + nr.y * vd[1] + nr.z * vd[2]), 0.f);
+            const float log_s = a.specular_log_s[g_id];
+            log_s_clamped = (log_s < 0.f) || (log_s > 5.0f);
+            s_exp = __expf(fminf(fmaxf(log_s, 0.f), 5.0f));
+            spec = (cos_nv > 0.f) ? __powf(cos_nv, s_exp) : 0.f;
+            c.x += a.specular_ks[3 * g_id] * spec;
+            c.y += a.specular_ks[3 * g_id + 1] * spec;
+            c.z += a.specular_ks[3 * g_id + 2] * spec;
+        }
+        acc[0] += w * v_out_r;
+        acc[1] += w * v_out_g;
+        acc[2] += w * v_out_b;
+        if (L.off_cg >= 0) {
+            acc[O.cg + 0] += w * v_out_r * ua;
+            acc[O.cg + 1] += w * v_out_g * ua;
+            acc[O.cg + 2] += w * v_out_b * ua;
+            acc[O.cg + 3] += w * v_out_r * va;
+            acc[O.cg + 4] += w * v_out_g * va;
+            acc[O.cg + 5] += w * v_out_b * va;
+        }
+        if (L.off_cq >= 0 && cq) {
+            const float q3[3] = {ub * ub, ub * vb, vb * vb};
+#pragma unroll
+            for (int r = 0; r < 3; ++r) {
+                acc[O.cq + 3 * r + 0] += w * v_out_r * q3[r];
+                acc[O.cq + 3 * r + 1] += w * v_out_g * q3[r];
+                acc[O.cq + 3 * r + 2] += w * v_out_b * q3[r];
+            }
+        }
+        if (a.use_view_grads && L.off_vd >= 0 && !use_filter) {
+            const float* vg = a.view_grads + 9 * g_id;
+            acc[O.vd + 0] += w * (v_out_r * vg[0] + v_out_g * vg[3] + v_out_b * vg[6]);
+            acc[O.vd + 1] += w * (v_out_r * vg[1] + v_out_g * vg[4] + v_out_b * vg[7]);
+            acc[O.vd + 2] += w * (v_out_r * vg[2] + v_out_g * vg[5] + v_out_b * vg[8]);
+        }
+        if (a.view_model == kViewLobe) {
+            if (L.off_ks >= 0) {
+                acc[O.ks + 0] += w * v_out_r * spec;
+                acc[O.ks + 1] += w * v_out_g * spec;
+                acc[O.ks + 2] += w * v_out_b * spec;
+            }
+            const float v_spec = w * (v_out_r * a.specular_ks[3 * g_id] +
+                                      v_out_g * a.specular_ks[3 * g_id + 1] +
+                                      v_out_b * a.specular_ks[3 * g_id + 2]);
+            if (L.off_ls >= 0 && !log_s_clamped && cos_nv > 0.f)
+                acc[O.ls] += v_spec * (spec * logf(cos_nv) * s_exp);
+            if (!use_filter && v_spec != 0.f && cos_nv > 0.f) {
+                const float v_cos = v_spec * (s_exp * spec / cos_nv);
+                if (L.off_vd >= 0) {
+                    acc[O.vd + 0] += -v_cos * nr.x;
+                    acc[O.vd + 1] += -v_cos * nr.y;
+                    acc[O.vd + 2] += -v_cos * nr.z;
+                }
+                if (L.off_n >= 0) {
+                    acc[O.n + 0] += -v_cos * vd[0];
+                    acc[O.n + 1] += -v_cos * vd[1];
+                    acc[O.n + 2] += -v_cos * vd[2];
+                }
+            }
+        }
+        v_alpha_total += T_before * (v_out_r * (c.x - q.behind.x) + v_out_g * (c.y - q.behind.y) +
+                                     v_out_b * (c.z - q.behind.z));
+        if (!use_filter && a.color_model >= kColorLinear) {
+            v_u += w * (v_out_r * s.gu[0] + v_out_g * s.gu[1] + v_out_b * s.gu[2]);
+            v_v += w * (v_out_r * s.gv[0] + v_out_g * s.gv[1] + v_out_b * s.gv[2]);
+        }
+        if (!use_filter && a.color_model == kColorQuadratic) {
+            const float du_r = 2.f * u * cq[0] + v * cq[3];
+            const float du_g = 2.f * u * cq[1] + v * cq[4];
+            const float du_b = 2.f * u * cq[2] + v * cq[5];
+            const float dv_r = u * cq[3] + 2.f * v * cq[6];
+            const float dv_g = u * cq[4] + 2.f * v * cq[7];
+            const float dv_b = u * cq[5] + 2.f * v * cq[8];
+            v_u += w * (v_out_r * du_r + v_out_g * du_g + v_out_b * du_b);
+            v_v += w * (v_out_r * dv_r + v_out_g * dv_g + v_out_b * dv_b);
+        } else if (!use_filter && a.color_model == kColorQuadBounded) {
+            float ubb, vbb;
+            bounded_coords(u, v, ubb, vbb);
+            const float du_r = 2.f * ubb * cq[0] + vbb * cq[3];
+            const float du_g = 2.f * ubb * cq[1] + vbb * cq[4];
+            const float du_b = 2.f * ubb * cq[2] + vbb * cq[5];
+            const float dv_r = ubb * cq[3] + 2.f * vbb * cq[6];
+            const float dv_g = ubb * cq[4] + 2.f * vbb * cq[7];
+            const float dv_b = ubb * cq[5] + 2.f * vbb * cq[8];
+            bounded_coords_vjp(u, v, w * (v_out_r * du_r + v_out_g * du_g + v_out_b * du_b),
+                               w * (v_out_r * dv_r + v_out_g * dv_g + v_out_b * dv_b), v_u, v_v);
+        }
+    }
+    float T_before_surf = 0.f;
+    float3 n_surf = {0.f, 0.f, 0.f};
+    if (SURF && active_surf) {
+        T_before_surf = q.T_after_surf * inv_1ma;
+        const float w_surf = alpha * T_before_surf;
+        if (q.v_depth != 0.f) {
+            v_alpha_total += T_before_surf * q.v_depth * (depth - q.behind_depth);
+            if (!use_filter) {
+                v_depth_direct += w_surf * q.v_depth;
+                v_u += v_depth_direct * Tw.x;
+                v_v += v_depth_direct * Tw.y;
+            }
+        }
+        if (q.v_dist != 0.f) {
+            const float m = k3FarPlane / (k3FarPlane - k3NearPlane) * (1.0f - k3NearPlane / depth);
+            const float weight_vjp =
+                (q.M2 + m * m * q.final_alpha_surf - 2.0f * m * q.M1) * q.v_dist;
+            v_alpha_total += T_before_surf * (weight_vjp - q.last_dist_vjp);
+            q.last_dist_vjp = alpha * weight_vjp + (1.0f - alpha) * q.last_dist_vjp;
+            if (!use_filter) {
+                const float m_vjp = 2.0f * w_surf * (m * q.final_alpha_surf - q.M1) * q.v_dist;
+                const float depth_vjp = m_vjp * (k3FarPlane * k3NearPlane) /
+                                        ((k3FarPlane - k3NearPlane) * depth * depth);
+                v_depth_direct += depth_vjp;
+                v_u += depth_vjp * Tw.x;
+                v_v += depth_vjp * Tw.y;
+            }
+        }
+        if (idx == q.median_index && q.v_median != 0.f) {
+            if (use_filter) {
+                acc[O.tm + 8] += q.v_median;
+            } else {
+                v_depth_direct += q.v_median;
+                v_u += q.v_median * Tw.x;
+                v_v += q.v_median * Tw.y;
+            }
+        }
+        if (q.v_alpha != 0.f)
+            v_alpha_total += T_before_surf * q.v_alpha * (1.f - q.behind_alpha);
+        if (a.grad_out_surf_normals && a.normals) {
+            n_surf = {s.n[0], s.n[1], s.n[2]};
+            v_alpha_total += T_before_surf * (q.v_normal.x * (n_surf.x - q.behind_normal.x) +
+                                              q.v_normal.y * (n_surf.y - q.behind_normal.y) +
+                                              q.v_normal.z * (n_surf.z - q.behind_normal.z));
+            if (!use_filter && L.off_n >= 0) {
+                acc[O.n + 0] += s.nsign * w_surf * q.v_normal.x;
+                acc[O.n + 1] += s.nsign * w_surf * q.v_normal.y;
+                acc[O.n + 2] += s.nsign * w_surf * q.v_normal.z;
+            }
+        }
+    }
+    // opacity
+    float v_op = 0.f;
+    if (use_filter) {
+        if (!clamped_filter) {
+            v_op += v_alpha_total * G;
+            if (PREFILTER && L.off_ctr >= 0) {
+                const float factor = v_alpha_total * s.opacity * G * k3FilterInvSquare;
+                acc[O.ctr + 0] += factor * dxf;
+                acc[O.ctr + 1] += factor * dyf;
+            }
+        }
+    } else if (!h.clamped) {
+        v_op += v_alpha_total * h.boundary;
+    }
+    const bool alpha_sdf_ok = h.alpha >= (1.0f / 255.0f);
+    const bool has_overdraw = (q.v_overdraw != 0.f) && active_color && is_base && alpha_sdf_ok;
+    if (has_overdraw) v_op += q.v_overdraw * h.boundary;
+    acc[O.op] += v_op;
+    if (L.off_soft >= 0) {
+        const float sig = h.boundary;
+        float v_soft = 0.f;
+        if (!use_filter && !h.clamped)
+            v_soft += v_alpha_total * s.opacity * (-h.dist) * sig * (1.f - sig);
+        if (has_overdraw) v_soft += q.v_overdraw * s.opacity * (-h.dist) * sig * (1.f - sig);
+        if (a.softness_stride == 3) {
+            acc[O.soft + 0] += h.edge == 0 ? v_soft : 0.f;
+            acc[O.soft + 1] += h.edge == 1 ? v_soft : 0.f;
+            acc[O.soft + 2] += h.edge == 2 ? v_soft : 0.f;
+        } else {
+            acc[O.soft] += v_soft;
+        }
+    }
+    if ((!use_filter && !h.clamped) || has_overdraw) {
+        float dist_g, ddu, ddv;
+        int edge_g;
+        hex_sdf3_grad(u, v, dist_g, ddu, ddv, edge_g);
+        const float soft_g = (edge_g == 0) ? soft3.x : ((edge_g == 1) ? soft3.y : soft3.z);
+        const float d_sig = -soft_g * h.boundary * (1.f - h.boundary);
+        float v_ad = has_overdraw ? (q.v_overdraw * s.opacity * d_sig) : 0.f;
+        if (!use_filter && !h.clamped) v_ad += v_alpha_total * s.opacity * d_sig;
+        v_u += v_ad * ddu;
+        v_v += v_ad * ddv;
+    }
+    const float3 k = {px * Tw.x - Tu.x, px * Tw.y - Tu.y, px * Tw.z - Tu.z};
+    const float3 l = {py * Tw.x - Tv.x, py * Tw.y - Tv.y, py * Tw.z - Tv.z};
+    const float3 p = cross3(k, l);
+    if (p.z != 0.f) {
+        const float inv_pz = 1.f / p.z;
+        const float dsx = v_u * inv_pz;
+        const float dsy = v_v * inv_pz;
+        const float3 v_p = {dsx, dsy, -(dsx * u + dsy * v)};
+        const float3 v_k = cross3(l, v_p);
+        const float3 v_l = cross3(v_p, k);
+        float3 v_Tw = {px * v_k.x + py * v_l.x, px * v_k.y + py * v_l.y,
+                       px * v_k.z + py * v_l.z};
+        if (SURF && active_surf && v_depth_direct != 0.f) {
+            v_Tw.x += u * v_depth_direct;
+            v_Tw.y += v * v_depth_direct;
+            v_Tw.z += v_depth_direct;
+        }
+        if (L.off_abs >= 0) {
+            const float gx = -v_k.z * Tw.z * 0.5f * (float)a.W;
+            const float gy = -v_l.z * Tw.z * 0.5f * (float)a.H;
+            acc[O.abs] += sqrtf(gx * gx + gy * gy);
+        }
+        acc[O.tm + 0] += -v_k.x;
+        acc[O.tm + 1] += -v_k.y;
+        acc[O.tm + 2] += -v_k.z;
+        acc[O.tm + 3] += -v_l.x;
+        acc[O.tm + 4] += -v_l.y;
+        acc[O.tm + 5] += -v_l.z;
+        acc[O.tm + 6] += v_Tw.x;
+        acc[O.tm + 7] += v_Tw.y;
+        acc[O.tm + 8] += v_Tw.z;
+    }
+    if (active_color) {
+        q.behind = {alpha * c.x + (1.f - alpha) * q.behind.x,
+                    alpha * c.y + (1.f - alpha) * q.behind.y,
+                    alpha * c.z + (1.f - alpha) * q.behind.z};
+        q.T_after = T_before;
+    }
+    if (SURF && active_surf) {
+        q.behind_depth = alpha * depth + (1.f - alpha) * q.behind_depth;
+        q.behind_alpha = alpha * 1.0f + (1.f - alpha) * q.behind_alpha;
+        if (a.grad_out_surf_normals && a.normals) {
+            q.behind_normal = {alpha * n_surf.x + (1.f - alpha) * q.behind_normal.x,
+                               alpha * n_surf.y + (1.f - alpha) * q.behind_normal.y,
+                               alpha * n_surf.z + (1.f - alpha) * q.behind_normal.z};
+        }
+        q.T_after_surf = T_before_surf;
+    }
+    return true;
+}
+
+// One CTA per 16x16 tile, 256 / PPT threads, PPT pixels per thread: warps
+// cover 8 x (4 PPT) pixel blocks (two across, 4 / PPT down), lane l owns
+// pixels (l % 8, l / 8 + 4 k), k < PPT.  Per list index the PPT pairs of a
+// thread are added into one gradient vector before the warp reduction.
+template <bool SURF, bool PREFILTER, int N, int PPT>
+__global__ void __launch_bounds__(k3BlockSize / PPT) render3d_bwd_kernel(const Backward3DArgs a,
+                                                                        const BwdLayout L) {
+    constexpr int kThreads = k3BlockSize / PPT;
+    constexpr int kBatch = kThreads;  // surfels staged per batch
+    constexpr int kWarpRows = 4 * PPT;
     extern __shared__ __align__(16) unsigned char s_raw[];
     Surfel3D* s_prim = reinterpret_cast<Surfel3D*>(s_raw);
-    float* s_acc = reinterpret_cast<float*>(s_raw + sizeof(Surfel3D) * k3BlockSize);
+    float* s_acc = reinterpret_cast<float*>(s_raw + sizeof(Surfel3D) * kBatch);
     __shared__ int s_max_visit;
 
-    // N == 32 uses the fixed slot layout below (compile-time indices keep
-    // the per-pixel gradient vector in registers); N == 64 takes the
-    // host-computed layout for the quadratic colour and lobe view models.
+    // N == 32 uses the fixed slot layout (compile-time indices keep the
+    // gradient vector in registers); N == 64 takes the host-computed layout
+    // of the quadratic colour and lobe view models.
     constexpr bool FIX = (N == 32);
-    const int O_cg = FIX ? kFixCg : L.off_cg;
-    const int O_cq = FIX ? 0 : L.off_cq;
-    const int O_op = FIX ? kFixOp : L.off_op;
-    const int O_soft = FIX ? kFixSoft : L.off_soft;
-    const int O_tm = FIX ? kFixTm : L.off_tm;
-    const int O_vd = FIX ? kFixVd : L.off_vd;
-    const int O_n = FIX ? kFixN : L.off_n;
-    const int O_ks = FIX ? 0 : L.off_ks;
-    const int O_ls = FIX ? 0 : L.off_ls;
-    const int O_abs = FIX ? kFixAbs : L.off_abs;
-    const int O_ctr = FIX ? kFixCtr : L.off_ctr;
+    BwdSlots O;
+    O.cg = FIX ? kFixCg : L.off_cg;
+    O.cq = FIX ? 0 : L.off_cq;
+    O.op = FIX ? kFixOp : L.off_op;
+    O.soft = FIX ? kFixSoft : L.off_soft;
+    O.tm = FIX ? kFixTm : L.off_tm;
+    O.vd = FIX ? kFixVd : L.off_vd;
+    O.n = FIX ? kFixN : L.off_n;
+    O.ks = FIX ? 0 : L.off_ks;
+    O.ls = FIX ? 0 : L.off_ls;
+    O.abs = FIX ? kFixAbs : L.off_abs;
+    O.ctr = FIX ? kFixCtr : L.off_ctr;
 
     const int W = a.W, H = a.H;
     const unsigned hblocks = (W + k3BlockX - 1) / k3BlockX;
-    const unsigned px_i = blockIdx.x * k3BlockX + threadIdx.x;
-    const unsigned py_i = blockIdx.y * k3BlockY + threadIdx.y;
-    const bool inside = px_i < (unsigned)W && py_i < (unsigned)H;
-    const unsigned pix_id = inside ? (unsigned)(W * (int)py_i + (int)px_i) : 0u;
-    const float px = (float)px_i;
-    const float py = (float)py_i;
-    const int tr = threadIdx.y * k3BlockX + threadIdx.x;
+    const int tr = threadIdx.x;
     const int lane = tr & 31;
+    const int warp = tr >> 5;
+    const int wx0 = (int)(blockIdx.x * k3BlockX) + ((warp & 1) << 3);
+    const int wy0 = (int)(blockIdx.y * k3BlockY) + (warp >> 1) * kWarpRows;
     const int HW = H * W;
 
     uint2 range = a.ranges[blockIdx.y * hblocks + blockIdx.x];
@@ -97,66 +431,79 @@ __global__ void __launch_bounds__(256) render3d_bwd_kernel(const Backward3DArgs 
     const int range_len = (int)(range.y - range.x);
     if (range_len <= 0) return;  // uniform across the CTA
 
-    float v_out_r = 0.f, v_out_g = 0.f, v_out_b = 0.f, v_overdraw = 0.f;
-    float v_surf_depth = 0.f, v_surf_alpha = 0.f, v_surf_dist = 0.f, v_surf_median = 0.f;
-    float3 v_surf_normal = {0.f, 0.f, 0.f};
-    float T_after = 1.f, T_after_surf = 1.f, M1 = 0.f, M2 = 0.f;
-    int n_color = 0, n_surf = 0, median_index = -1;
-    if (inside) {
-        v_out_r = a.grad_out_color[pix_id];
-        v_out_g = a.grad_out_color[HW + pix_id];
-        v_out_b = a.grad_out_color[2 * HW + pix_id];
-        if (a.grad_out_overdraw) v_overdraw = a.grad_out_overdraw[pix_id];
-        T_after = a.final_T[pix_id];
-        n_color = min(a.last_index[pix_id], range_len);
-        if (SURF) {
-            if (a.grad_out_surf_depth) v_surf_depth = a.grad_out_surf_depth[pix_id];
-            if (a.grad_out_surf_alpha) v_surf_alpha = a.grad_out_surf_alpha[pix_id];
-            if (a.grad_out_surf_normals) {
-                v_surf_normal = {a.grad_out_surf_normals[pix_id],
-                                 a.grad_out_surf_normals[HW + pix_id],
-                                 a.grad_out_surf_normals[2 * HW + pix_id]};
-                v_surf_dist = a.grad_out_surf_normals[3 * HW + pix_id];
-                if (a.has_median_grad) v_surf_median = a.grad_out_surf_normals[4 * HW + pix_id];
+    BwdPixel q[PPT];
+    int n_max = 0;
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+        const int pxi = wx0 + (lane & 7);
+        const int pyi = wy0 + (lane >> 3) + 4 * k;
+        const bool inside = pxi < W && pyi < H;
+        const int pix = pyi * W + pxi;
+        BwdPixel& p = q[k];
+        p.px = (float)pxi;
+        p.py = (float)pyi;
+        p.v_r = p.v_g = p.v_b = p.v_overdraw = 0.f;
+        p.T_after = 1.f;
+        p.behind = {a.bg[0], a.bg[1], a.bg[2]};
+        p.n_color = 0;
+        p.v_depth = p.v_alpha = p.v_dist = p.v_median = 0.f;
+        p.v_normal = {0.f, 0.f, 0.f};
+        p.T_after_surf = 1.f;
+        p.M1 = p.M2 = 0.f;
+        p.last_dist_vjp = 0.f;
+        p.behind_depth = p.behind_alpha = 0.f;
+        p.behind_normal = {0.f, 0.f, 0.f};
+        p.n_surf = 0;
+        p.median_index = -1;
+        if (inside) {
+            p.v_r = a.grad_out_color[pix];
+            p.v_g = a.grad_out_color[HW + pix];
+            p.v_b = a.grad_out_color[2 * HW + pix];
+            if (a.grad_out_overdraw) p.v_overdraw = a.grad_out_overdraw[pix];
+            p.T_after = a.final_T[pix];
+            p.n_color = min(a.last_index[pix], range_len);
+            if (SURF) {
+                if (a.grad_out_surf_depth) p.v_depth = a.grad_out_surf_depth[pix];
+                if (a.grad_out_surf_alpha) p.v_alpha = a.grad_out_surf_alpha[pix];
+                if (a.grad_out_surf_normals) {
+                    p.v_normal = {a.grad_out_surf_normals[pix],
+                                  a.grad_out_surf_normals[HW + pix],
+                                  a.grad_out_surf_normals[2 * HW + pix]};
+                    p.v_dist = a.grad_out_surf_normals[3 * HW + pix];
+                    if (a.has_median_grad) p.v_median = a.grad_out_surf_normals[4 * HW + pix];
+                }
+                p.T_after_surf = a.final_T_surf[pix];
+                p.n_surf = min(a.last_index_surf[pix], range_len);
+                p.M1 = a.m1_surf[pix];
+                p.M2 = a.m2_surf[pix];
+                p.median_index = a.median_index[pix];
             }
-            T_after_surf = a.final_T_surf[pix_id];
-            n_surf = min(a.last_index_surf[pix_id], range_len);
-            M1 = a.m1_surf[pix_id];
-            M2 = a.m2_surf[pix_id];
-            median_index = a.median_index[pix_id];
         }
+        p.final_alpha_surf = 1.0f - p.T_after_surf;
+        n_max = max(n_max, SURF ? max(p.n_color, p.n_surf) : p.n_color);
     }
-    const int n_max = SURF ? max(n_color, n_surf) : n_color;
     if (tr == 0) s_max_visit = 0;
     __syncthreads();
     if (n_max > 0) atomicMax(&s_max_visit, n_max);
     __syncthreads();
     const int block_max = s_max_visit;
 
-    float3 behind = {a.bg[0], a.bg[1], a.bg[2]};
-    float behind_depth = 0.f, behind_alpha = 0.f;
-    float3 behind_normal = {0.f, 0.f, 0.f};
-    float last_dist_vjp = 0.f;
-    const float final_alpha_surf = 1.0f - T_after_surf;
-    const float bg0 = behind.x;
-    (void)bg0;
-
-    const int nb = (block_max + k3BlockSize - 1) / k3BlockSize;
+    const int nb = (block_max + kBatch - 1) / kBatch;
     for (int b = nb - 1; b >= 0; --b) {
-        const int bstart = b * k3BlockSize;
-        const int bend = min(bstart + k3BlockSize, block_max);
+        const int bstart = b * kBatch;
+        const int bend = min(bstart + kBatch, block_max);
         __syncthreads();
-        if (bstart + tr < bend) {
-            int g = a.point_list[range.x + bstart + tr];
+        for (int t = tr; bstart + t < bend; t += kThreads) {
+            int g = a.point_list[range.x + bstart + t];
             g = min(max(g, 0), a.P - 1);
-            Surfel3D& s = s_prim[tr];
+            Surfel3D& s = s_prim[t];
             s.id = g;
             const float* Tm = a.transMats + 9 * g;
 #pragma unroll
-            for (int q = 0; q < 3; ++q) {
-                s.tu[q] = Tm[q];
-                s.tv[q] = Tm[3 + q];
-                s.tw[q] = Tm[6 + q];
+            for (int c = 0; c < 3; ++c) {
+                s.tu[c] = Tm[c];
+                s.tv[c] = Tm[3 + c];
+                s.tw[c] = Tm[6 + c];
             }
             s.opacity = a.opacities[g];
             if (a.softness_stride == 3) {
@@ -167,16 +514,16 @@ __global__ void __launch_bounds__(256) render3d_bwd_kernel(const Backward3DArgs 
                 s.s0 = s.s1 = s.s2 = a.softnesses[g];
             }
 #pragma unroll
-            for (int q = 0; q < 3; ++q) s.cb[q] = a.colors[3 * g + q];
+            for (int c = 0; c < 3; ++c) s.cb[c] = a.colors[3 * g + c];
             if (a.color_model >= kColorLinear) {
 #pragma unroll
-                for (int q = 0; q < 3; ++q) {
-                    s.gu[q] = a.color_grads[6 * g + q];
-                    s.gv[q] = a.color_grads[6 * g + 3 + q];
+                for (int c = 0; c < 3; ++c) {
+                    s.gu[c] = a.color_grads[6 * g + c];
+                    s.gv[c] = a.color_grads[6 * g + 3 + c];
                 }
             } else {
 #pragma unroll
-                for (int q = 0; q < 3; ++q) s.gu[q] = s.gv[q] = 0.f;
+                for (int c = 0; c < 3; ++c) s.gu[c] = s.gv[c] = 0.f;
             }
             if (a.use_view_grads) {
                 const float* vd = a.view_dirs + 3 * g;
@@ -199,343 +546,43 @@ __global__ void __launch_bounds__(256) render3d_bwd_kernel(const Backward3DArgs 
                 s.nsign = 1.f;
             }
             if (PREFILTER) {
-                const float2 c = a.points_xy_center[g];
-                s.cx = c.x;
-                s.cy = c.y;
+                s.q.ctr = a.points_xy_center[g];
+            } else {
+                s.q.box = surfel_pixel_box(s, W, H);
             }
         }
-        for (int q = tr; q < k3BlockSize * L.ncomp; q += k3BlockSize) s_acc[q] = 0.f;
+        for (int t = tr; t < kBatch * L.ncomp; t += kThreads) s_acc[t] = 0.f;
         __syncthreads();
 
         for (int idx = bend - 1; idx >= bstart; --idx) {
             const Surfel3D& s = s_prim[idx - bstart];
+            // no pixel of a warp block the surfel's box misses blends it, so
+            // nothing of the pair changes there (warp-uniform)
+            if (!PREFILTER && box_misses(s.q.box, wx0, wy0, wx0 + 7, wy0 + kWarpRows - 1))
+                continue;
             float acc[N];
 #pragma unroll
-            for (int q = 0; q < N; ++q) acc[q] = 0.f;
+            for (int c = 0; c < N; ++c) acc[c] = 0.f;
             bool contributed = false;
-            const int g_id = s.id;
-            const bool is_base = g_id < a.overdraw_base;
-            const bool active_color = idx < n_color;
-            const bool active_surf = SURF && is_base && idx < n_surf;
-            HexHit h;
-            const float3 Tu = {s.tu[0], s.tu[1], s.tu[2]};
-            const float3 Tv = {s.tv[0], s.tv[1], s.tv[2]};
-            const float3 Tw = {s.tw[0], s.tw[1], s.tw[2]};
-            const float3 soft3 = {s.s0, s.s1, s.s2};
-            if ((active_color || active_surf) &&
-                hexel_hit(px, py, Tu, Tv, Tw, s.opacity, soft3, h)) {
-                float alpha = h.alpha;
-                bool use_filter = false, clamped_filter = false;
-                float G = 0.f, dxf = 0.f, dyf = 0.f;
-                if (PREFILTER) {
-                    dxf = px - s.cx;
-                    dyf = py - s.cy;
-                    G = __expf(-0.5f * k3FilterInvSquare * (dxf * dxf + dyf * dyf));
-                    const float arf = s.opacity * G;
-                    clamped_filter = arf > 0.99f;
-                    const float af = clamped_filter ? 0.99f : arf;
-                    use_filter = af > h.alpha;
-                    alpha = use_filter ? af : h.alpha;
-                }
-                if (alpha >= 1.0f / 255.0f) {
-                    contributed = true;
-                    const float u = h.u, v = h.v;
-                    const float depth = use_filter ? Tw.z : h.depth;
-                    const float inv_1ma = 1.f / (1.f - alpha);
-                    float3 c = {0.f, 0.f, 0.f};
-                    float v_alpha_total = 0.f, v_u = 0.f, v_v = 0.f, v_depth_direct = 0.f;
-                    float T_before = 0.f, w = 0.f;
-                    if (active_color) {
-                        T_before = T_after * inv_1ma;
-                        w = alpha * T_before;
-                        const float ua = use_filter ? 0.f : u;
-                        const float va = use_filter ? 0.f : v;
-                        c = {s.cb[0], s.cb[1], s.cb[2]};
-                        if (a.color_model >= kColorLinear) {
-                            c.x += ua * s.gu[0] + va * s.gv[0];
-                            c.y += ua * s.gu[1] + va * s.gv[1];
-                            c.z += ua * s.gu[2] + va * s.gv[2];
-                        }
-                        const float* cq = nullptr;
-                        float ub = ua, vb = va;
-                        if (a.color_model == kColorQuadratic || a.color_model == kColorQuadBounded) {
-                            cq = a.color_quads + 9 * g_id;
-                            if (a.color_model == kColorQuadBounded) bounded_coords(ua, va, ub, vb);
-                            const float u2 = ub * ub, uv = ub * vb, v2 = vb * vb;
-                            c.x += u2 * cq[0] + uv * cq[3] + v2 * cq[6];
-                            c.y += u2 * cq[1] + uv * cq[4] + v2 * cq[7];
-                            c.z += u2 * cq[2] + uv * cq[5] + v2 * cq[8];
-                        }
-                        if (a.use_view_grads) {
-                            c.x += s.cv[0];
-                            c.y += s.cv[1];
-                            c.z += s.cv[2];
-                        }
-                        float spec = 0.f, cos_nv = 0.f, s_exp = 0.f;
-                        bool log_s_clamped = false;
-                        const float* vd = a.view_dirs + 3 * g_id;
-                        float3 nr = {0.f, 0.f, 0.f};
-                        if (a.view_model == kViewLobe) {
-                            if (a.normals)
-                                nr = {a.normals[3 * g_id], a.normals[3 * g_id + 1],
-                                      a.normals[3 * g_id + 2]};
-                            cos_nv = fmaxf(-(nr.x * vd[0] + nr.y * vd[1] + nr.z * vd[2]), 0.f);
-                            const float log_s = a.specular_log_s[g_id];
-                            log_s_clamped = (log_s < 0.f) || (log_s > 5.0f);
-                            s_exp = __expf(fminf(fmaxf(log_s, 0.f), 5.0f));
-                            spec = (cos_nv > 0.f) ? __powf(cos_nv, s_exp) : 0.f;
-                            c.x += a.specular_ks[3 * g_id] * spec;
-                            c.y += a.specular_ks[3 * g_id + 1] * spec;
-                            c.z += a.specular_ks[3 * g_id + 2] * spec;
-                        }
-                        acc[0] = w * v_out_r;
-                        acc[1] = w * v_out_g;
-                        acc[2] = w * v_out_b;
-                        if (L.off_cg >= 0) {
-                            acc[O_cg + 0] = w * v_out_r * ua;
-                            acc[O_cg + 1] = w * v_out_g * ua;
-                            acc[O_cg + 2] = w * v_out_b * ua;
-                            acc[O_cg + 3] = w * v_out_r * va;
-                            acc[O_cg + 4] = w * v_out_g * va;
-                            acc[O_cg + 5] = w * v_out_b * va;
-                        }
-                        if (L.off_cq >= 0 && cq) {
-                            const float u2 = ub * ub, uv = ub * vb, v2 = vb * vb;
-                            const float q3[3] = {u2, uv, v2};
 #pragma unroll
-                            for (int r = 0; r < 3; ++r) {
-                                acc[O_cq + 3 * r + 0] = w * v_out_r * q3[r];
-                                acc[O_cq + 3 * r + 1] = w * v_out_g * q3[r];
-                                acc[O_cq + 3 * r + 2] = w * v_out_b * q3[r];
-                            }
-                        }
-                        if (a.use_view_grads && L.off_vd >= 0 && !use_filter) {
-                            const float* vg = a.view_grads + 9 * g_id;
-                            acc[O_vd + 0] += w * (v_out_r * vg[0] + v_out_g * vg[3] + v_out_b * vg[6]);
-                            acc[O_vd + 1] += w * (v_out_r * vg[1] + v_out_g * vg[4] + v_out_b * vg[7]);
-                            acc[O_vd + 2] += w * (v_out_r * vg[2] + v_out_g * vg[5] + v_out_b * vg[8]);
-                        }
-                        if (a.view_model == kViewLobe) {
-                            if (L.off_ks >= 0) {
-                                acc[O_ks + 0] = w * v_out_r * spec;
-                                acc[O_ks + 1] = w * v_out_g * spec;
-                                acc[O_ks + 2] = w * v_out_b * spec;
-                            }
-                            const float v_spec = w * (v_out_r * a.specular_ks[3 * g_id] +
-                                                      v_out_g * a.specular_ks[3 * g_id + 1] +
-                                                      v_out_b * a.specular_ks[3 * g_id + 2]);
-                            if (L.off_ls >= 0 && !log_s_clamped && cos_nv > 0.f)
-                                acc[O_ls] = v_spec * (spec * logf(cos_nv) * s_exp);
-                            if (!use_filter && v_spec != 0.f && cos_nv > 0.f) {
-                                const float v_cos = v_spec * (s_exp * spec / cos_nv);
-                                if (L.off_vd >= 0) {
-                                    acc[O_vd + 0] += -v_cos * nr.x;
-                                    acc[O_vd + 1] += -v_cos * nr.y;
-                                    acc[O_vd + 2] += -v_cos * nr.z;
-                                }
-                                if (L.off_n >= 0) {
-                                    acc[O_n + 0] += -v_cos * vd[0];
-                                    acc[O_n + 1] += -v_cos * vd[1];
-                                    acc[O_n + 2] += -v_cos * vd[2];
-                                }
-                            }
-                        }
-                        v_alpha_total += T_before * (v_out_r * (c.x - behind.x) +
-                                                     v_out_g * (c.y - behind.y) +
-                                                     v_out_b * (c.z - behind.z));
-                        if (!use_filter && a.color_model >= kColorLinear) {
-                            v_u += w * (v_out_r * s.gu[0] + v_out_g * s.gu[1] + v_out_b * s.gu[2]);
-                            v_v += w * (v_out_r * s.gv[0] + v_out_g * s.gv[1] + v_out_b * s.gv[2]);
-                        }
-                        if (!use_filter && a.color_model == kColorQuadratic) {
-                            const float du_r = 2.f * u * cq[0] + v * cq[3];
-                            const float du_g = 2.f * u * cq[1] + v * cq[4];
-                            const float du_b = 2.f * u * cq[2] + v * cq[5];
-                            const float dv_r = u * cq[3] + 2.f * v * cq[6];
-                            const float dv_g = u * cq[4] + 2.f * v * cq[7];
-                            const float dv_b = u * cq[5] + 2.f * v * cq[8];
-                            v_u += w * (v_out_r * du_r + v_out_g * du_g + v_out_b * du_b);
-                            v_v += w * (v_out_r * dv_r + v_out_g * dv_g + v_out_b * dv_b);
-                        } else if (!use_filter && a.color_model == kColorQuadBounded) {
-                            float ubb, vbb;
-                            bounded_coords(u, v, ubb, vbb);
-                            const float du_r = 2.f * ubb * cq[0] + vbb * cq[3];
-                            const float du_g = 2.f * ubb * cq[1] + vbb * cq[4];
-                            const float du_b = 2.f * ubb * cq[2] + vbb * cq[5];
-                            const float dv_r = ubb * cq[3] + 2.f * vbb * cq[6];
-                            const float dv_g = ubb * cq[4] + 2.f * vbb * cq[7];
-                            const float dv_b = ubb * cq[5] + 2.f * vbb * cq[8];
-                            bounded_coords_vjp(u, v,
-                                               w * (v_out_r * du_r + v_out_g * du_g + v_out_b * du_b),
-                                               w * (v_out_r * dv_r + v_out_g * dv_g + v_out_b * dv_b),
-                                               v_u, v_v);
-                        }
-                    }
-                    float T_before_surf = 0.f, w_surf = 0.f;
-                    float3 n_surf = {0.f, 0.f, 0.f};
-                    if (SURF && active_surf) {
-                        T_before_surf = T_after_surf * inv_1ma;
-                        w_surf = alpha * T_before_surf;
-                        if (v_surf_depth != 0.f) {
-                            v_alpha_total += T_before_surf * v_surf_depth * (depth - behind_depth);
-                            if (!use_filter) {
-                                v_depth_direct += w_surf * v_surf_depth;
-                                v_u += v_depth_direct * Tw.x;
-                                v_v += v_depth_direct * Tw.y;
-                            }
-                        }
-                        if (v_surf_dist != 0.f) {
-                            const float m = k3FarPlane / (k3FarPlane - k3NearPlane) *
-                                            (1.0f - k3NearPlane / depth);
-                            const float weight_vjp =
-                                (M2 + m * m * final_alpha_surf - 2.0f * m * M1) * v_surf_dist;
-                            v_alpha_total += T_before_surf * (weight_vjp - last_dist_vjp);
-                            last_dist_vjp = alpha * weight_vjp + (1.0f - alpha) * last_dist_vjp;
-                            if (!use_filter) {
-                                const float m_vjp =
-                                    2.0f * w_surf * (m * final_alpha_surf - M1) * v_surf_dist;
-                                const float depth_vjp = m_vjp * (k3FarPlane * k3NearPlane) /
-                                                        ((k3FarPlane - k3NearPlane) * depth * depth);
-                                v_depth_direct += depth_vjp;
-                                v_u += depth_vjp * Tw.x;
-                                v_v += depth_vjp * Tw.y;
-                            }
-                        }
-                        if (idx == median_index && v_surf_median != 0.f) {
-                            if (use_filter) {
-                                acc[O_tm + 8] += v_surf_median;
-                            } else {
-                                v_depth_direct += v_surf_median;
-                                v_u += v_surf_median * Tw.x;
-                                v_v += v_surf_median * Tw.y;
-                            }
-                        }
-                        if (v_surf_alpha != 0.f)
-                            v_alpha_total += T_before_surf * v_surf_alpha * (1.f - behind_alpha);
-                        if (a.grad_out_surf_normals && a.normals) {
-                            n_surf = {s.n[0], s.n[1], s.n[2]};
-                            v_alpha_total += T_before_surf *
-                                             (v_surf_normal.x * (n_surf.x - behind_normal.x) +
-                                              v_surf_normal.y * (n_surf.y - behind_normal.y) +
-                                              v_surf_normal.z * (n_surf.z - behind_normal.z));
-                            if (!use_filter && L.off_n >= 0) {
-                                acc[O_n + 0] += s.nsign * w_surf * v_surf_normal.x;
-                                acc[O_n + 1] += s.nsign * w_surf * v_surf_normal.y;
-                                acc[O_n + 2] += s.nsign * w_surf * v_surf_normal.z;
-                            }
-                        }
-                    }
-                    // opacity
-                    float v_op = 0.f;
-                    if (use_filter) {
-                        if (!clamped_filter) {
-                            v_op += v_alpha_total * G;
-                            if (PREFILTER && L.off_ctr >= 0) {
-                                const float factor = v_alpha_total * s.opacity * G * k3FilterInvSquare;
-                                acc[O_ctr + 0] = factor * dxf;
-                                acc[O_ctr + 1] = factor * dyf;
-                            }
-                        }
-                    } else if (!h.clamped) {
-                        v_op += v_alpha_total * h.boundary;
-                    }
-                    const bool alpha_sdf_ok = h.alpha >= (1.0f / 255.0f);
-                    const bool has_overdraw =
-                        (v_overdraw != 0.f) && active_color && is_base && alpha_sdf_ok;
-                    if (has_overdraw) v_op += v_overdraw * h.boundary;
-                    acc[O_op] = v_op;
-                    if (L.off_soft >= 0) {
-                        const float sig = h.boundary;
-                        float v_soft = 0.f;
-                        if (!use_filter && !h.clamped)
-                            v_soft += v_alpha_total * s.opacity * (-h.dist) * sig * (1.f - sig);
-                        if (has_overdraw)
-                            v_soft += v_overdraw * s.opacity * (-h.dist) * sig * (1.f - sig);
-                        if (a.softness_stride == 3) {
-                            acc[O_soft + 0] = h.edge == 0 ? v_soft : 0.f;
-                            acc[O_soft + 1] = h.edge == 1 ? v_soft : 0.f;
-                            acc[O_soft + 2] = h.edge == 2 ? v_soft : 0.f;
-                        } else {
-                            acc[O_soft] = v_soft;
-                        }
-                    }
-                    if ((!use_filter && !h.clamped) || has_overdraw) {
-                        float dist_g, ddu, ddv;
-                        int edge_g;
-                        hex_sdf3_grad(u, v, dist_g, ddu, ddv, edge_g);
-                        const float soft_g = (edge_g == 0) ? soft3.x : ((edge_g == 1) ? soft3.y : soft3.z);
-                        const float d_sig = -soft_g * h.boundary * (1.f - h.boundary);
-                        float v_ad = has_overdraw ? (v_overdraw * s.opacity * d_sig) : 0.f;
-                        if (!use_filter && !h.clamped) v_ad += v_alpha_total * s.opacity * d_sig;
-                        v_u += v_ad * ddu;
-                        v_v += v_ad * ddv;
-                    }
-                    const float3 k = {px * Tw.x - Tu.x, px * Tw.y - Tu.y, px * Tw.z - Tu.z};
-                    const float3 l = {py * Tw.x - Tv.x, py * Tw.y - Tv.y, py * Tw.z - Tv.z};
-                    const float3 p = cross3(k, l);
-                    if (p.z != 0.f) {
-                        const float inv_pz = 1.f / p.z;
-                        const float dsx = v_u * inv_pz;
-                        const float dsy = v_v * inv_pz;
-                        const float3 v_p = {dsx, dsy, -(dsx * u + dsy * v)};
-                        const float3 v_k = cross3(l, v_p);
-                        const float3 v_l = cross3(v_p, k);
-                        float3 v_Tw = {px * v_k.x + py * v_l.x, px * v_k.y + py * v_l.y,
-                                       px * v_k.z + py * v_l.z};
-                        if (SURF && active_surf && v_depth_direct != 0.f) {
-                            v_Tw.x += u * v_depth_direct;
-                            v_Tw.y += v * v_depth_direct;
-                            v_Tw.z += v_depth_direct;
-                        }
-                        if (L.off_abs >= 0) {
-                            const float gx = -v_k.z * Tw.z * 0.5f * (float)W;
-                            const float gy = -v_l.z * Tw.z * 0.5f * (float)H;
-                            acc[O_abs] = sqrtf(gx * gx + gy * gy);
-                        }
-                        acc[O_tm + 0] += -v_k.x;
-                        acc[O_tm + 1] += -v_k.y;
-                        acc[O_tm + 2] += -v_k.z;
-                        acc[O_tm + 3] += -v_l.x;
-                        acc[O_tm + 4] += -v_l.y;
-                        acc[O_tm + 5] += -v_l.z;
-                        acc[O_tm + 6] += v_Tw.x;
-                        acc[O_tm + 7] += v_Tw.y;
-                        acc[O_tm + 8] += v_Tw.z;
-                    }
-                    if (active_color) {
-                        behind = {alpha * c.x + (1.f - alpha) * behind.x,
-                                  alpha * c.y + (1.f - alpha) * behind.y,
-                                  alpha * c.z + (1.f - alpha) * behind.z};
-                        T_after = T_before;
-                    }
-                    if (SURF && active_surf) {
-                        behind_depth = alpha * depth + (1.f - alpha) * behind_depth;
-                        behind_alpha = alpha * 1.0f + (1.f - alpha) * behind_alpha;
-                        if (a.grad_out_surf_normals && a.normals) {
-                            behind_normal = {alpha * n_surf.x + (1.f - alpha) * behind_normal.x,
-                                             alpha * n_surf.y + (1.f - alpha) * behind_normal.y,
-                                             alpha * n_surf.z + (1.f - alpha) * behind_normal.z};
-                        }
-                        T_after_surf = T_before_surf;
-                    }
-                }
-            }
+            for (int k = 0; k < PPT; ++k)
+                contributed |= bwd_pair<SURF, PREFILTER, N>(a, L, O, s, idx, q[k], acc);
             if (__any_sync(0xffffffffu, contributed)) {
                 const int start = warp_reduce_scatter<N>(acc, lane);
                 float* dst = s_acc + (idx - bstart) * L.ncomp;
 #pragma unroll
-                for (int q = 0; q < N / 32; ++q) {
-                    const int comp = start + q;
-                    if (comp < L.ncomp && acc[q] != 0.f) atomicAdd(dst + comp, acc[q]);
+                for (int c = 0; c < N / 32; ++c) {
+                    const int comp = start + c;
+                    if (comp < L.ncomp && acc[c] != 0.f) atomicAdd(dst + comp, acc[c]);
                 }
             }
         }
         __syncthreads();
         // Flush this batch: one global atomic per (surfel, non-zero component).
-        if (bstart + tr < bend) {
-            const Surfel3D& s = s_prim[tr];
+        for (int t = tr; bstart + t < bend; t += kThreads) {
+            const Surfel3D& s = s_prim[t];
             const int g = s.id;
-            const float* sa = s_acc + tr * L.ncomp;
+            const float* sa = s_acc + t * L.ncomp;
             auto put = [](float* p, float v) {
                 if (v != 0.f) atomicAdd(p, v);
             };
@@ -543,21 +590,21 @@ __global__ void __launch_bounds__(256) render3d_bwd_kernel(const Backward3DArgs 
             put(a.grad_colors + 3 * g + 1, sa[1]);
             put(a.grad_colors + 3 * g + 2, sa[2]);
             if (L.off_cg >= 0 && a.grad_color_grads)
-                for (int q = 0; q < 6; ++q) put(a.grad_color_grads + 6 * g + q, sa[L.off_cg + q]);
+                for (int c = 0; c < 6; ++c) put(a.grad_color_grads + 6 * g + c, sa[L.off_cg + c]);
             if (L.off_cq >= 0 && a.grad_color_quads)
-                for (int q = 0; q < 9; ++q) put(a.grad_color_quads + 9 * g + q, sa[L.off_cq + q]);
+                for (int c = 0; c < 9; ++c) put(a.grad_color_quads + 9 * g + c, sa[L.off_cq + c]);
             put(a.grad_opacities + g, sa[L.off_op]);
             if (L.off_soft >= 0) {
                 if (a.softness_stride == 3)
-                    for (int q = 0; q < 3; ++q) put(a.grad_softnesses + 3 * g + q, sa[L.off_soft + q]);
+                    for (int c = 0; c < 3; ++c) put(a.grad_softnesses + 3 * g + c, sa[L.off_soft + c]);
                 else
                     put(a.grad_softnesses + g, sa[L.off_soft]);
             }
-            for (int q = 0; q < 9; ++q) put(a.grad_transMats + 9 * g + q, sa[L.off_tm + q]);
+            for (int c = 0; c < 9; ++c) put(a.grad_transMats + 9 * g + c, sa[L.off_tm + c]);
             if (L.off_n >= 0)
-                for (int q = 0; q < 3; ++q) put(a.grad_normals + 3 * g + q, sa[L.off_n + q]);
+                for (int c = 0; c < 3; ++c) put(a.grad_normals + 3 * g + c, sa[L.off_n + c]);
             if (L.off_ks >= 0)
-                for (int q = 0; q < 3; ++q) put(a.grad_specular_ks + 3 * g + q, sa[L.off_ks + q]);
+                for (int c = 0; c < 3; ++c) put(a.grad_specular_ks + 3 * g + c, sa[L.off_ks + c]);
             if (L.off_ls >= 0) put(a.grad_specular_log_s + g, sa[L.off_ls]);
             if (L.off_abs >= 0) put(a.abs_means2d + 4 * g + 3, sa[L.off_abs]);
             if (L.off_ctr >= 0) {
@@ -566,22 +613,22 @@ __global__ void __launch_bounds__(256) render3d_bwd_kernel(const Backward3DArgs 
             }
             float vd_acc[3] = {0.f, 0.f, 0.f};
             if (L.off_vd >= 0)
-                for (int q = 0; q < 3; ++q) vd_acc[q] = sa[L.off_vd + q];
+                for (int c = 0; c < 3; ++c) vd_acc[c] = sa[L.off_vd + c];
             if (L.derive_vg || L.derive_vd) {
                 const float* vd = a.view_dirs + 3 * g;
                 const float* vg = a.view_grads + 9 * g;
                 if (L.derive_vg) {
                     for (int c = 0; c < 3; ++c)
-                        for (int q = 0; q < 3; ++q)
-                            put(a.grad_view_grads + 9 * g + 3 * c + q, sa[c] * vd[q]);
+                        for (int r = 0; r < 3; ++r)
+                            put(a.grad_view_grads + 9 * g + 3 * c + r, sa[c] * vd[r]);
                 }
                 if (L.derive_vd) {
-                    for (int q = 0; q < 3; ++q)
-                        vd_acc[q] += sa[0] * vg[q] + sa[1] * vg[3 + q] + sa[2] * vg[6 + q];
+                    for (int r = 0; r < 3; ++r)
+                        vd_acc[r] += sa[0] * vg[r] + sa[1] * vg[3 + r] + sa[2] * vg[6 + r];
                 }
             }
             if (L.off_vd >= 0 || L.derive_vd)
-                for (int q = 0; q < 3; ++q) put(a.grad_view_dirs + 3 * g + q, vd_acc[q]);
+                for (int r = 0; r < 3; ++r) put(a.grad_view_dirs + 3 * g + r, vd_acc[r]);
         }
     }
 }
@@ -735,30 +782,34 @@ using namespace hx;
 
 namespace {
 
-template <bool SURF, bool PREFILTER, int N>
+template <bool SURF, bool PREFILTER, int N, int PPT>
 int launch_bwd3d(const Backward3DArgs& a, const BwdLayout& L, cudaStream_t stream) {
-    const size_t smem = sizeof(Surfel3D) * k3BlockSize + sizeof(float) * k3BlockSize * L.ncomp;
+    constexpr int kBatch = k3BlockSize / PPT;
+    const size_t smem = sizeof(Surfel3D) * kBatch + sizeof(float) * kBatch * L.ncomp;
     static bool attr_set[64] = {};
     int dev = 0;
     HX_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        HX_CUDA_TRY(cudaFuncSetAttribute(render3d_bwd_kernel<SURF, PREFILTER, N>,
+        HX_CUDA_TRY(cudaFuncSetAttribute(render3d_bwd_kernel<SURF, PREFILTER, N, PPT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)(sizeof(Surfel3D) * k3BlockSize +
-                                               sizeof(float) * k3BlockSize * N)));
+                                         (int)(sizeof(Surfel3D) * kBatch +
+                                               sizeof(float) * kBatch * N)));
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    dim3 grid(ceil_div(a.W, k3BlockX), ceil_div(a.H, k3BlockY)), block(k3BlockX, k3BlockY);
-    render3d_bwd_kernel<SURF, PREFILTER, N><<<grid, block, smem, stream>>>(a, L);
+    dim3 grid(ceil_div(a.W, k3BlockX), ceil_div(a.H, k3BlockY));
+    render3d_bwd_kernel<SURF, PREFILTER, N, PPT><<<grid, k3BlockSize / PPT, smem, stream>>>(a, L);
     HX_LAUNCH_CHECK("render3d_bwd_kernel");
     return HX_OK;
 }
 
+// Two pixels per thread where the per-pixel state is small (no surface
+// gradients); one with surface gradients, whose state would spill.
 template <bool SURF, bool PREFILTER>
 int launch_bwd3d_n(const Backward3DArgs& a, const BwdLayout& L, bool generic,
                    cudaStream_t stream) {
-    if (!generic) return launch_bwd3d<SURF, PREFILTER, 32>(a, L, stream);
-    return launch_bwd3d<SURF, PREFILTER, 64>(a, L, stream);
+    constexpr int kPPT = SURF ? 1 : 2;
+    if (!generic) return launch_bwd3d<SURF, PREFILTER, 32, kPPT>(a, L, stream);
+    return launch_bwd3d<SURF, PREFILTER, 64, kPPT>(a, L, stream);
 }
 
 }  // namespace

@@ -116,52 +116,12 @@ __device__ __forceinline__ bool compute_aabb(const Cmat<3, 3>& T, float cutoff, 
     return true;
 }
 
-__device__ __forceinline__ float dot3v(const float (&a)[3], const float* b) {
-    return a[0] * b[0] + a[1] * b[1] + a[2] * b[2];
-}
-
-// Bounds of the projected hexagon of apothem `apothem` (in surfel units),
-// clipped at the near plane (hexels3d_forward.cu:221-258).
+// Centre and half extents of the projected hexagon of apothem `apothem` (in
+// surfel units), clipped at the near plane (hexels3d_forward.cu:221-258).
 __device__ __forceinline__ bool compute_hex_bounds(const Cmat<3, 3>& T, float apothem, int W,
                                                    int H, float2& center, int2& radius) {
-    apothem += 4e-5f * fmaxf(1.f, fabsf(apothem));
-    if (apothem <= 0.f) return false;
-    const float r = k3HexRadius * apothem;
-    const float vx[6] = {r, 0.5f * r, -0.5f * r, -r, -0.5f * r, 0.5f * r};
-    const float vy[6] = {0.f, apothem, apothem, 0.f, -apothem, -apothem};
-    float lox = FLT_MAX, loy = FLT_MAX, hix = -FLT_MAX, hiy = -FLT_MAX;
-#pragma unroll
-    for (int i = 0; i < 6; ++i) {
-        const int i2 = (i + 1) % 6;
-        const float a[3] = {vx[i], vy[i], 1.f};
-        const float b[3] = {vx[i2], vy[i2], 1.f};
-        const float za = dot3v(a, T.m[2]);
-        const float zb = dot3v(b, T.m[2]);
-        if (za >= k3NearPlane) {
-            const float qx = dot3v(a, T.m[0]) / za;
-            const float qy = dot3v(a, T.m[1]) / za;
-            lox = gmin(lox, qx);
-            loy = gmin(loy, qy);
-            hix = gmax(hix, qx);
-            hiy = gmax(hiy, qy);
-        }
-        if ((za < k3NearPlane) != (zb < k3NearPlane)) {
-            const float s = (k3NearPlane - za) / (zb - za);
-            const float e[3] = {a[0] + s * (b[0] - a[0]), a[1] + s * (b[1] - a[1]),
-                                a[2] + s * (b[2] - a[2])};
-            const float qx = dot3v(e, T.m[0]) / k3NearPlane;
-            const float qy = dot3v(e, T.m[1]) / k3NearPlane;
-            lox = gmin(lox, qx);
-            loy = gmin(loy, qy);
-            hix = gmax(hix, qx);
-            hiy = gmax(hiy, qy);
-        }
-    }
-    if (lox > W || loy > H || hix < -1.f || hiy < -1.f) return false;
-    lox = gmax(lox - 1.f, (float)-k3BlockX);
-    loy = gmax(loy - 1.f, (float)-k3BlockY);
-    hix = gmin(hix + 1.f, (float)(W + k3BlockX));
-    hiy = gmin(hiy + 1.f, (float)(H + k3BlockY));
+    float lox, loy, hix, hiy;
+    if (!hex_screen_box(T.m[0], T.m[1], T.m[2], apothem, W, H, lox, loy, hix, hiy)) return false;
     center = {(lox + hix) * 0.5f, (loy + hiy) * 0.5f};
     radius = {(int)ceilf((hix - lox) * 0.5f) + 1, (int)ceilf((hiy - loy) * 0.5f) + 1};
     return true;
@@ -235,13 +195,9 @@ __global__ void __launch_bounds__(256) preprocess3d_kernel(const Prep3DArgs a) {
         const uint2 legacy_min = rmin, legacy_max = rmax;
         if (!a.prefilter) {
             if (opacity < 1.f / 255.f) break;
-            float margin = k3Log254 / softness_min;
-            if (opacity > 1.f / 255.f) {
-                const float log_cutoff = logf((255.f * (1.f + 8.f * FLT_EPSILON)) * opacity - 1.f);
-                const float softness_max = fmaxf(softness3.x, fmaxf(softness3.y, softness3.z));
-                margin = log_cutoff / (log_cutoff < 0.f ? softness_max : softness_min);
-            }
-            if (!compute_hex_bounds(T, 1.f + margin, a.W, a.H, point_image, tile_radius)) break;
+            const float softness_max = fmaxf(softness3.x, fmaxf(softness3.y, softness3.z));
+            const float apothem = hex_alpha_apothem(opacity, softness_min, softness_max);
+            if (!compute_hex_bounds(T, apothem, a.W, a.H, point_image, tile_radius)) break;
             get_rect(point_image, tile_radius, rmin, rmax, a.grid);
             if (!corrected) {
                 rmin = {max(rmin.x, legacy_min.x), max(rmin.y, legacy_min.y)};

@@ -23,9 +23,14 @@ __global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a)
 
     const int W = a.W, H = a.H;
     const unsigned hblocks = (W + k3BlockX - 1) / k3BlockX;
-    const unsigned px_i = blockIdx.x * k3BlockX + threadIdx.x;
-    const unsigned py_i = blockIdx.y * k3BlockY + threadIdx.y;
+    const int tr = threadIdx.y * k3BlockX + threadIdx.x;
+    const int2 lp = tile_pixel(tr);
+    const unsigned px_i = blockIdx.x * k3BlockX + lp.x;
+    const unsigned py_i = blockIdx.y * k3BlockY + lp.y;
     const unsigned pix_id = (unsigned)(W * (int)py_i + (int)px_i);
+    // this warp's 8x4 pixel block
+    const int wx0 = (int)(blockIdx.x * k3BlockX) + (((tr >> 5) & 1) << 3);
+    const int wy0 = (int)(blockIdx.y * k3BlockY) + ((tr >> 6) << 2);
     const float px = (float)px_i;
     const float py = (float)py_i;
     const bool inside = px_i < (unsigned)W && py_i < (unsigned)H;
@@ -38,7 +43,6 @@ __global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a)
     range.x = min(range.x, range.y);
     const int rounds = (int)((range.y - range.x + k3BlockSize - 1) / k3BlockSize);
     int to_do = (int)(range.y - range.x);
-    const int tr = threadIdx.y * k3BlockX + threadIdx.x;
 
     int n_visited = 0;
     int n_blended = 0;
@@ -110,9 +114,9 @@ __global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a)
                 s.nsign = 1.f;
             }
             if (PREFILTER) {
-                const float2 ctr = a.points_xy_center[g];
-                s.cx = ctr.x;
-                s.cy = ctr.y;
+                s.q.ctr = a.points_xy_center[g];
+            } else {
+                s.q.box = surfel_pixel_box(s, W, H);
             }
         }
         __syncthreads();
@@ -120,6 +124,8 @@ __global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a)
         const int batch_size = min(k3BlockSize, to_do);
         for (int j = 0; !done && j < batch_size; ++j) {
             const Surfel3D& s = s_prim[j];
+            // every pixel of a warp block the surfel's box misses has alpha < 1/255
+            if (!PREFILTER && box_misses(s.q.box, wx0, wy0, wx0 + 7, wy0 + 3)) continue;
             const int g_id = s.id;
             const bool is_base = g_id < a.overdraw_base;
             if (SURF && done_color && !is_base) continue;
@@ -143,8 +149,8 @@ __global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a)
             float alpha = alpha_sdf;
             bool use_filter = false;
             if (PREFILTER) {
-                const float dx = px - s.cx;
-                const float dy = py - s.cy;
+                const float dx = px - s.q.ctr.x;
+                const float dy = py - s.q.ctr.y;
                 const float G = __expf(-0.5f * k3FilterInvSquare * (dx * dx + dy * dy));
                 const float alpha_filter = fminf(s.opacity * G, 0.99f);
                 use_filter = alpha_filter > alpha_sdf;

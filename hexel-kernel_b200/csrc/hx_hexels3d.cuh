@@ -1,6 +1,8 @@
 // Shared definitions of the 3D hexel surfel kernels.
 #pragma once
 
+#include <float.h>
+
 #include "hx_common.cuh"
 
 namespace hx {
@@ -16,6 +18,81 @@ constexpr float k3FilterSize = 0.707106f;
 constexpr float k3FilterInvSquare = 2.0f;
 constexpr float k3HexRadius = 1.15470053838f;
 constexpr float k3Log254 = 5.537334267f;
+
+// min/max with the reference's matrix-library semantics (ties and NaN pick x).
+__device__ __forceinline__ float glm_min(float x, float y) { return (y < x) ? y : x; }
+__device__ __forceinline__ float glm_max(float x, float y) { return (x < y) ? y : x; }
+
+// Apothem, in surfel units, of the hexagon outside which the SDF alpha of a
+// surfel with this opacity and softness range is below 1/255
+// (hexels3d_forward.cu:479-487): 1 + ln(255 (1 + 8 eps) o - 1) / softness,
+// with the smallest softness for a positive log and the largest for a
+// negative one.
+__device__ __forceinline__ float hex_alpha_apothem(float opacity, float softness_min,
+                                                   float softness_max) {
+    float margin = k3Log254 / softness_min;
+    if (opacity > 1.f / 255.f) {
+        const float log_cutoff = logf((255.f * (1.f + 8.f * FLT_EPSILON)) * opacity - 1.f);
+        margin = log_cutoff / (log_cutoff < 0.f ? softness_max : softness_min);
+    }
+    return 1.f + margin;
+}
+
+__device__ __forceinline__ float dot3p(const float (&a)[3], const float* b) {
+    return a[0] * b[0] + a[1] * b[1] + a[2] * b[2];
+}
+
+// Screen bounds [lo, hi] of the hexagon of the given apothem on the surfel
+// plane, clipped at the near plane, padded by one pixel and clamped to one
+// tile outside the image (hexels3d_forward.cu:221-258).  Tu, Tv, Tw are the
+// transform's pixel-x, pixel-y and depth rows.  False when the hexagon does
+// not reach the image.
+__device__ __forceinline__ bool hex_screen_box(const float* Tu, const float* Tv, const float* Tw,
+                                               float apothem, int W, int H, float& lox,
+                                               float& loy, float& hix, float& hiy) {
+    apothem += 4e-5f * fmaxf(1.f, fabsf(apothem));
+    if (apothem <= 0.f) return false;
+    const float r = k3HexRadius * apothem;
+    const float vx[6] = {r, 0.5f * r, -0.5f * r, -r, -0.5f * r, 0.5f * r};
+    const float vy[6] = {0.f, apothem, apothem, 0.f, -apothem, -apothem};
+    lox = FLT_MAX;
+    loy = FLT_MAX;
+    hix = -FLT_MAX;
+    hiy = -FLT_MAX;
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+        const int i2 = (i + 1) % 6;
+        const float a[3] = {vx[i], vy[i], 1.f};
+        const float b[3] = {vx[i2], vy[i2], 1.f};
+        const float za = dot3p(a, Tw);
+        const float zb = dot3p(b, Tw);
+        if (za >= k3NearPlane) {
+            const float qx = dot3p(a, Tu) / za;
+            const float qy = dot3p(a, Tv) / za;
+            lox = glm_min(lox, qx);
+            loy = glm_min(loy, qy);
+            hix = glm_max(hix, qx);
+            hiy = glm_max(hiy, qy);
+        }
+        if ((za < k3NearPlane) != (zb < k3NearPlane)) {
+            const float s = (k3NearPlane - za) / (zb - za);
+            const float e[3] = {a[0] + s * (b[0] - a[0]), a[1] + s * (b[1] - a[1]),
+                                a[2] + s * (b[2] - a[2])};
+            const float qx = dot3p(e, Tu) / k3NearPlane;
+            const float qy = dot3p(e, Tv) / k3NearPlane;
+            lox = glm_min(lox, qx);
+            loy = glm_min(loy, qy);
+            hix = glm_max(hix, qx);
+            hiy = glm_max(hiy, qy);
+        }
+    }
+    if (lox > W || loy > H || hix < -1.f || hiy < -1.f) return false;
+    lox = glm_max(lox - 1.f, (float)-k3BlockX);
+    loy = glm_max(loy - 1.f, (float)-k3BlockY);
+    hix = glm_min(hix + 1.f, (float)(W + k3BlockX));
+    hiy = glm_min(hiy + 1.f, (float)(H + k3BlockY));
+    return true;
+}
 
 enum ColorModel { kColorFlat = 0, kColorLinear = 1, kColorQuadratic = 2, kColorQuadBounded = 3 };
 enum ViewModel { kViewNone = 0, kViewLinear = 1, kViewLobe = 2 };

@@ -6,7 +6,8 @@
 
 namespace hx {
 
-// Per-surfel record staged in shared memory by the compositing kernels.
+// Per-surfel record staged in shared memory by the compositing kernels
+// (128 bytes).
 struct __align__(16) Surfel3D {
     float tu[3], tv[3], tw[3];
     float opacity;
@@ -15,10 +16,41 @@ struct __align__(16) Surfel3D {
     float cv[3];     // view_dir . view_grads (linear view model), else 0
     float gu[3], gv[3];
     float n[3];      // viewer-facing normal (surface outputs), else 0
+    union {
+        float2 ctr;  // prefilter centre (prefilter on)
+        short4 box;  // pixel box [x, z] x [y, w] holding every pixel with alpha >= 1/255
+    } q;
     float nsign;     // the sign applied to that normal
-    float cx, cy;    // prefilter centre
     int id;
 };
+
+// The staged surfel's pixel box: the screen bounds of the hexagon outside
+// which its alpha is below 1/255 (the bound the reference's preprocess uses
+// to pick the surfel's tiles), rounded outwards.  When the bound cannot be
+// formed the box is unbounded, so nothing is skipped.
+__device__ __forceinline__ short4 surfel_pixel_box(const Surfel3D& s, int W, int H) {
+    const float smin = fminf(s.s0, fminf(s.s1, s.s2));
+    const float smax = fmaxf(s.s0, fmaxf(s.s1, s.s2));
+    float lox, loy, hix, hiy;
+    if (!hex_screen_box(s.tu, s.tv, s.tw, hex_alpha_apothem(s.opacity, smin, smax), W, H, lox,
+                        loy, hix, hiy))
+        return make_short4(-32768, -32768, 32767, 32767);
+    return make_short4((short)floorf(lox), (short)floorf(loy), (short)ceilf(hix),
+                       (short)ceilf(hiy));
+}
+
+// Warp-uniform: does the box miss the warp's pixel block [x0, x1] x [y0, y1]?
+__device__ __forceinline__ bool box_misses(const short4 b, int x0, int y0, int x1, int y1) {
+    return b.x > x1 || b.z < x0 || b.y > y1 || b.w < y0;
+}
+
+// Pixel of thread `tr` within a 16x16 tile: each warp covers an 8x4 block
+// (two blocks across, four down), so a small surfel's footprint meets fewer
+// warps than with 16x2 rows.
+__device__ __forceinline__ int2 tile_pixel(int tr) {
+    const int warp = tr >> 5, lane = tr & 31;
+    return make_int2(((warp & 1) << 3) + (lane & 7), ((warp >> 1) << 2) + (lane >> 3));
+}
 
 __device__ __forceinline__ float3 cross3(const float3 a, const float3 b) {
     return make_float3(a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x);

@@ -352,7 +352,9 @@ def test_surface_outputs_and_grads_match_oracle(median, pre):
                  upstream=up)
     HW = W * H
     assert_close_oracle(f["out_color"].cpu().reshape(3, HW), r["color"], "color")
-    assert_close_oracle(f["surf_depth"].cpu().reshape(HW), r["depth"], "depth", rtol=1e-5)
+    # depth = w (u Tw.x + v Tw.y + Tw.z) carries the ill-conditioning of (u, v) at
+    # depths ~3: relative tolerance
+    assert_close_oracle(f["surf_depth"].cpu().reshape(HW), r["depth"], "depth", rtol=2e-4)
     assert_close_oracle(f["surf_alpha"].cpu().reshape(HW), r["alpha"], "alpha")
     maps = f["surf_maps"].cpu().reshape(nch, HW)
     assert_close_oracle(maps[:3], r["normal"], "normal")

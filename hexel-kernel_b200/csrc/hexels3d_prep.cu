@@ -444,3 +444,201 @@ extern "C" int hx_hexels3d_bin(int P, int num_rendered, int image_width, int ima
     HX_LAUNCH_CHECK("ranges3d_kernel");
     return HX_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Depth-ordered binning.  Sorting the surfels once by depth (32-bit keys,
+// stable) and emitting their tiles in that order leaves only the tile index
+// to sort per intersection: bits [0, bits(tiles)) instead of
+// [0, 32 + bits(tiles)).  Within a tile the entries end up ordered by depth
+// bits, then surfel index -- the order of the stable sort of
+// (tile << 32 | depth bits) over surfel-major emission.
+// ---------------------------------------------------------------------------
+namespace hx {
+
+__global__ void __launch_bounds__(256) iota_kernel(int n, int* __restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = i;
+}
+
+__global__ void __launch_bounds__(256) gather_counts_kernel(int n, const int* __restrict__ order,
+                                                            const int* __restrict__ counts,
+                                                            int* __restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = counts[min(max(order[i], 0), n - 1)];
+}
+
+// Tile keys and surfel ids for every tile of each surfel's rectangle, surfels
+// in depth order; a warp writes 32 surfels' rectangles cooperatively.
+__global__ void __launch_bounds__(256) emit3d_ordered_kernel(
+    int P, int num_rendered, const int* __restrict__ order, const float2* __restrict__ points_xy,
+    const int* __restrict__ offsets, const int* __restrict__ radii,
+    const int2* __restrict__ tile_radii, uint2 grid, unsigned* __restrict__ keys,
+    int* __restrict__ vals) {
+    const int lane = threadIdx.x & 31;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    bool valid = false;
+    uint2 rmin = {0, 0}, rmax = {0, 0};
+    int off = 0, sid = 0;
+    if (i < P) {
+        sid = min(max(order[i], 0), P - 1);
+        const int2 tr = tile_radii[sid];
+        if (radii[sid] > 0 && tr.x > 0 && tr.y > 0) {
+            get_rect(points_xy[sid], tr, rmin, rmax, grid);
+            valid = rmax.x > rmin.x && rmax.y > rmin.y;
+            off = i == 0 ? 0 : offsets[i - 1];
+        }
+    }
+    unsigned todo = __ballot_sync(0xffffffffu, valid);
+    while (todo) {
+        const int j = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const unsigned x0 = __shfl_sync(0xffffffffu, rmin.x, j);
+        const unsigned y0 = __shfl_sync(0xffffffffu, rmin.y, j);
+        const unsigned x1 = __shfl_sync(0xffffffffu, rmax.x, j);
+        const unsigned y1 = __shfl_sync(0xffffffffu, rmax.y, j);
+        const int base = __shfl_sync(0xffffffffu, off, j);
+        const int id = __shfl_sync(0xffffffffu, sid, j);
+        const int w = (int)(x1 - x0);
+        const int area = w * (int)(y1 - y0);
+        for (int e = lane; e < area; e += 32) {
+            const int pos = base + e;
+            if (pos < 0 || pos >= num_rendered) continue;
+            const unsigned ty = y0 + (unsigned)(e / w);
+            const unsigned tx = x0 + (unsigned)(e % w);
+            keys[pos] = ty * grid.x + tx;
+            vals[pos] = id;
+        }
+    }
+}
+
+// ranges[t] = [first, last + 1) of tile t in the sorted tile keys; ranges
+// must be zeroed beforehand.
+__global__ void __launch_bounds__(256) ranges3d_u32_kernel(int L, int num_tiles,
+                                                           const unsigned* __restrict__ keys,
+                                                           uint2* __restrict__ ranges) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= L) return;
+    const unsigned cur = keys[idx];
+    if (cur >= (unsigned)num_tiles) return;
+    if (idx == 0) {
+        ranges[cur].x = 0;
+    } else {
+        const unsigned prev = keys[idx - 1];
+        if (cur != prev) {
+            if (prev < (unsigned)num_tiles) ranges[prev].y = (unsigned)idx;
+            ranges[cur].x = (unsigned)idx;
+        }
+    }
+    if (idx == L - 1) ranges[cur].y = (unsigned)L;
+}
+
+// The reference's 64-bit keys of the sorted list, (tile << 32) | depth bits.
+__global__ void __launch_bounds__(256) full_keys_kernel(int L, int P,
+                                                        const unsigned* __restrict__ tiles,
+                                                        const int* __restrict__ ids,
+                                                        const float* __restrict__ depths,
+                                                        unsigned long long* __restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= L) return;
+    const int id = min(max(ids[i], 0), P - 1);
+    out[i] = ((unsigned long long)tiles[i] << 32) | __float_as_uint(depths[id]);
+}
+
+}  // namespace hx
+
+extern "C" size_t hx_hexels3d_depth_order_workspace_bytes(int P) {
+    const size_t n = P > 0 ? (size_t)P : 1;
+    return align256(sizeof(unsigned) * n) + align256(sizeof(int) * n) +
+           align256(sizeof(int) * n) + hx_scan_workspace_bytes((int)n) +
+           sort_workspace_bytes<uint32_t>((int)n);
+}
+
+extern "C" int hx_hexels3d_depth_order(int P, const float* depths, const int32_t* tiles_touched,
+                                       int32_t* order, int32_t* offsets, int64_t* total_out,
+                                       void* workspace, size_t workspace_bytes,
+                                       cudaStream_t stream) {
+    HX_REQUIRE(P >= 0, "hexels3d_depth_order: bad P");
+    if (P == 0) {
+        if (total_out) HX_CUDA_TRY(cudaMemsetAsync(total_out, 0, sizeof(int64_t), stream));
+        return HX_OK;
+    }
+    HX_REQUIRE(depths && tiles_touched && order && offsets, "hexels3d_depth_order: null pointer");
+    const size_t need = hx_hexels3d_depth_order_workspace_bytes(P);
+    if (!workspace || workspace_bytes < need)
+        return set_error(HX_ERR_WORKSPACE, "hexels3d_depth_order: workspace of %zu bytes needed",
+                         need);
+    char* p = (char*)workspace;
+    unsigned* keys_sorted = (unsigned*)p;
+    p += align256(sizeof(unsigned) * (size_t)P);
+    int* ids = (int*)p;
+    p += align256(sizeof(int) * (size_t)P);
+    int* counts = (int*)p;
+    p += align256(sizeof(int) * (size_t)P);
+    void* scan_ws = p;
+    const size_t scan_bytes = hx_scan_workspace_bytes(P);
+    p += scan_bytes;
+    iota_kernel<<<ceil_div(P, 256), 256, 0, stream>>>(P, ids);
+    HX_LAUNCH_CHECK("iota_kernel");
+    // depths are >= the near plane (> 0) for every surfel that touches a
+    // tile, so their bit patterns order like the values
+    int rc = sort_pairs<uint32_t>((const uint32_t*)depths, ids, keys_sorted, order, P, 0, 32, p,
+                                  sort_workspace_bytes<uint32_t>(P), stream);
+    if (rc != HX_OK) return rc;
+    gather_counts_kernel<<<ceil_div(P, 256), 256, 0, stream>>>(P, order, tiles_touched, counts);
+    HX_LAUNCH_CHECK("gather_counts_kernel");
+    return hx_inclusive_scan_i32(counts, offsets, P, total_out, scan_ws, scan_bytes, stream);
+}
+
+extern "C" size_t hx_hexels3d_bin_ordered_workspace_bytes(int num_rendered) {
+    const size_t n = num_rendered > 0 ? (size_t)num_rendered : 1;
+    return align256(sizeof(unsigned) * n) * 2 + align256(sizeof(int) * n) +
+           sort_workspace_bytes<uint32_t>((int)n);
+}
+
+extern "C" int hx_hexels3d_bin_ordered(int P, int num_rendered, int image_width,
+                                       int image_height, const float* points_xy_image,
+                                       const int32_t* order, const int32_t* offsets,
+                                       const int32_t* radii, const int32_t* tile_radii,
+                                       const float* depths, int64_t* keys_sorted,
+                                       int32_t* point_list, int32_t* ranges, void* workspace,
+                                       size_t workspace_bytes, cudaStream_t stream) {
+    HX_REQUIRE(P >= 0 && num_rendered >= 0, "hexels3d_bin_ordered: bad sizes");
+    HX_REQUIRE(image_width > 0 && image_height > 0, "invalid image dimensions");
+    const uint2 grid = {(unsigned)ceil_div(image_width, k3BlockX),
+                        (unsigned)ceil_div(image_height, k3BlockY)};
+    const int num_tiles = (int)(grid.x * grid.y);
+    HX_REQUIRE(ranges, "hexels3d_bin_ordered: null ranges");
+    HX_CUDA_TRY(cudaMemsetAsync(ranges, 0, sizeof(uint2) * (size_t)num_tiles, stream));
+    if (P == 0 || num_rendered == 0) return HX_OK;
+    HX_REQUIRE(points_xy_image && order && offsets && radii && tile_radii && point_list,
+               "hexels3d_bin_ordered: null pointer");
+    HX_REQUIRE(!keys_sorted || depths, "hexels3d_bin_ordered: keys_sorted needs depths");
+    const size_t need = hx_hexels3d_bin_ordered_workspace_bytes(num_rendered);
+    if (!workspace || workspace_bytes < need)
+        return set_error(HX_ERR_WORKSPACE, "hexels3d_bin_ordered: workspace of %zu bytes needed",
+                         need);
+    char* p = (char*)workspace;
+    unsigned* keys = (unsigned*)p;
+    p += align256(sizeof(unsigned) * (size_t)num_rendered);
+    unsigned* keys_out = (unsigned*)p;
+    p += align256(sizeof(unsigned) * (size_t)num_rendered);
+    int* vals = (int*)p;
+    p += align256(sizeof(int) * (size_t)num_rendered);
+    emit3d_ordered_kernel<<<ceil_div(P, 256), 256, 0, stream>>>(
+        P, num_rendered, order, (const float2*)points_xy_image, offsets, radii,
+        (const int2*)tile_radii, grid, keys, vals);
+    HX_LAUNCH_CHECK("emit3d_ordered_kernel");
+    int rc = sort_pairs<uint32_t>(keys, vals, keys_out, point_list, num_rendered, 0,
+                                  tile_bits(num_tiles), p,
+                                  sort_workspace_bytes<uint32_t>(num_rendered), stream);
+    if (rc != HX_OK) return rc;
+    ranges3d_u32_kernel<<<ceil_div(num_rendered, 256), 256, 0, stream>>>(
+        num_rendered, num_tiles, keys_out, (uint2*)ranges);
+    HX_LAUNCH_CHECK("ranges3d_u32_kernel");
+    if (keys_sorted) {
+        full_keys_kernel<<<ceil_div(num_rendered, 256), 256, 0, stream>>>(
+            num_rendered, P, keys_out, point_list, depths, (unsigned long long*)keys_sorted);
+        HX_LAUNCH_CHECK("full_keys_kernel");
+    }
+    return HX_OK;
+}

@@ -156,21 +156,23 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                  ptr(depths), ptr(transMats), ptr(tiles_touched), ptr(opacities_out),
                  ptr(softnesses_out), ptr(view_dirs), ptr(normals) if need_normals else None, s)
         _mark("preprocess")
+        # surfels in depth order, intersection offsets in that order and their
+        # total (the one 8-byte read-back of the step, as in the reference)
+        order = torch.empty((P,), **i32)
         offsets = torch.empty((P,), **i32)
         total = torch.zeros((1,), dtype=torch.int64, device=dev)
-        ws = workspace(lib.query("hx_scan_workspace_bytes", P), dev)
-        lib.call("hx_inclusive_scan_i32", ptr(tiles_touched), ptr(offsets), P, ptr(total),
-                 ptr(ws), ws.numel(), s)
+        ws = workspace(lib.query("hx_hexels3d_depth_order_workspace_bytes", P), dev)
+        lib.call("hx_hexels3d_depth_order", P, ptr(depths), ptr(tiles_touched), ptr(order),
+                 ptr(offsets), ptr(total), ptr(ws), ws.numel(), s)
         _mark("scan")
         num_rendered = int(total.item()) if P > 0 else 0
         _check(num_rendered <= 2**31 - 1, "number of rendered intersections overflows int32")
         tx, ty = (W + 15) // 16, (H + 15) // 16
         ranges = torch.empty((tx * ty, 2), **i32)
         values_sorted = torch.empty((num_rendered,), **i32)
-        keys_sorted = torch.empty((num_rendered,), dtype=torch.int64, device=dev)
-        ws = workspace(lib.query("hx_hexels3d_bin_workspace_bytes", num_rendered), dev)
-        lib.call("hx_hexels3d_bin", P, num_rendered, W, H, ptr(points_xy_image), ptr(depths),
-                 ptr(offsets), ptr(radii), ptr(tile_radii), ptr(keys_sorted),
+        ws = workspace(lib.query("hx_hexels3d_bin_ordered_workspace_bytes", num_rendered), dev)
+        lib.call("hx_hexels3d_bin_ordered", P, num_rendered, W, H, ptr(points_xy_image),
+                 ptr(order), ptr(offsets), ptr(radii), ptr(tile_radii), None, None,
                  ptr(values_sorted), ptr(ranges), ptr(ws), ws.numel(), s)
 
         _mark("bin")

@@ -273,6 +273,30 @@ HX_API int hx_hexels3d_preprocess(
     int32_t* tiles_touched, float* opacities_out, float* softnesses_out, float* view_dirs,
     float* normals, cudaStream_t stream);
 
+/* Depth-ordered binning, the same sorted lists as hx_hexels3d_bin with far
+ * less sorting; together the two calls replace the scan, duplicate_with_keys,
+ * cub::DeviceRadixSort::SortPairs and identify_tile_ranges
+ * (hexels3d_forward.cu:553-604, 2972-3043).
+ * hx_hexels3d_depth_order: order (P,) = surfel ids stably sorted by depth
+ * bits; offsets (P,) = inclusive scan of tiles_touched taken in that order;
+ * total_out (device int64) = num_rendered.
+ * hx_hexels3d_bin_ordered: emits each surfel's tiles in that order, stably
+ * sorts the tile indices and writes point_list (I,) and ranges (tiles,2)
+ * (zeros for empty tiles); keys_sorted (I,) int64 (tile << 32 | depth bits)
+ * is optional (NULL to skip; needs depths).  Within a tile the order is
+ * depth bits then surfel id -- the reference's stable (tile, depth) order. */
+HX_API size_t hx_hexels3d_depth_order_workspace_bytes(int P);
+HX_API int hx_hexels3d_depth_order(int P, const float* depths, const int32_t* tiles_touched,
+                                   int32_t* order, int32_t* offsets, int64_t* total_out,
+                                   void* workspace, size_t workspace_bytes, cudaStream_t stream);
+HX_API size_t hx_hexels3d_bin_ordered_workspace_bytes(int num_rendered);
+HX_API int hx_hexels3d_bin_ordered(int P, int num_rendered, int image_width, int image_height,
+                                   const float* points_xy_image, const int32_t* order,
+                                   const int32_t* offsets, const int32_t* radii,
+                                   const int32_t* tile_radii, const float* depths,
+                                   int64_t* keys_sorted, int32_t* point_list, int32_t* ranges,
+                                   void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* Intersection emission, stable sort and tile ranges; replaces
  * duplicate_with_keys + cub::DeviceRadixSort::SortPairs + identify_tile_ranges
  * (hexels3d_forward.cu:553-604, 2990-3043).  offsets = inclusive scan of

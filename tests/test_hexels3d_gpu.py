@@ -243,6 +243,50 @@ def test_full_scene_properties():
     lens = ranges[:, 1] - ranges[:, 0]
     assert int(lens.sum()) == a[2][8].numel()
     assert torch.isfinite(a[0]).all()
+    _check_ordered_binning_matches_full_keys(w, cam, a[2])
+
+
+def _check_ordered_binning_matches_full_keys(w, cam, saved):
+    """The depth-ordered binning (sort surfels by depth, then only tile bits)
+    against the direct stable sort of the reference's (tile << 32 | depth)
+    keys: identical point lists and ranges, sorted keys non-decreasing."""
+    from gsplat._lib import lib, ptr, stream, workspace
+
+    P, W, H = w.num_points, cam.width, cam.height
+    dev = w.means3d.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    radii = torch.empty((P,), **i32)
+    tile_radii = torch.empty((P, 2), **i32)
+    xy = torch.empty((P, 2), **f32)
+    depths = torch.empty((P,), **f32)
+    tm = torch.empty((P, 9), **f32)
+    touched = torch.empty((P,), **i32)
+    op_out = torch.empty((P,), **f32)
+    soft_out = torch.empty((P,), **f32)
+    vd = torch.empty((P, 3), **f32)
+    s = stream(dev)
+    lib.call("hx_hexels3d_preprocess", P, ptr(w.means3d), ptr(w.scales), 1.0, ptr(w.rotations),
+             ptr(w.opacities), None, w.softness, 1, ptr(cam.viewmatrix), ptr(cam.projmatrix),
+             ptr(cam.campos), W, H, 0, 0, ptr(radii), ptr(tile_radii), ptr(xy), None,
+             ptr(depths), ptr(tm), ptr(touched), ptr(op_out), ptr(soft_out), ptr(vd), None, s)
+    offsets = torch.empty((P,), **i32)
+    total = torch.zeros((1,), dtype=torch.int64, device=dev)
+    ws = workspace(lib.query("hx_scan_workspace_bytes", P), dev)
+    lib.call("hx_inclusive_scan_i32", ptr(touched), ptr(offsets), P, ptr(total), ptr(ws),
+             ws.numel(), s)
+    n = int(total.item())
+    tiles = ((W + 15) // 16) * ((H + 15) // 16)
+    ranges = torch.empty((tiles, 2), **i32)
+    plist = torch.empty((n,), **i32)
+    keys = torch.empty((n,), dtype=torch.int64, device=dev)
+    ws = workspace(lib.query("hx_hexels3d_bin_workspace_bytes", n), dev)
+    lib.call("hx_hexels3d_bin", P, n, W, H, ptr(xy), ptr(depths), ptr(offsets), ptr(radii),
+             ptr(tile_radii), ptr(keys), ptr(plist), ptr(ranges), ptr(ws), ws.numel(), s)
+    assert n == saved[8].numel()
+    assert torch.equal(plist, saved[8]) and torch.equal(ranges, saved[7])
+    k = keys.cpu()
+    assert bool((k[1:] >= k[:-1]).all())
 
 
 # ---------------------------------------------------------------------------

@@ -460,7 +460,16 @@ class Hexels3DStep:
         self.empty = torch.empty(0, device=dev)
         self.zero_hw = torch.zeros((self.H, self.W), device=dev)
         self.numel = 3 * self.H * self.W
-        self.acc = [torch.zeros_like(p) for p in self.params]
+        # per-step gradient sums: one flat buffer (zeroed once per step,
+        # all-reduced in place), 16-byte aligned views per parameter, the
+        # loss in the last slot
+        sizes = [(p.numel() + 3) // 4 * 4 for p in self.params]
+        self.flat = torch.zeros(sum(sizes) + 4, device=dev)
+        self.acc, o = [], 0
+        for p, n in zip(self.params, sizes):
+            self.acc.append(self.flat[o:o + p.numel()].view(p.shape))
+            o += n
+        self.loss_slot = self.flat[o:o + 1]
         self.marks: list = []
         self.stage_ms = {k: 0.0 for k in self.STAGES}
         self.info: dict = {}
@@ -491,12 +500,15 @@ class Hexels3DStep:
             ga = self.zero_hw
             gn = torch.cat([normals * (2 * LAMBDA_NORMAL2 / (3 * hw)), self.zero_hw[None]])
         self._mark("loss")
+        names = ("means3d", "scales", "rotations", "colors", "color_grads", "view_grads",
+                 "opacities")
         grads = C._backward_core(m3, e, sc, rot, col, cg, e, vg, e, e, op, e, cam.viewmatrix,
                                  cam.projmatrix, cam.campos, self.bg, g_color, e, gd, ga, gn,
                                  self.W, self.H, cam.tan_fovx, cam.tan_fovy, self.w.softness,
                                  1.0, 1, 1, True, -1, False, False, False, o["saved"],
                                  surf_state=o["surf_state"],
-                                 surf_normals=o["normals"] if self.surface else None)
+                                 surf_normals=o["normals"] if self.surface else None,
+                                 accumulate_into=dict(zip(names, self.acc)))
         if keep_info:
             saved = o["saved"]
             self.info.setdefault("num_rendered", []).append(o["num_rendered"])
@@ -513,23 +525,17 @@ class Hexels3DStep:
         self.C.stage_hook = self._mark
         try:
             self._mark("start")
-            total = torch.zeros((), device=self.dev)
-            for a in self.acc:
-                a.zero_()
+            self.flat.zero_()
             for cam, tgt in zip(self.cams, self.targets):
-                loss, g = self._view(cam, tgt, keep_info)
-                # grads: means3d, means2d, scales, rotations, colors, color_grads,
-                # color_quads, view_grads, specular_ks, specular_log_s, opacities, softnesses
-                for a, gi in zip(self.acc, (g[0], g[2], g[3], g[4], g[5], g[7], g[10])):
-                    a.add_(gi)
-                total = total + loss
+                # the backward adds this view's gradients into self.acc
+                loss, _ = self._view(cam, tgt, keep_info)
+                self.loss_slot.add_(loss)
                 self._mark("accumulate")
             if self.world > 1:
                 import torch.distributed as dist
 
-                packed = torch.cat([a.view(-1) for a in self.acc] + [total.view(1)])
-                dist.all_reduce(packed)
-                total = packed[-1]
+                dist.all_reduce(self.flat)
+            total = self.loss_slot
             self._mark("allreduce")
         finally:
             self.C.stage_hook = None

@@ -693,7 +693,7 @@ __global__ void __launch_bounds__(256) geometry3d_bwd_kernel(
     const float* __restrict__ campos, int W, int H, const int* __restrict__ radii,
     const float* __restrict__ grad_T, const float* __restrict__ grad_view_dirs,
     const float* __restrict__ grad_normals, float* __restrict__ grad_means3d,
-    float2* __restrict__ grad_scales, float4* __restrict__ grad_rotations) {
+    float2* __restrict__ grad_scales, float4* __restrict__ grad_rotations, bool accumulate) {
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= P) return;
     if (radii[idx] <= 0) return;
@@ -716,9 +716,15 @@ __global__ void __launch_bounds__(256) geometry3d_bwd_kernel(
     v_mean.x += v_d.x;
     v_mean.y += v_d.y;
     v_mean.z += v_d.z;
-    grad_means3d[3 * idx] = v_mean.x;
-    grad_means3d[3 * idx + 1] = v_mean.y;
-    grad_means3d[3 * idx + 2] = v_mean.z;
+    if (accumulate) {
+        grad_means3d[3 * idx] += v_mean.x;
+        grad_means3d[3 * idx + 1] += v_mean.y;
+        grad_means3d[3 * idx + 2] += v_mean.z;
+    } else {
+        grad_means3d[3 * idx] = v_mean.x;
+        grad_means3d[3 * idx + 1] = v_mean.y;
+        grad_means3d[3 * idx + 2] = v_mean.z;
+    }
     float3 vR2 = {0.f, 0.f, 0.f};
     if (grad_normals) {
         vR2.x += grad_normals[3 * idx];
@@ -735,23 +741,41 @@ __global__ void __launch_bounds__(256) geometry3d_bwd_kernel(
     vR.m[2][0] = vR2.x;
     vR.m[2][1] = vR2.y;
     vR.m[2][2] = vR2.z;
-    grad_rotations[idx] = quat_vjp(q, vR);
-    grad_scales[idx] = {(vM.m[0][0] * R.m[0][0] + vM.m[0][1] * R.m[0][1] + vM.m[0][2] * R.m[0][2]) * mod,
-                        (vM.m[1][0] * R.m[1][0] + vM.m[1][1] * R.m[1][1] + vM.m[1][2] * R.m[1][2]) * mod};
+    const float4 v_rot = quat_vjp(q, vR);
+    const float2 v_scale = {
+        (vM.m[0][0] * R.m[0][0] + vM.m[0][1] * R.m[0][1] + vM.m[0][2] * R.m[0][2]) * mod,
+        (vM.m[1][0] * R.m[1][0] + vM.m[1][1] * R.m[1][1] + vM.m[1][2] * R.m[1][2]) * mod};
+    if (accumulate) {
+        const float4 r0 = grad_rotations[idx];
+        const float2 s0 = grad_scales[idx];
+        grad_rotations[idx] = {r0.x + v_rot.x, r0.y + v_rot.y, r0.z + v_rot.z, r0.w + v_rot.w};
+        grad_scales[idx] = {s0.x + v_scale.x, s0.y + v_scale.y};
+    } else {
+        grad_rotations[idx] = v_rot;
+        grad_scales[idx] = v_scale;
+    }
 }
 
 __global__ void __launch_bounds__(256) means2d3d_bwd_kernel(int P, int W, int H, int stride,
                                                             const int* __restrict__ radii,
                                                             const float* __restrict__ transMats,
                                                             const float* __restrict__ grad_T,
-                                                            float* __restrict__ grad_means2d) {
+                                                            float* __restrict__ grad_means2d,
+                                                            bool accumulate) {
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= P) return;
     if (radii[idx] <= 0) return;
     const float depth = transMats[9 * idx + 8];
-    grad_means2d[idx * stride + 0] = grad_T[9 * idx + 2] * depth * 0.5f * (float)W;
-    grad_means2d[idx * stride + 1] = grad_T[9 * idx + 5] * depth * 0.5f * (float)H;
-    grad_means2d[idx * stride + 2] = 0.f;
+    const float gx = grad_T[9 * idx + 2] * depth * 0.5f * (float)W;
+    const float gy = grad_T[9 * idx + 5] * depth * 0.5f * (float)H;
+    if (accumulate) {
+        grad_means2d[idx * stride + 0] += gx;
+        grad_means2d[idx * stride + 1] += gy;
+    } else {
+        grad_means2d[idx * stride + 0] = gx;
+        grad_means2d[idx * stride + 1] = gy;
+        grad_means2d[idx * stride + 2] = 0.f;
+    }
 }
 
 __global__ void __launch_bounds__(256) center3d_bwd_kernel(int P, const float* __restrict__ means3d,
@@ -802,8 +826,9 @@ int launch_bwd3d(const Backward3DArgs& a, const BwdLayout& L, cudaStream_t strea
     return HX_OK;
 }
 
-// Two pixels per thread where the per-pixel state is small (no surface
-// gradients); one with surface gradients, whose state would spill.
+// Two pixels per thread on the RGB path; one with surface gradients, whose
+// larger per-pixel state costs more in occupancy (167 registers at two
+// pixels) than the shared per-surfel work saves.
 template <bool SURF, bool PREFILTER>
 int launch_bwd3d_n(const Backward3DArgs& a, const BwdLayout& L, bool generic,
                    cudaStream_t stream) {
@@ -957,7 +982,7 @@ extern "C" int hx_hexels3d_geometry_backward(
     int image_height, const int32_t* radii, const float* transMats, const float* grad_transMats,
     const float* grad_view_dirs, const float* grad_normals, const float* grad_points_xy_center,
     float* grad_means3d, float* grad_means2d, int means2d_stride, float* grad_scales,
-    float* grad_rotations, cudaStream_t stream) {
+    float* grad_rotations, int accumulate, cudaStream_t stream) {
     HX_REQUIRE(P >= 0, "hexels3d_geometry_backward: bad P");
     if (P == 0 || num_rendered == 0) return HX_OK;
     HX_REQUIRE(means3d && scales && rotations && projmatrix && campos && radii &&
@@ -970,13 +995,14 @@ extern "C" int hx_hexels3d_geometry_backward(
                    "means2d stride must be 3 or 4");
         means2d3d_bwd_kernel<<<blocks, 256, 0, stream>>>(P, image_width, image_height,
                                                          means2d_stride, radii, transMats,
-                                                         grad_transMats, grad_means2d);
+                                                         grad_transMats, grad_means2d,
+                                                         accumulate != 0);
         HX_LAUNCH_CHECK("means2d3d_bwd_kernel");
     }
     geometry3d_bwd_kernel<<<blocks, 256, 0, stream>>>(
         P, means3d, (const float2*)scales, scale_modifier, (const float4*)rotations, projmatrix,
         campos, image_width, image_height, radii, grad_transMats, grad_view_dirs, grad_normals,
-        grad_means3d, (float2*)grad_scales, (float4*)grad_rotations);
+        grad_means3d, (float2*)grad_scales, (float4*)grad_rotations, accumulate != 0);
     HX_LAUNCH_CHECK("geometry3d_bwd_kernel");
     if (grad_points_xy_center) {
         center3d_bwd_kernel<<<blocks, 256, 0, stream>>>(P, means3d, projmatrix, image_width,

@@ -29,7 +29,6 @@ __device__ __forceinline__ float3 transform_point_4x3(const float3 p, const floa
             m[2] * p.x + m[6] * p.y + m[10] * p.z + m[14]};
 }
 
-__device__ __forceinline__ float gmin(float x, float y) { return (y < x) ? y : x; }
 __device__ __forceinline__ float gmax(float x, float y) { return (x < y) ? y : x; }
 
 // Tile rectangle [min, max) of a box centred at p with half extents r, in
@@ -468,45 +467,64 @@ __global__ void __launch_bounds__(256) gather_counts_kernel(int n, const int* __
 }
 
 // Tile keys and surfel ids for every tile of each surfel's rectangle, surfels
-// in depth order; a warp writes 32 surfels' rectangles cooperatively.
+// in depth order.  A warp takes 32 consecutive surfels, whose entries are one
+// contiguous run of the output: it scans their tile counts and then writes
+// the run 32 consecutive entries at a time, each lane finding the surfel
+// that owns its entry by a binary search over the warp's prefix sums.
 __global__ void __launch_bounds__(256) emit3d_ordered_kernel(
     int P, int num_rendered, const int* __restrict__ order, const float2* __restrict__ points_xy,
     const int* __restrict__ offsets, const int* __restrict__ radii,
     const int2* __restrict__ tile_radii, uint2 grid, unsigned* __restrict__ keys,
     int* __restrict__ vals) {
+    const unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    bool valid = false;
-    uint2 rmin = {0, 0}, rmax = {0, 0};
-    int off = 0, sid = 0;
+    int cnt = 0, x0 = 0, y0 = 0, w = 1, sid = 0, off = 0;
     if (i < P) {
         sid = min(max(order[i], 0), P - 1);
         const int2 tr = tile_radii[sid];
         if (radii[sid] > 0 && tr.x > 0 && tr.y > 0) {
+            uint2 rmin, rmax;
             get_rect(points_xy[sid], tr, rmin, rmax, grid);
-            valid = rmax.x > rmin.x && rmax.y > rmin.y;
-            off = i == 0 ? 0 : offsets[i - 1];
+            if (rmax.x > rmin.x && rmax.y > rmin.y) {
+                x0 = (int)rmin.x;
+                y0 = (int)rmin.y;
+                w = (int)(rmax.x - rmin.x);
+                cnt = w * (int)(rmax.y - rmin.y);
+            }
         }
+        off = i == 0 ? 0 : offsets[i - 1];
     }
-    unsigned todo = __ballot_sync(0xffffffffu, valid);
-    while (todo) {
-        const int j = __ffs(todo) - 1;
-        todo &= todo - 1;
-        const unsigned x0 = __shfl_sync(0xffffffffu, rmin.x, j);
-        const unsigned y0 = __shfl_sync(0xffffffffu, rmin.y, j);
-        const unsigned x1 = __shfl_sync(0xffffffffu, rmax.x, j);
-        const unsigned y1 = __shfl_sync(0xffffffffu, rmax.y, j);
-        const int base = __shfl_sync(0xffffffffu, off, j);
-        const int id = __shfl_sync(0xffffffffu, sid, j);
-        const int w = (int)(x1 - x0);
-        const int area = w * (int)(y1 - y0);
-        for (int e = lane; e < area; e += 32) {
-            const int pos = base + e;
-            if (pos < 0 || pos >= num_rendered) continue;
-            const unsigned ty = y0 + (unsigned)(e / w);
-            const unsigned tx = x0 + (unsigned)(e % w);
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(full, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const int excl = incl - cnt;
+    const int total = __shfl_sync(full, incl, 31);
+    const int base = __shfl_sync(full, off, 0);  // first entry of the warp's run
+    for (int e0 = 0; e0 < total; e0 += 32) {
+        const int e = e0 + lane;
+        // owner: the last lane whose exclusive prefix is <= e
+        int j = 0;
+#pragma unroll
+        for (int step = 16; step >= 1; step >>= 1) {
+            const int ex = __shfl_sync(full, excl, j + step);
+            if (ex <= e) j += step;
+        }
+        const int jx0 = __shfl_sync(full, x0, j);
+        const int jy0 = __shfl_sync(full, y0, j);
+        const int jw = __shfl_sync(full, w, j);
+        const int jid = __shfl_sync(full, sid, j);
+        const int jex = __shfl_sync(full, excl, j);
+        const int pos = base + e;
+        if (e < total && pos >= 0 && pos < num_rendered) {
+            const int local = e - jex;
+            const unsigned ty = (unsigned)(jy0 + local / jw);
+            const unsigned tx = (unsigned)(jx0 + local % jw);
             keys[pos] = ty * grid.x + tx;
-            vals[pos] = id;
+            vals[pos] = jid;
         }
     }
 }

@@ -17,6 +17,7 @@ provided by this build.
 
 from __future__ import annotations
 
+import math
 from typing import Optional
 
 import torch
@@ -35,6 +36,20 @@ stage_hook = None
 def _mark(name: str) -> None:
     if stage_hook is not None:
         stage_hook(name)
+
+
+def _zero_views(dev, shapes):
+    """Zero-filled float32 tensors of the given shapes carved out of one
+    allocation (one fill launch instead of one per tensor); each view starts
+    on a 16-byte boundary so the kernels' vector loads stay aligned."""
+    sizes = [int(math.prod(s)) for s in shapes]
+    padded = [(n + 3) // 4 * 4 for n in sizes]
+    buf = torch.zeros(max(1, sum(padded)), dtype=torch.float32, device=dev)
+    out, o = [], 0
+    for shape, n, pn in zip(shapes, sizes, padded):
+        out.append(buf[o:o + n].view(shape))
+        o += pn
+    return out
 
 
 def _empty(x: torch.Tensor, dtype=None) -> torch.Tensor:
@@ -160,7 +175,7 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
         # total (the one 8-byte read-back of the step, as in the reference)
         order = torch.empty((P,), **i32)
         offsets = torch.empty((P,), **i32)
-        total = torch.zeros((1,), dtype=torch.int64, device=dev)
+        total = torch.empty((1,), dtype=torch.int64, device=dev)
         ws = workspace(lib.query("hx_hexels3d_depth_order_workspace_bytes", P), dev)
         lib.call("hx_hexels3d_depth_order", P, ptr(depths), ptr(tiles_touched), ptr(order),
                  ptr(offsets), ptr(total), ptr(ws), ws.numel(), s)
@@ -176,15 +191,16 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                  ptr(values_sorted), ptr(ranges), ptr(ws), ws.numel(), s)
 
         _mark("bin")
-        out_color = torch.zeros((kNumChannels, H, W), **f32)
+        # the compositing kernel writes every pixel of these outputs
+        out_color = torch.empty((kNumChannels, H, W), **f32)
         contrib = torch.zeros((P,), **f32) if return_contrib else torch.empty((0,), **f32)
-        overdraw = torch.zeros((H, W), **f32) if return_overdraw else torch.empty((0,), **f32)
-        overdraw_hits = (torch.zeros((H, W), **f32) if return_overdraw_hits
+        overdraw = torch.empty((H, W), **f32) if return_overdraw else torch.empty((0,), **f32)
+        overdraw_hits = (torch.empty((H, W), **f32) if return_overdraw_hits
                          else torch.empty((0,), **f32))
         if return_surface:
-            surf_depth = torch.zeros((H, W), **f32)
-            surf_alpha = torch.zeros((H, W), **f32)
-            surf_maps = torch.zeros((kNumChannels + 1 + int(return_median_depth), H, W), **f32)
+            surf_depth = torch.empty((H, W), **f32)
+            surf_alpha = torch.empty((H, W), **f32)
+            surf_maps = torch.empty((kNumChannels + 1 + int(return_median_depth), H, W), **f32)
         else:
             surf_depth = surf_alpha = surf_maps = torch.empty((0,), **f32)
         contrib_count = torch.empty((H, W), **i32) if count_contrib else None
@@ -197,10 +213,10 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                           torch.empty((H, W), **i32))
         own = None
         if owner:
-            own = (torch.full((H, W), -1, dtype=torch.int64, device=dev),
-                   torch.zeros((H, W), **f32), torch.zeros((2, H, W), **f32),
-                   torch.zeros((H, W), **f32), torch.zeros((H, W), **f32),
-                   torch.zeros((H, W), **f32))
+            own = (torch.empty((H, W), dtype=torch.int64, device=dev),
+                   torch.empty((H, W), **f32), torch.empty((2, H, W), **f32),
+                   torch.empty((H, W), **f32), torch.empty((H, W), **f32),
+                   torch.empty((H, W), **f32))
         # launched even with nothing binned: every pixel is then the background
         lib.call("hx_hexels3d_render_forward", P, num_rendered, ptr(ranges),
                  ptr(values_sorted), ptr(points_xy_center) if prefilter_edge_on else None,
@@ -243,9 +259,14 @@ def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, col
                    grad_out_surf_depth, grad_out_surf_alpha, grad_out_surf_normals, image_width,
                    image_height, tan_fovx, tan_fovy, softness, scale_modifier, color_model,
                    view_model, use_view_grads, overdraw_base_count, prefilter_edge_on,
-                   conservative_bounds, debug, saved, surf_state=None, surf_normals=None):
+                   conservative_bounds, debug, saved, surf_state=None, surf_normals=None,
+                   accumulate_into=None):
     """rasterize_hexels3d_backward_impl (hexels3d_forward.cu:4882-5582) on the
-    forward's saved state."""
+    forward's saved state.  With `accumulate_into` (a dict from parameter
+    name -- means3d, scales, rotations, colors, color_grads, view_grads,
+    opacities -- to float32 buffers of the parameters' shapes) those gradients
+    are added into the given buffers instead of returned fresh: gradient
+    accumulation over views without a separate pass."""
     W, H = int(image_width), int(image_height)
     P, stride = _checks(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
                         specular_ks, specular_log_s, opacities, softnesses, viewmatrix,
@@ -277,29 +298,43 @@ def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, col
     (radii, transMats, opacities_out, softnesses_out, view_dirs, normals_saved, points_xy_center,
      ranges, values_sorted, final_T, last_index) = saved
     num_rendered = values_sorted.numel()
-    grad_means3d = torch.zeros((P, 3), **f32)
-    grad_means2d = torch.zeros_like(means2d)
     stride2d = means2d.size(1) if means2d.numel() > 0 else 3
-    grad_scales = torch.zeros((P, 2), **f32)
-    grad_rotations = torch.zeros((P, 4), **f32)
-    grad_colors = torch.zeros((P, 3), **f32)
-    grad_color_grads = torch.zeros_like(color_grads)
-    grad_color_quads = torch.zeros_like(color_quads)
-    grad_view_grads = torch.zeros_like(view_grads)
-    grad_specular_ks = torch.zeros_like(specular_ks)
-    grad_specular_log_s = torch.zeros_like(specular_log_s)
-    grad_opacities = torch.zeros((P,), **f32)
-    grad_softnesses = torch.zeros_like(softnesses, dtype=torch.float32)
     has_surface = (grad_out_surf_depth.numel() > 0 or grad_out_surf_alpha.numel() > 0 or
                    grad_out_surf_normals.numel() > 0)
     need_normals = view_model == 2 or grad_out_surf_normals.numel() > 0
     normals = surf_normals if (surf_normals is not None and surf_normals.numel() > 0) \
         else normals_saved
     _check(not need_normals or normals.numel() == 3 * P, "normals are required by this backward")
-    grad_normals = torch.zeros((P, 3), **f32) if need_normals else None
-    grad_transMats = torch.zeros((P, 9), **f32)
-    grad_view_dirs = torch.zeros((P, 3), **f32)
-    grad_center = torch.zeros((P, 2), **f32) if prefilter_edge_on else None
+    acc = dict(accumulate_into or {})
+    shapes = {"means3d": (P, 3), "means2d": tuple(means2d.shape), "scales": (P, 2),
+              "rotations": (P, 4), "colors": (P, 3), "color_grads": tuple(color_grads.shape),
+              "color_quads": tuple(color_quads.shape), "view_grads": tuple(view_grads.shape),
+              "specular_ks": tuple(specular_ks.shape),
+              "specular_log_s": tuple(specular_log_s.shape), "opacities": (P,),
+              "softnesses": tuple(softnesses.shape), "normals": (P, 3) if need_normals else (0,),
+              "transMats": (P, 9), "view_dirs": (P, 3),
+              "center": (P, 2) if prefilter_edge_on else (0,)}
+    for k, t in acc.items():
+        _check(k in ("means3d", "scales", "rotations", "colors", "color_grads", "view_grads",
+                     "opacities"), f"cannot accumulate the gradient of {k}")
+        check_input(t, k)
+        _check(t.dtype == torch.float32 and tuple(t.shape) == shapes[k],
+               f"accumulation buffer {k} must be float32 of shape {shapes[k]}")
+    fresh = [k for k in shapes if k not in acc]
+    g = dict(zip(fresh, _zero_views(dev, [shapes[k] for k in fresh])))
+    g.update(acc)
+    grad_means3d, grad_means2d, grad_scales, grad_rotations = (
+        g["means3d"], g["means2d"], g["scales"], g["rotations"])
+    grad_colors, grad_color_grads, grad_color_quads, grad_view_grads = (
+        g["colors"], g["color_grads"], g["color_quads"], g["view_grads"])
+    grad_specular_ks, grad_specular_log_s, grad_opacities, grad_softnesses = (
+        g["specular_ks"], g["specular_log_s"], g["opacities"], g["softnesses"])
+    grad_normals = g["normals"] if need_normals else None
+    grad_transMats, grad_view_dirs = g["transMats"], g["view_dirs"]
+    grad_center = g["center"] if prefilter_edge_on else None
+    geo_acc = int(bool(acc))
+    _check(not acc or all(k in acc for k in ("means3d", "scales", "rotations")),
+           "accumulation needs means3d, scales and rotations buffers together")
     _check(not has_surface or surf_state is not None,
            "surface gradients need a forward run with surface outputs")
     nz = lambda t: ptr(t) if t.numel() > 0 else None  # noqa: E731
@@ -340,7 +375,7 @@ def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, col
                      ptr(radii), ptr(transMats), ptr(grad_transMats), ptr(grad_view_dirs),
                      ptr(grad_normals), ptr(grad_center), ptr(grad_means3d),
                      ptr(grad_means2d) if means2d.numel() > 0 else None, int(stride2d),
-                     ptr(grad_scales), ptr(grad_rotations), s)
+                     ptr(grad_scales), ptr(grad_rotations), geo_acc, s)
             _mark("geometry_bwd")
         if debug:
             torch.cuda.synchronize(dev)

@@ -366,14 +366,16 @@ HX_API int hx_hexels3d_render_backward(
  * transmat_to_means2d_backward and points_xy_center_to_means3d_backward
  * (hexels3d_forward.cu:2494-2664).  grad_means3d, grad_scales and
  * grad_rotations are written for visible surfels and must be zeroed first;
- * grad_means2d (P, means2d_stride) may be NULL. */
+ * grad_means2d (P, means2d_stride) may be NULL.  With accumulate != 0 the
+ * gradients are added to the buffers' contents instead (gradient
+ * accumulation over views; no reference counterpart). */
 HX_API int hx_hexels3d_geometry_backward(
     int P, int num_rendered, const float* means3d, const float* scales, float scale_modifier,
     const float* rotations, const float* projmatrix, const float* campos, int image_width,
     int image_height, const int32_t* radii, const float* transMats, const float* grad_transMats,
     const float* grad_view_dirs, const float* grad_normals, const float* grad_points_xy_center,
     float* grad_means3d, float* grad_means2d, int means2d_stride, float* grad_scales,
-    float* grad_rotations, cudaStream_t stream);
+    float* grad_rotations, int accumulate, cudaStream_t stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -35,6 +35,8 @@ sys.path.insert(0, ROOT)
 
 import torch  # noqa: E402
 
+from sharding import GradBuffer, stripe_rows, view_split  # noqa: E402
+
 METRIC = "fwd+bwd Mpix/s"
 UNIT = "Mpix/s"
 L2_FLUSH_BYTES = 256 << 20
@@ -150,14 +152,6 @@ def max_over_ranks(x: float, world: int) -> float:
 # ---------------------------------------------------------------------------
 # Image-GS fit step
 # ---------------------------------------------------------------------------
-def stripe_rows(tiles_y: int, world: int, rank: int):
-    if world == 1:
-        return None
-    b = tiles_y * rank // world
-    e = tiles_y * (rank + 1) // world
-    return (b, e)
-
-
 class ImageGSStep:
     """Device-resident fit step, stage by stage (the same kernels as the
     public autograd API), with CUDA events between stages."""
@@ -418,10 +412,6 @@ FWD_FLOP_PER_PAIR = 90.0
 BWD_FLOP_PER_PAIR = 260.0
 
 
-def view_split(num_views: int, world: int, rank: int):
-    return [v for v in range(num_views) if v % world == rank]
-
-
 def make_targets(w, views, device):
     """Seeded U[0,1) target image per view (3,H,W)."""
     cam = w.cameras[0]
@@ -460,16 +450,9 @@ class Hexels3DStep:
         self.empty = torch.empty(0, device=dev)
         self.zero_hw = torch.zeros((self.H, self.W), device=dev)
         self.numel = 3 * self.H * self.W
-        # per-step gradient sums: one flat buffer (zeroed once per step,
-        # all-reduced in place), 16-byte aligned views per parameter, the
-        # loss in the last slot
-        sizes = [(p.numel() + 3) // 4 * 4 for p in self.params]
-        self.flat = torch.zeros(sum(sizes) + 4, device=dev)
-        self.acc, o = [], 0
-        for p, n in zip(self.params, sizes):
-            self.acc.append(self.flat[o:o + p.numel()].view(p.shape))
-            o += n
-        self.loss_slot = self.flat[o:o + 1]
+        # per-step gradient sums, zeroed once per step and all-reduced in place
+        self.grads = GradBuffer([p.shape for p in self.params], dev)
+        self.acc = self.grads.views
         self.marks: list = []
         self.stage_ms = {k: 0.0 for k in self.STAGES}
         self.info: dict = {}
@@ -525,17 +508,14 @@ class Hexels3DStep:
         self.C.stage_hook = self._mark
         try:
             self._mark("start")
-            self.flat.zero_()
+            self.grads.zero_()
             for cam, tgt in zip(self.cams, self.targets):
                 # the backward adds this view's gradients into self.acc
                 loss, _ = self._view(cam, tgt, keep_info)
-                self.loss_slot.add_(loss)
+                self.grads.loss.add_(loss)
                 self._mark("accumulate")
-            if self.world > 1:
-                import torch.distributed as dist
-
-                dist.all_reduce(self.flat)
-            total = self.loss_slot
+            self.grads.all_reduce_(self.world)
+            total = self.grads.loss
             self._mark("allreduce")
         finally:
             self.C.stage_hook = None
@@ -907,21 +887,36 @@ def cpu_baseline(args, w):
 
 def run_reference(args, world, rank):
     """Reference arm: the CPU restatement of the reference's algorithm (the
-    reference has no CPU implementation), all host threads, bounded sample per step."""
+    reference has no CPU implementation), all host threads, a bounded sample
+    of the workload per step.  Rank 0 only."""
     if rank != 0:
         return None
     import workloads
 
-    w = getattr(workloads, args.config)()
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    crop = max(1, min(args.cpu_crop_tiles, w.tile_bounds[0]))
+    three_d = args.config.startswith("hexels3d")
+    if three_d:
+        w = workload_3d(args.config)
+        crop = args.cpu_crop_tiles_3d
+        sample = lambda: cpu_sample_run_3d(w, crop)[:2]  # noqa: E731
+        cam = w.cameras[0]
+        config = {"workload": w.name, "views": len(w.cameras), "height": cam.height,
+                  "width": cam.width, "num_surfels": w.num_points,
+                  "outputs": "rgb + depth + alpha + normal + distortion"
+                  if args.config == "hexels3d_single" else "rgb"}
+    else:
+        w = getattr(workloads, args.config)()
+        crop = max(1, min(args.cpu_crop_tiles, w.tile_bounds[0]))
+        sample = lambda: cpu_sample_run(w, crop)  # noqa: E731
+        config = {"workload": w.name, "height": w.height, "width": w.width,
+                  "num_gaussians": w.num_points, "top_k": 10, "tile": 16}
     for _ in range(min(args.warmup, 1)):
-        cpu_sample_run(w, crop)
+        sample()
     secs_total, mpix_total = 0.0, 0.0
     steps = max(1, min(args.steps, args.ref_max_steps))
     for _ in range(steps):
-        s, mp = cpu_sample_run(w, crop)
+        s, mp = sample()
         secs_total += s
         mpix_total += mp
     value = mpix_total / secs_total
@@ -929,15 +924,16 @@ def run_reference(args, world, rank):
         "metric": METRIC, "value": round(value, 5), "unit": UNIT, "impl": "reference",
         "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 1),
         "ms_per_step": round(secs_total / steps * 1e3, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded)",
-        "config": {"workload": w.name, "height": w.height, "width": w.width,
-                   "num_gaussians": w.num_points, "top_k": 10, "tile": 16},
+        "higher_is_better": True, "scaling": "strong" if three_d else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": config,
         "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads,
                          "kind": "port",
                          "sample": f"each step: one fwd+bwd over a {crop}x{crop}-tile centre "
-                                   f"crop ({mpix_total / steps:.4f} Mpix); the reference ships "
-                                   "CUDA only, so this is its algorithm restated on the CPU"},
+                                   f"crop ({mpix_total / steps:.4f} Mpix)"
+                                   + (" of view 0" if three_d else "")
+                                   + "; the reference ships CUDA only, so this is its "
+                                   "algorithm restated on the CPU"},
         "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

@@ -487,6 +487,9 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_bwd_kernel(const B
     if (n_max > 0) atomicMax(&s_max_visit, n_max);
     __syncthreads();
     const int block_max = s_max_visit;
+    // list entries at or past every one of this warp's last indices change
+    // nothing for the warp: it starts its walk below them
+    const int warp_max = __reduce_max_sync(0xffffffffu, n_max);
 
     const int nb = (block_max + kBatch - 1) / kBatch;
     for (int b = nb - 1; b >= 0; --b) {
@@ -554,7 +557,7 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_bwd_kernel(const B
         for (int t = tr; t < kBatch * L.ncomp; t += kThreads) s_acc[t] = 0.f;
         __syncthreads();
 
-        for (int idx = bend - 1; idx >= bstart; --idx) {
+        for (int idx = min(bend, warp_max) - 1; idx >= bstart; --idx) {
             const Surfel3D& s = s_prim[idx - bstart];
             // no pixel of a warp block the surfel's box misses blends it, so
             // nothing of the pair changes there (warp-uniform)

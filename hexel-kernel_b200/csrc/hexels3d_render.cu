@@ -16,27 +16,193 @@
 
 namespace hx {
 
+// Per-pixel state of the front-to-back compositing.  Surface and owner
+// fields are dead (and eliminated) in the instantiations without them.
+struct FwdPixel {
+    float px, py;
+    bool done_color, done_surf;
+    float T, C0, C1, C2;
+    int n_visited, n_blended;
+    float overdraw, overdraw_hits;
+    float T_surf, D_surf, median_depth, M1, M2, distortion;
+    float3 N_surf;
+    int n_visited_surf, median_idx;
+    long long owner_id;
+    float owner_weight, owner_sdf, owner_depth;
+    float2 owner_uv;
+};
+
+// One (pixel, surfel) pair at list index `idx` (batch slot j): the
+// reference's per-pair arithmetic (hexels3d_forward.cu:690-1000).
 template <bool SURF, bool PREFILTER, bool OWNER>
-__global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a) {
+__device__ __forceinline__ void fwd_pair(const Render3DArgs& a, const Surfel3D& s, int idx, int j,
+                                         FwdPixel& q, float* s_contrib) {
+    const int g_id = s.id;
+    const bool is_base = g_id < a.overdraw_base;
+    if (SURF && q.done_color && !is_base) return;
+    const float px = q.px, py = q.py;
+    const float3 Tu = {s.tu[0], s.tu[1], s.tu[2]};
+    const float3 Tv = {s.tv[0], s.tv[1], s.tv[2]};
+    const float3 Tw = {s.tw[0], s.tw[1], s.tw[2]};
+    const float3 k = {px * Tw.x - Tu.x, px * Tw.y - Tu.y, px * Tw.z - Tu.z};
+    const float3 l = {py * Tw.x - Tv.x, py * Tw.y - Tv.y, py * Tw.z - Tv.z};
+    const float3 p = cross3(k, l);
+    if (p.z == 0.0f) return;
+    const float sx = p.x / p.z;
+    const float sy = p.y / p.z;
+    const float depth_sdf = (sx * Tw.x + sy * Tw.y) + Tw.z;
+    if (depth_sdf < k3NearPlane) return;
+    int edge;
+    const float dist = hex_sdf3(sx, sy, edge);
+    const float soft = (edge == 0) ? s.s0 : ((edge == 1) ? s.s1 : s.s2);
+    const float boundary = sigmoid_neg(dist, soft);
+    const float alpha_raw_sdf = s.opacity * boundary;
+    const float alpha_sdf = fminf(alpha_raw_sdf, 0.99f);
+    float alpha = alpha_sdf;
+    bool use_filter = false;
+    if (PREFILTER) {
+        const float dx = px - s.q.ctr.x;
+        const float dy = py - s.q.ctr.y;
+        const float G = __expf(-0.5f * k3FilterInvSquare * (dx * dx + dy * dy));
+        const float alpha_filter = fminf(s.opacity * G, 0.99f);
+        use_filter = alpha_filter > alpha_sdf;
+        alpha = use_filter ? alpha_filter : alpha_sdf;
+    }
+    if (alpha < 1.0f / 255.0f) return;
+    const float depth = use_filter ? Tw.z : depth_sdf;
+
+    if (!q.done_color) {
+        if (is_base && alpha_sdf >= 1.0f / 255.0f) {
+            if (a.overdraw) q.overdraw += alpha_raw_sdf;
+            if (a.overdraw_hits) q.overdraw_hits += 1.0f;
+        }
+        const float test_T = q.T * (1.f - alpha);
+        if (test_T < 0.0001f) {
+            q.done_color = true;
+        } else {
+            const float w = alpha * q.T;
+            const float u = use_filter ? 0.f : sx;
+            const float v = use_filter ? 0.f : sy;
+            if (OWNER) {
+                if (w > q.owner_weight) {
+                    q.owner_id = g_id;
+                    q.owner_weight = w;
+                    q.owner_uv = {sx, sy};
+                    q.owner_sdf = dist;
+                    q.owner_depth = depth;
+                }
+            }
+            float cx = s.cb[0], cy = s.cb[1], cz = s.cb[2];
+            if (a.color_model >= kColorLinear) {
+                cx += u * s.gu[0] + v * s.gv[0];
+                cy += u * s.gu[1] + v * s.gv[1];
+                cz += u * s.gu[2] + v * s.gv[2];
+            }
+            if (a.color_model == kColorQuadratic || a.color_model == kColorQuadBounded) {
+                const float* cq = a.color_quads + 9 * g_id;
+                float uu = u, vv = v;
+                if (a.color_model == kColorQuadBounded) bounded_coords(u, v, uu, vv);
+                const float u2 = uu * uu, uv = uu * vv, v2 = vv * vv;
+                cx += u2 * cq[0] + uv * cq[3] + v2 * cq[6];
+                cy += u2 * cq[1] + uv * cq[4] + v2 * cq[7];
+                cz += u2 * cq[2] + uv * cq[5] + v2 * cq[8];
+            }
+            if (a.use_view_grads) {
+                cx += s.cv[0];
+                cy += s.cv[1];
+                cz += s.cv[2];
+            }
+            if (a.view_model == kViewLobe) {
+                const float* vd = a.view_dirs + 3 * g_id;
+                const float* nr = a.normals + 3 * g_id;
+                const float cos_nv = fmaxf(-(nr[0] * vd[0] + nr[1] * vd[1] + nr[2] * vd[2]), 0.f);
+                const float log_s = a.specular_log_s[g_id];
+                const float s_exp = __expf(fminf(fmaxf(log_s, 0.f), 5.0f));
+                const float spec = (cos_nv > 0.f) ? __powf(cos_nv, s_exp) : 0.f;
+                cx += a.specular_ks[3 * g_id] * spec;
+                cy += a.specular_ks[3 * g_id + 1] * spec;
+                cz += a.specular_ks[3 * g_id + 2] * spec;
+            }
+            q.C0 += cx * w;
+            q.C1 += cy * w;
+            q.C2 += cz * w;
+            q.T = test_T;
+            q.n_visited = idx + 1;
+            ++q.n_blended;
+            if (a.contrib) atomicAdd(&s_contrib[j], w);
+        }
+    }
+    if (SURF && !q.done_surf && is_base) {
+        const float test_T_surf = q.T_surf * (1.f - alpha);
+        if (test_T_surf < 0.0001f) {
+            q.done_surf = true;
+        } else {
+            if (a.median && q.T_surf > 0.5f) {
+                q.median_depth = depth;
+                q.median_idx = idx;
+            }
+            const float w_surf = alpha * q.T_surf;
+            const float m = k3FarPlane / (k3FarPlane - k3NearPlane) * (1.0f - k3NearPlane / depth);
+            const float acc_alpha = 1.0f - q.T_surf;
+            q.distortion += (m * m * acc_alpha + q.M2 - 2.0f * m * q.M1) * w_surf;
+            q.M1 += m * w_surf;
+            q.M2 += m * m * w_surf;
+            q.D_surf += depth * w_surf;
+            q.N_surf.x += s.n[0] * w_surf;
+            q.N_surf.y += s.n[1] * w_surf;
+            q.N_surf.z += s.n[2] * w_surf;
+            q.T_surf = test_T_surf;
+            q.n_visited_surf = idx + 1;
+        }
+    }
+}
+
+// One CTA per 16x16 tile, 256 / PPT threads, PPT pixels per thread: warps
+// cover 8 x (4 PPT) pixel blocks (two across, 4 / PPT down), lane l owns
+// pixels (l % 8, l / 8 + 4 k), k < PPT.  The tile's list is staged 256
+// surfels at a time; a warp skips a surfel whose pixel box misses its block.
+template <bool SURF, bool PREFILTER, bool OWNER, int PPT>
+__global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const Render3DArgs a) {
+    constexpr int kThreads = k3BlockSize / PPT;
+    constexpr int kWarpRows = 4 * PPT;
     __shared__ Surfel3D s_prim[k3BlockSize];
     __shared__ float s_contrib[k3BlockSize];
 
     const int W = a.W, H = a.H;
     const unsigned hblocks = (W + k3BlockX - 1) / k3BlockX;
-    const int tr = threadIdx.y * k3BlockX + threadIdx.x;
-    const int2 lp = tile_pixel(tr);
-    const unsigned px_i = blockIdx.x * k3BlockX + lp.x;
-    const unsigned py_i = blockIdx.y * k3BlockY + lp.y;
-    const unsigned pix_id = (unsigned)(W * (int)py_i + (int)px_i);
-    // this warp's 8x4 pixel block
-    const int wx0 = (int)(blockIdx.x * k3BlockX) + (((tr >> 5) & 1) << 3);
-    const int wy0 = (int)(blockIdx.y * k3BlockY) + ((tr >> 6) << 2);
-    const float px = (float)px_i;
-    const float py = (float)py_i;
-    const bool inside = px_i < (unsigned)W && py_i < (unsigned)H;
-    bool done_color = !inside;
-    bool done_surf = SURF ? !inside : true;
-    bool done = SURF ? (done_color && done_surf) : done_color;
+    const int tr = threadIdx.x;
+    const int lane = tr & 31;
+    const int warp = tr >> 5;
+    const int wx0 = (int)(blockIdx.x * k3BlockX) + ((warp & 1) << 3);
+    const int wy0 = (int)(blockIdx.y * k3BlockY) + (warp >> 1) * kWarpRows;
+
+    FwdPixel q[PPT];
+    bool inside[PPT];
+    bool thread_done = true;
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+        const int pxi = wx0 + (lane & 7);
+        const int pyi = wy0 + (lane >> 3) + 4 * k;
+        inside[k] = pxi < W && pyi < H;
+        FwdPixel& p = q[k];
+        p.px = (float)pxi;
+        p.py = (float)pyi;
+        p.done_color = !inside[k];
+        p.done_surf = SURF ? !inside[k] : true;
+        p.T = 1.0f;
+        p.C0 = p.C1 = p.C2 = 0.f;
+        p.n_visited = p.n_blended = 0;
+        p.overdraw = p.overdraw_hits = 0.f;
+        p.T_surf = 1.0f;
+        p.D_surf = p.median_depth = p.M1 = p.M2 = p.distortion = 0.f;
+        p.N_surf = {0.f, 0.f, 0.f};
+        p.n_visited_surf = 0;
+        p.median_idx = -1;
+        p.owner_id = -1;
+        p.owner_weight = p.owner_sdf = p.owner_depth = 0.f;
+        p.owner_uv = {0.f, 0.f};
+        thread_done = thread_done && p.done_color && p.done_surf;
+    }
 
     uint2 range = a.ranges[blockIdx.y * hblocks + blockIdx.x];
     range.y = min(range.y, (unsigned)a.num_rendered);
@@ -44,34 +210,22 @@ __global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a)
     const int rounds = (int)((range.y - range.x + k3BlockSize - 1) / k3BlockSize);
     int to_do = (int)(range.y - range.x);
 
-    int n_visited = 0;
-    int n_blended = 0;
-    float T = 1.0f;
-    float C0 = 0.f, C1 = 0.f, C2 = 0.f;
-    float overdraw = 0.f, overdraw_hits = 0.f;
-    float T_surf = 1.0f, D_surf = 0.f, median_depth = 0.f, M1 = 0.f, M2 = 0.f, distortion = 0.f;
-    float3 N_surf = {0.f, 0.f, 0.f};
-    int n_visited_surf = 0;
-    int median_idx = -1;
-    long long owner_id = -1;
-    float owner_weight = 0.f, owner_sdf = 0.f, owner_depth = 0.f;
-    float2 owner_uv = {0.f, 0.f};
-
     for (int i = 0; i < rounds; ++i, to_do -= k3BlockSize) {
-        if (__syncthreads_count(done) == k3BlockSize) break;
-        const int progress = i * k3BlockSize + tr;
-        s_contrib[tr] = 0.f;
-        if ((int)range.x + progress < (int)range.y) {
+        if (__syncthreads_count(thread_done) == kThreads) break;
+        for (int t = tr; t < k3BlockSize; t += kThreads) {
+            s_contrib[t] = 0.f;
+            const int progress = i * k3BlockSize + t;
+            if ((int)range.x + progress >= (int)range.y) continue;
             int g = a.point_list[range.x + progress];
             g = min(max(g, 0), a.P - 1);
-            Surfel3D& s = s_prim[tr];
+            Surfel3D& s = s_prim[t];
             s.id = g;
             const float* Tm = a.transMats + 9 * g;
 #pragma unroll
-            for (int q = 0; q < 3; ++q) {
-                s.tu[q] = Tm[q];
-                s.tv[q] = Tm[3 + q];
-                s.tw[q] = Tm[6 + q];
+            for (int c = 0; c < 3; ++c) {
+                s.tu[c] = Tm[c];
+                s.tv[c] = Tm[3 + c];
+                s.tw[c] = Tm[6 + c];
             }
             s.opacity = a.opacities[g];
             if (a.softness_stride == 3) {
@@ -82,16 +236,16 @@ __global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a)
                 s.s0 = s.s1 = s.s2 = a.softnesses[g];
             }
 #pragma unroll
-            for (int q = 0; q < 3; ++q) s.cb[q] = a.colors[3 * g + q];
+            for (int c = 0; c < 3; ++c) s.cb[c] = a.colors[3 * g + c];
             if (a.color_model >= kColorLinear) {
 #pragma unroll
-                for (int q = 0; q < 3; ++q) {
-                    s.gu[q] = a.color_grads[6 * g + q];
-                    s.gv[q] = a.color_grads[6 * g + 3 + q];
+                for (int c = 0; c < 3; ++c) {
+                    s.gu[c] = a.color_grads[6 * g + c];
+                    s.gv[c] = a.color_grads[6 * g + 3 + c];
                 }
             } else {
 #pragma unroll
-                for (int q = 0; q < 3; ++q) s.gu[q] = s.gv[q] = 0.f;
+                for (int c = 0; c < 3; ++c) s.gu[c] = s.gv[c] = 0.f;
             }
             if (a.use_view_grads) {
                 const float* vd = a.view_dirs + 3 * g;
@@ -122,179 +276,71 @@ __global__ void __launch_bounds__(256) render3d_fwd_kernel(const Render3DArgs a)
         __syncthreads();
 
         const int batch_size = min(k3BlockSize, to_do);
-        for (int j = 0; !done && j < batch_size; ++j) {
+        for (int j = 0; !thread_done && j < batch_size; ++j) {
             const Surfel3D& s = s_prim[j];
             // every pixel of a warp block the surfel's box misses has alpha < 1/255
-            if (!PREFILTER && box_misses(s.q.box, wx0, wy0, wx0 + 7, wy0 + 3)) continue;
-            const int g_id = s.id;
-            const bool is_base = g_id < a.overdraw_base;
-            if (SURF && done_color && !is_base) continue;
-            const float3 Tu = {s.tu[0], s.tu[1], s.tu[2]};
-            const float3 Tv = {s.tv[0], s.tv[1], s.tv[2]};
-            const float3 Tw = {s.tw[0], s.tw[1], s.tw[2]};
-            const float3 k = {px * Tw.x - Tu.x, px * Tw.y - Tu.y, px * Tw.z - Tu.z};
-            const float3 l = {py * Tw.x - Tv.x, py * Tw.y - Tv.y, py * Tw.z - Tv.z};
-            const float3 p = cross3(k, l);
-            if (p.z == 0.0f) continue;
-            const float sx = p.x / p.z;
-            const float sy = p.y / p.z;
-            const float depth_sdf = (sx * Tw.x + sy * Tw.y) + Tw.z;
-            if (depth_sdf < k3NearPlane) continue;
-            int edge;
-            const float dist = hex_sdf3(sx, sy, edge);
-            const float soft = (edge == 0) ? s.s0 : ((edge == 1) ? s.s1 : s.s2);
-            const float boundary = sigmoid_neg(dist, soft);
-            const float alpha_raw_sdf = s.opacity * boundary;
-            const float alpha_sdf = fminf(alpha_raw_sdf, 0.99f);
-            float alpha = alpha_sdf;
-            bool use_filter = false;
-            if (PREFILTER) {
-                const float dx = px - s.q.ctr.x;
-                const float dy = py - s.q.ctr.y;
-                const float G = __expf(-0.5f * k3FilterInvSquare * (dx * dx + dy * dy));
-                const float alpha_filter = fminf(s.opacity * G, 0.99f);
-                use_filter = alpha_filter > alpha_sdf;
-                alpha = use_filter ? alpha_filter : alpha_sdf;
+            if (!PREFILTER && box_misses(s.q.box, wx0, wy0, wx0 + 7, wy0 + kWarpRows - 1))
+                continue;
+            bool all_done = true;
+#pragma unroll
+            for (int k = 0; k < PPT; ++k) {
+                if (!(q[k].done_color && q[k].done_surf))
+                    fwd_pair<SURF, PREFILTER, OWNER>(a, s, i * k3BlockSize + j, j, q[k],
+                                                     s_contrib);
+                all_done = all_done && q[k].done_color && q[k].done_surf;
             }
-            if (alpha < 1.0f / 255.0f) continue;
-            const float depth = use_filter ? Tw.z : depth_sdf;
-
-            if (!done_color) {
-                if (is_base && alpha_sdf >= 1.0f / 255.0f) {
-                    if (a.overdraw) overdraw += alpha_raw_sdf;
-                    if (a.overdraw_hits) overdraw_hits += 1.0f;
-                }
-                const float test_T = T * (1.f - alpha);
-                if (test_T < 0.0001f) {
-                    done_color = true;
-                } else {
-                    const float w = alpha * T;
-                    const float u = use_filter ? 0.f : sx;
-                    const float v = use_filter ? 0.f : sy;
-                    if (OWNER) {
-                        if (w > owner_weight) {
-                            owner_id = g_id;
-                            owner_weight = w;
-                            owner_uv = {sx, sy};
-                            owner_sdf = dist;
-                            owner_depth = depth;
-                        }
-                    }
-                    float cx = s.cb[0], cy = s.cb[1], cz = s.cb[2];
-                    if (a.color_model >= kColorLinear) {
-                        cx += u * s.gu[0] + v * s.gv[0];
-                        cy += u * s.gu[1] + v * s.gv[1];
-                        cz += u * s.gu[2] + v * s.gv[2];
-                    }
-                    if (a.color_model == kColorQuadratic || a.color_model == kColorQuadBounded) {
-                        const float* cq = a.color_quads + 9 * g_id;
-                        float uu = u, vv = v;
-                        if (a.color_model == kColorQuadBounded) bounded_coords(u, v, uu, vv);
-                        const float u2 = uu * uu, uv = uu * vv, v2 = vv * vv;
-                        cx += u2 * cq[0] + uv * cq[3] + v2 * cq[6];
-                        cy += u2 * cq[1] + uv * cq[4] + v2 * cq[7];
-                        cz += u2 * cq[2] + uv * cq[5] + v2 * cq[8];
-                    }
-                    if (a.use_view_grads) {
-                        cx += s.cv[0];
-                        cy += s.cv[1];
-                        cz += s.cv[2];
-                    }
-                    if (a.view_model == kViewLobe) {
-                        const float* vd = a.view_dirs + 3 * g_id;
-                        const float* nr = a.normals + 3 * g_id;
-                        const float cos_nv =
-                            fmaxf(-(nr[0] * vd[0] + nr[1] * vd[1] + nr[2] * vd[2]), 0.f);
-                        const float log_s = a.specular_log_s[g_id];
-                        const float s_exp = __expf(fminf(fmaxf(log_s, 0.f), 5.0f));
-                        const float spec = (cos_nv > 0.f) ? __powf(cos_nv, s_exp) : 0.f;
-                        cx += a.specular_ks[3 * g_id] * spec;
-                        cy += a.specular_ks[3 * g_id + 1] * spec;
-                        cz += a.specular_ks[3 * g_id + 2] * spec;
-                    }
-                    C0 += cx * w;
-                    C1 += cy * w;
-                    C2 += cz * w;
-                    T = test_T;
-                    n_visited = i * k3BlockSize + j + 1;
-                    ++n_blended;
-                    if (a.contrib) atomicAdd(&s_contrib[j], w);
-                }
-            }
-            if (SURF) {
-                if (!done_surf && is_base) {
-                    const float test_T_surf = T_surf * (1.f - alpha);
-                    if (test_T_surf < 0.0001f) {
-                        done_surf = true;
-                    } else {
-                        if (a.median && T_surf > 0.5f) {
-                            median_depth = depth;
-                            median_idx = i * k3BlockSize + j;
-                        }
-                        const float w_surf = alpha * T_surf;
-                        const float m = k3FarPlane / (k3FarPlane - k3NearPlane) *
-                                        (1.0f - k3NearPlane / depth);
-                        const float acc_alpha = 1.0f - T_surf;
-                        distortion += (m * m * acc_alpha + M2 - 2.0f * m * M1) * w_surf;
-                        M1 += m * w_surf;
-                        M2 += m * m * w_surf;
-                        D_surf += depth * w_surf;
-                        N_surf.x += s.n[0] * w_surf;
-                        N_surf.y += s.n[1] * w_surf;
-                        N_surf.z += s.n[2] * w_surf;
-                        T_surf = test_T_surf;
-                        n_visited_surf = i * k3BlockSize + j + 1;
-                    }
-                }
-                done = done_color && done_surf;
-            } else {
-                done = done_color;
-            }
+            thread_done = all_done;
         }
         if (a.contrib) {
             __syncthreads();
-            if (tr < batch_size && s_contrib[tr] != 0.f) atomicAdd(&a.contrib[s_prim[tr].id], s_contrib[tr]);
+            for (int t = tr; t < batch_size; t += kThreads)
+                if (s_contrib[t] != 0.f) atomicAdd(&a.contrib[s_prim[t].id], s_contrib[t]);
         }
     }
 
-    if (!inside) return;
     const int HW = H * W;
-    if (a.final_T) {
-        a.final_T[pix_id] = T;
-        a.last_index[pix_id] = n_visited;
-    }
-    if (a.contrib_count) a.contrib_count[pix_id] = n_blended;
-    // With nothing binned every tile range is empty and the pixel is the
-    // background, as in the reference (hexels3d_forward.cu:3300-3470).
-    a.out_color[pix_id] = C0 + T * a.bg[0];
-    a.out_color[HW + pix_id] = C1 + T * a.bg[1];
-    a.out_color[2 * HW + pix_id] = C2 + T * a.bg[2];
-    if (a.overdraw) a.overdraw[pix_id] = overdraw;
-    if (a.overdraw_hits) a.overdraw_hits[pix_id] = overdraw_hits;
-    if (SURF) {
-        a.out_depth[pix_id] = D_surf;
-        a.out_alpha[pix_id] = 1.0f - T_surf;
-        a.out_surface[pix_id] = N_surf.x;
-        a.out_surface[HW + pix_id] = N_surf.y;
-        a.out_surface[2 * HW + pix_id] = N_surf.z;
-        a.out_surface[3 * HW + pix_id] = distortion;
-        if (a.median) a.out_surface[4 * HW + pix_id] = median_depth;
-        if (a.final_T_surf) {
-            a.final_T_surf[pix_id] = T_surf;
-            a.last_index_surf[pix_id] = n_visited_surf;
-            a.m1_surf[pix_id] = M1;
-            a.m2_surf[pix_id] = M2;
-            a.median_index[pix_id] = median_idx;
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+        if (!inside[k]) continue;
+        const FwdPixel& p = q[k];
+        const int pix = (int)p.py * W + (int)p.px;
+        if (a.final_T) {
+            a.final_T[pix] = p.T;
+            a.last_index[pix] = p.n_visited;
         }
-    }
-    if (OWNER) {
-        a.owner_id[pix_id] = owner_id;
-        a.owner_weight[pix_id] = owner_weight;
-        a.owner_uv[pix_id] = owner_uv.x;
-        a.owner_uv[HW + pix_id] = owner_uv.y;
-        a.owner_sdf[pix_id] = owner_sdf;
-        a.owner_depth[pix_id] = owner_depth;
-        a.total_alpha[pix_id] = 1.0f - T;
+        if (a.contrib_count) a.contrib_count[pix] = p.n_blended;
+        // With nothing binned every tile range is empty and the pixel is the
+        // background, as in the reference (hexels3d_forward.cu:3300-3470).
+        a.out_color[pix] = p.C0 + p.T * a.bg[0];
+        a.out_color[HW + pix] = p.C1 + p.T * a.bg[1];
+        a.out_color[2 * HW + pix] = p.C2 + p.T * a.bg[2];
+        if (a.overdraw) a.overdraw[pix] = p.overdraw;
+        if (a.overdraw_hits) a.overdraw_hits[pix] = p.overdraw_hits;
+        if (SURF) {
+            a.out_depth[pix] = p.D_surf;
+            a.out_alpha[pix] = 1.0f - p.T_surf;
+            a.out_surface[pix] = p.N_surf.x;
+            a.out_surface[HW + pix] = p.N_surf.y;
+            a.out_surface[2 * HW + pix] = p.N_surf.z;
+            a.out_surface[3 * HW + pix] = p.distortion;
+            if (a.median) a.out_surface[4 * HW + pix] = p.median_depth;
+            if (a.final_T_surf) {
+                a.final_T_surf[pix] = p.T_surf;
+                a.last_index_surf[pix] = p.n_visited_surf;
+                a.m1_surf[pix] = p.M1;
+                a.m2_surf[pix] = p.M2;
+                a.median_index[pix] = p.median_idx;
+            }
+        }
+        if (OWNER) {
+            a.owner_id[pix] = p.owner_id;
+            a.owner_weight[pix] = p.owner_weight;
+            a.owner_uv[pix] = p.owner_uv.x;
+            a.owner_uv[HW + pix] = p.owner_uv.y;
+            a.owner_sdf[pix] = p.owner_sdf;
+            a.owner_depth[pix] = p.owner_depth;
+            a.total_alpha[pix] = 1.0f - p.T;
+        }
     }
 }
 
@@ -306,8 +352,11 @@ namespace {
 
 template <bool SURF, bool PREFILTER, bool OWNER>
 int launch_render(const Render3DArgs& a, cudaStream_t stream) {
-    dim3 grid(ceil_div(a.W, k3BlockX), ceil_div(a.H, k3BlockY)), block(k3BlockX, k3BlockY);
-    render3d_fwd_kernel<SURF, PREFILTER, OWNER><<<grid, block, 0, stream>>>(a);
+    // One pixel per thread: each pixel terminates on its own, and two per
+    // thread keep a lane busy until both have (measured slower on B200).
+    constexpr int kPPT = 1;
+    dim3 grid(ceil_div(a.W, k3BlockX), ceil_div(a.H, k3BlockY));
+    render3d_fwd_kernel<SURF, PREFILTER, OWNER, kPPT><<<grid, k3BlockSize / kPPT, 0, stream>>>(a);
     HX_LAUNCH_CHECK("render3d_fwd_kernel");
     return HX_OK;
 }

@@ -37,6 +37,38 @@ struct BwdLayout {
 constexpr int kFixCg = 3, kFixOp = 9, kFixSoft = 10, kFixTm = 13, kFixN = 22, kFixAbs = 25,
               kFixCtr = 26, kFixVd = 28, kFixComp = 31;
 
+// Lite slot layout of the plain RGB configuration (flat or linear colour, no
+// or linear view model, no softness, normal, prefilter or means2d-norm
+// gradients): colour 0-2, colour gradients 3-8, opacity 9, transform 10-18;
+// padded to 24 slots.
+constexpr int kLiteCg = 3, kLiteOp = 9, kLiteTm = 10, kLiteComp = 19;
+
+// Sum of a 24-slot vector over the warp: three reduce-scatter halvings
+// (over lane bits 4, 3, 2) leave each lane 3 slots summed over 8 lanes, then
+// an all-reduce over lane bits 1 and 0 completes the sums.  Lanes that share
+// bits 2-4 hold the same 3 slots, starting at the returned index.
+__device__ __forceinline__ int warp_reduce_scatter24(float (&v)[24], const int lane) {
+    int start = 0;
+#pragma unroll
+    for (int o = 16, n = 24; o >= 4; o >>= 1, n >>= 1) {
+        const int half = n / 2;
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+        if (upper) start += half;
+    }
+#pragma unroll
+    for (int o = 2; o >= 1; o >>= 1) {
+#pragma unroll
+        for (int i = 0; i < 3; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
+    }
+    return start;
+}
+
 template <int N>
 __device__ __forceinline__ int warp_reduce_scatter(float (&v)[N], const int lane) {
     int start = 0;
@@ -389,7 +421,7 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
 // pixels (l % 8, l / 8 + 4 k), k < PPT.  Per list index the PPT pairs of a
 // thread are added into one gradient vector before the warp reduction.
 template <bool SURF, bool PREFILTER, int N, int PPT>
-__global__ void __launch_bounds__(k3BlockSize / PPT) render3d_bwd_kernel(const Backward3DArgs a,
+__global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_bwd_kernel(const Backward3DArgs a,
                                                                         const BwdLayout L) {
     constexpr int kThreads = k3BlockSize / PPT;
     constexpr int kBatch = kThreads;  // surfels staged per batch
@@ -403,18 +435,19 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_bwd_kernel(const B
     // gradient vector in registers); N == 64 takes the host-computed layout
     // of the quadratic colour and lobe view models.
     constexpr bool FIX = (N == 32);
+    constexpr bool LITE = (N == 24);  // lite layout: slots absent from it are never touched
     BwdSlots O;
-    O.cg = FIX ? kFixCg : L.off_cg;
-    O.cq = FIX ? 0 : L.off_cq;
-    O.op = FIX ? kFixOp : L.off_op;
-    O.soft = FIX ? kFixSoft : L.off_soft;
-    O.tm = FIX ? kFixTm : L.off_tm;
-    O.vd = FIX ? kFixVd : L.off_vd;
-    O.n = FIX ? kFixN : L.off_n;
-    O.ks = FIX ? 0 : L.off_ks;
-    O.ls = FIX ? 0 : L.off_ls;
-    O.abs = FIX ? kFixAbs : L.off_abs;
-    O.ctr = FIX ? kFixCtr : L.off_ctr;
+    O.cg = LITE ? kLiteCg : FIX ? kFixCg : L.off_cg;
+    O.cq = (FIX || LITE) ? 0 : L.off_cq;
+    O.op = LITE ? kLiteOp : FIX ? kFixOp : L.off_op;
+    O.soft = LITE ? 0 : FIX ? kFixSoft : L.off_soft;
+    O.tm = LITE ? kLiteTm : FIX ? kFixTm : L.off_tm;
+    O.vd = LITE ? 0 : FIX ? kFixVd : L.off_vd;
+    O.n = LITE ? 0 : FIX ? kFixN : L.off_n;
+    O.ks = (FIX || LITE) ? 0 : L.off_ks;
+    O.ls = (FIX || LITE) ? 0 : L.off_ls;
+    O.abs = LITE ? 0 : FIX ? kFixAbs : L.off_abs;
+    O.ctr = LITE ? 0 : FIX ? kFixCtr : L.off_ctr;
 
     const int W = a.W, H = a.H;
     const unsigned hblocks = (W + k3BlockX - 1) / k3BlockX;
@@ -571,12 +604,20 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_bwd_kernel(const B
             for (int k = 0; k < PPT; ++k)
                 contributed |= bwd_pair<SURF, PREFILTER, N>(a, L, O, s, idx, q[k], acc);
             if (__any_sync(0xffffffffu, contributed)) {
-                const int start = warp_reduce_scatter<N>(acc, lane);
                 float* dst = s_acc + (idx - bstart) * L.ncomp;
-#pragma unroll
-                for (int c = 0; c < N / 32; ++c) {
+                if constexpr (N == 24) {
+                    const int start = warp_reduce_scatter24(acc, lane);
+                    const int c = lane & 3;  // lanes 0-2 of each group of 4 write
+                    const float val = c == 0 ? acc[0] : (c == 1 ? acc[1] : acc[2]);
                     const int comp = start + c;
-                    if (comp < L.ncomp && acc[c] != 0.f) atomicAdd(dst + comp, acc[c]);
+                    if (c < 3 && comp < L.ncomp && val != 0.f) atomicAdd(dst + comp, val);
+                } else {
+                    const int start = warp_reduce_scatter<N>(acc, lane);
+#pragma unroll
+                    for (int c = 0; c < N / 32; ++c) {
+                        const int comp = start + c;
+                        if (comp < L.ncomp && acc[c] != 0.f) atomicAdd(dst + comp, acc[c]);
+                    }
                 }
             }
         }
@@ -833,10 +874,11 @@ int launch_bwd3d(const Backward3DArgs& a, const BwdLayout& L, cudaStream_t strea
 // larger per-pixel state costs more in occupancy (167 registers at two
 // pixels) than the shared per-surfel work saves.
 template <bool SURF, bool PREFILTER>
-int launch_bwd3d_n(const Backward3DArgs& a, const BwdLayout& L, bool generic,
+int launch_bwd3d_n(const Backward3DArgs& a, const BwdLayout& L, int slots,
                    cudaStream_t stream) {
     constexpr int kPPT = SURF ? 1 : 2;
-    if (!generic) return launch_bwd3d<SURF, PREFILTER, 32, kPPT>(a, L, stream);
+    if (slots == 24 && !SURF && !PREFILTER) return launch_bwd3d<SURF, PREFILTER, 24, kPPT>(a, L, stream);
+    if (slots <= 32) return launch_bwd3d<SURF, PREFILTER, 32, kPPT>(a, L, stream);
     return launch_bwd3d<SURF, PREFILTER, 64, kPPT>(a, L, stream);
 }
 
@@ -928,7 +970,24 @@ extern "C" int hx_hexels3d_render_backward(
     BwdLayout L;
     const bool explicit_vd = view_model == 2 || (use_view_grads && prefilter);
     const bool generic = color_model >= 2 || view_model == 2;
-    if (!generic) {
+    const bool lite = !generic && !grad_softnesses && !explicit_vd && !grad_normals &&
+                      !abs_means2d && !prefilter && !surf;
+    int slots = generic ? 64 : 32;
+    if (lite) {
+        slots = 24;
+        L.off_cg = (color_model >= 1 && grad_color_grads) ? kLiteCg : -1;
+        L.off_cq = -1;
+        L.off_op = kLiteOp;
+        L.off_soft = -1;
+        L.off_tm = kLiteTm;
+        L.off_vd = -1;
+        L.off_n = -1;
+        L.off_ks = -1;
+        L.off_ls = -1;
+        L.off_abs = -1;
+        L.off_ctr = -1;
+        L.ncomp = kLiteComp;
+    } else if (!generic) {
         L.off_cg = (color_model >= 1 && grad_color_grads) ? kFixCg : -1;
         L.off_cq = -1;
         L.off_op = kFixOp;
@@ -973,10 +1032,10 @@ extern "C" int hx_hexels3d_render_backward(
     HX_REQUIRE(color_model < 1 || color_grads, "color_grads required for color_model >= 1");
     HX_REQUIRE(color_model < 2 || color_quads, "color_quads required for quadratic models");
     HX_REQUIRE(view_model != 2 || (specular_ks && specular_log_s), "lobe needs specular params");
-    if (surf) return prefilter ? launch_bwd3d_n<true, true>(a, L, generic, stream)
-                               : launch_bwd3d_n<true, false>(a, L, generic, stream);
-    return prefilter ? launch_bwd3d_n<false, true>(a, L, generic, stream)
-                     : launch_bwd3d_n<false, false>(a, L, generic, stream);
+    if (surf) return prefilter ? launch_bwd3d_n<true, true>(a, L, slots, stream)
+                               : launch_bwd3d_n<true, false>(a, L, slots, stream);
+    return prefilter ? launch_bwd3d_n<false, true>(a, L, slots, stream)
+                     : launch_bwd3d_n<false, false>(a, L, slots, stream);
 }
 
 extern "C" int hx_hexels3d_geometry_backward(

@@ -112,6 +112,14 @@ def test_cached_forward_backward_matches_reference(ref, cm, vm, soft, pre, cons)
     for n, a, b in zip(GRAD_NAMES, gm, gr):
         assert a.shape == b.shape, n
         assert_grad_parity(a, b, None, n)
+    # without means2d: the plain-RGB configurations take the backward's
+    # 19-component layout
+    bargs = (t[0], e, *t[1:], gc, e, e, e, e, *s, -1, pre, cons, False)
+    gm = _C.rasterize_hexels3d_backward_cached(*bargs, list(mine[2]))
+    gr = ref.rasterize_hexels3d_backward_cached(*bargs, list(theirs[2]))
+    for n, a, b in zip(GRAD_NAMES, gm, gr):
+        assert a.shape == b.shape, n
+        assert_grad_parity(a, b, None, n)
 
 
 @pytest.mark.parametrize("median", [False, True])

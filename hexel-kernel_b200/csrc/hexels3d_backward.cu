@@ -430,6 +430,8 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
     Surfel3D* s_prim = reinterpret_cast<Surfel3D*>(s_raw);
     float* s_acc = reinterpret_cast<float*>(s_raw + sizeof(Surfel3D) * kBatch);
     __shared__ int s_max_visit;
+    // per warp: the batch slots whose pixel box meets the warp's block
+    __shared__ unsigned char s_list[kThreads / 32][kBatch];
 
     // N == 32 uses the fixed slot layout (compile-time indices keep the
     // gradient vector in registers); N == 64 takes the host-computed layout
@@ -590,12 +592,24 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
         for (int t = tr; t < kBatch * L.ncomp; t += kThreads) s_acc[t] = 0.f;
         __syncthreads();
 
-        for (int idx = min(bend, warp_max) - 1; idx >= bstart; --idx) {
+        // compact the batch slots below this warp's pixels' last indices to the
+        // surfels whose box meets the warp's block: no pixel of a block a box
+        // misses blends that surfel, so nothing of the pair changes there
+        const int n_slots = min(bend, warp_max) - bstart;
+        int n_mine = 0;
+        for (int base = 0; base < n_slots; base += 32) {
+            const int t = base + lane;
+            const bool hit = t < n_slots &&
+                             (PREFILTER || !box_misses(s_prim[t].q.box, wx0, wy0, wx0 + 7,
+                                                       wy0 + kWarpRows - 1));
+            const unsigned m = __ballot_sync(0xffffffffu, hit);
+            if (hit) s_list[warp][n_mine + __popc(m & ((1u << lane) - 1u))] = (unsigned char)t;
+            n_mine += __popc(m);
+        }
+        __syncwarp();
+        for (int jj = n_mine - 1; jj >= 0; --jj) {
+            const int idx = bstart + s_list[warp][jj];
             const Surfel3D& s = s_prim[idx - bstart];
-            // no pixel of a warp block the surfel's box misses blends it, so
-            // nothing of the pair changes there (warp-uniform)
-            if (!PREFILTER && box_misses(s.q.box, wx0, wy0, wx0 + 7, wy0 + kWarpRows - 1))
-                continue;
             float acc[N];
 #pragma unroll
             for (int c = 0; c < N; ++c) acc[c] = 0.f;

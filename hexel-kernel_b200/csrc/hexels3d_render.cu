@@ -52,9 +52,15 @@ __device__ __forceinline__ void fwd_pair(const Render3DArgs& a, const Surfel3D& 
     const float sy = p.y / p.z;
     const float depth_sdf = (sx * Tw.x + sy * Tw.y) + Tw.z;
     if (depth_sdf < k3NearPlane) return;
-    int edge;
-    const float dist = hex_sdf3(sx, sy, edge);
-    const float soft = (edge == 0) ? s.s0 : ((edge == 1) ? s.s1 : s.s2);
+    float dist, soft;
+    if (a.softness_stride == 1) {  // one softness for all edges: no edge needed
+        dist = hex_sdf_value(sx, sy);
+        soft = s.s0;
+    } else {
+        int edge;
+        dist = hex_sdf3(sx, sy, edge);
+        soft = (edge == 0) ? s.s0 : ((edge == 1) ? s.s1 : s.s2);
+    }
     const float boundary = sigmoid_neg(dist, soft);
     const float alpha_raw_sdf = s.opacity * boundary;
     const float alpha_sdf = fminf(alpha_raw_sdf, 0.99f);
@@ -167,6 +173,8 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const R
     constexpr int kWarpRows = 4 * PPT;
     __shared__ Surfel3D s_prim[k3BlockSize];
     __shared__ float s_contrib[k3BlockSize];
+    // per warp: the batch slots whose pixel box meets the warp's block
+    __shared__ unsigned char s_list[kThreads / 32][k3BlockSize];
 
     const int W = a.W, H = a.H;
     const unsigned hblocks = (W + k3BlockX - 1) / k3BlockX;
@@ -276,11 +284,24 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const R
         __syncthreads();
 
         const int batch_size = min(k3BlockSize, to_do);
-        for (int j = 0; !thread_done && j < batch_size; ++j) {
+        // compact the batch to the surfels whose box meets this warp's block
+        // (every pixel of a block a box misses has alpha < 1/255)
+        int n_mine = 0;
+        if (!__all_sync(0xffffffffu, thread_done)) {
+            for (int base = 0; base < batch_size; base += 32) {
+                const int t = base + lane;
+                const bool hit = t < batch_size &&
+                                 (PREFILTER || !box_misses(s_prim[t].q.box, wx0, wy0, wx0 + 7,
+                                                           wy0 + kWarpRows - 1));
+                const unsigned m = __ballot_sync(0xffffffffu, hit);
+                if (hit) s_list[warp][n_mine + __popc(m & ((1u << lane) - 1u))] = (unsigned char)t;
+                n_mine += __popc(m);
+            }
+            __syncwarp();
+        }
+        for (int jj = 0; !thread_done && jj < n_mine; ++jj) {
+            const int j = s_list[warp][jj];
             const Surfel3D& s = s_prim[j];
-            // every pixel of a warp block the surfel's box misses has alpha < 1/255
-            if (!PREFILTER && box_misses(s.q.box, wx0, wy0, wx0 + 7, wy0 + kWarpRows - 1))
-                continue;
             bool all_done = true;
 #pragma unroll
             for (int k = 0; k < PPT; ++k) {

@@ -61,6 +61,15 @@ __device__ __forceinline__ float sigmoid_neg(const float dist, const float softn
     return 1.f / (1.f + __expf(x));
 }
 
+// Hexagon SDF max(|v|, |a u + b v|, |a u - b v|) - 1 without the edge: the
+// same value as hex_sdf3 (for surfels whose three edges share one softness).
+__device__ __forceinline__ float hex_sdf_value(const float u, const float v) {
+    constexpr float k = 1.7320508f;
+    constexpr float a = 0.5f * k;
+    constexpr float b = 0.5f;
+    return fmaxf(fmaxf(fabsf(a * u + b * v), fabsf(a * u - b * v)), fabsf(v)) - 1.f;
+}
+
 // Hexagon SDF max(|v|, |a u + b v|, |a u - b v|) - 1 and the active edge;
 // slanted edges win ties with |v|, edge 2 wins ties with edge 1.
 __device__ __forceinline__ float hex_sdf3(const float u, const float v, int& edge) {

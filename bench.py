@@ -1,21 +1,26 @@
 """Benchmark of the hexel-kernel hot path on B200: fwd+bwd Mpix/s (and frames/s).
 
-Default workload: the Image-GS 2D fit step at 2048x2048 with 100,000
-Gaussians (projection -> binning -> top-10 normalised compositing -> L2 loss
--> backward to the Gaussian parameters).  One JSON line on rank 0.
+Default workload (--config hexels3d_multiview): one training step over 64
+views of a 1,000,000-surfel 3D hexel scene at 1920x1080 -- per view:
+preprocess -> depth-ordered binning -> front-to-back compositing -> L2 loss
+against the view's target -> backward to the surfel parameters, the views'
+gradients summed.  One JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config hexels3d_multiview|hexels3d_single|imagegs_large|imagegs_small]
 
-Multi-GPU (torchrun, one rank per GPU): the image is split into horizontal
-stripes of 16-pixel tile rows, Gaussians are replicated, each rank renders
-and back-propagates its stripe and the packed per-Gaussian gradients are
-summed with one NCCL all-reduce (strong scaling: total work fixed).
+Multi-GPU (torchrun, one rank per GPU): the 64 views are dealt round-robin
+over the ranks, surfels are replicated, and the per-surfel gradients are
+summed with one NCCL all-reduce per step (strong scaling: the 64-view batch
+is fixed).  The Image-GS configurations split the image into horizontal
+stripes of 16-pixel tile rows instead.
 
-`--impl reference` times the CPU restatement of the reference's algorithm
-(the reference ships no CPU implementation) on the host's cores, on a bounded
-sample of the same workload.  When the reference's own CUDA kernels were
-built from its sources (oracle/_ref), our line also reports them timed on
-the same GPU under "ref_cuda_sm100a".
+The line also reports the single 1080p view with depth/normal outputs
+("single_view_surface"), the reference's own CUDA kernels compiled from its
+sources (oracle/_ref) timed on the same GPU and inputs ("ref_cuda_sm100a"),
+and the CPU restatement of the reference's algorithm on a bounded sample
+("cpu_baseline").  `--impl reference` times that CPU restatement alone (the
+reference ships no CPU implementation), on the host's cores.
 """
 
 from __future__ import annotations
@@ -676,16 +681,36 @@ def run_e2e_3d(w, args, world, rank, surface):
     cams = [w.cameras[v].to("cuda") for v in views]
     h2d = sum(t.numel() * t.element_size() for t in host_params + host_targets)
     bg = w.background.to("cuda")
+    # the next view's target image is copied on a side stream while the
+    # current view renders (double-buffered, as a training loop's loader would)
+    main = torch.cuda.current_stream()
+    copy_stream = torch.cuda.Stream()
+    bufs = [torch.empty(host_targets[0].shape, device="cuda") for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+
+    def prefetch(i):
+        b = i % 2
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(free[b])
+            bufs[b].copy_(host_targets[i], non_blocking=True)
+            ready[b].record(copy_stream)
 
     def one():
         params = [t.to("cuda", non_blocking=True).requires_grad_(True) for t in host_params]
         total = torch.zeros((), device="cuda")
-        for cam, ht in zip(cams, host_targets):
-            tgt = ht.to("cuda", non_blocking=True)
+        prefetch(0)
+        for i, cam in enumerate(cams):
+            if i + 1 < len(cams):
+                prefetch(i + 1)
+            b = i % 2
+            main.wait_event(ready[b])
+            tgt = bufs[b]
             out = gsplat.rasterize_hexels3d(
                 *params[:7], cam.viewmatrix, cam.projmatrix, cam.campos, bg, cam.width,
                 cam.height, cam.tan_fovx, cam.tan_fovy, w.softness, return_surface=surface)
             d = out[0] - tgt
+            free[b].record(main)  # the target is read only by the subtraction
             loss = (d * d).mean()
             if surface:
                 depth, normals = out[2], out[4]
@@ -718,7 +743,8 @@ def run_e2e_3d(w, args, world, rank, surface):
             "unit": UNIT, "ms_per_step": round(ms, 4), "steps": steps,
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
             "path": "gsplat.rasterize_hexels3d(" + ("return_surface=True" if surface else "")
-                    + ") per view + loss.backward()"}
+                    + ") per view + loss.backward(); each view's target copied from pinned "
+                    "host memory on a side stream while the previous view renders"}
 
 
 def ref_cuda_timing_3d(args, w, surface, steps=None):

@@ -127,7 +127,7 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
     const float3 Tw = {s.tw[0], s.tw[1], s.tw[2]};
     const float3 soft3 = {s.s0, s.s1, s.s2};
     HexHit h;
-    if (!hexel_hit(px, py, Tu, Tv, Tw, s.opacity, soft3, h)) return false;
+    if (!hexel_hit(px, py, Tu, Tv, Tw, s.opacity, soft3, a.softness_stride == 1, h)) return false;
     float alpha = h.alpha;
     bool use_filter = false, clamped_filter = false;
     float G = 0.f, dxf = 0.f, dyf = 0.f;

@@ -164,6 +164,8 @@ __device__ __forceinline__ float normal_sign(const float3 n, const float* vd) {
 // Ray-splat intersection of pixel (px, py) with a surfel of transform rows
 // Tu, Tv, Tw: returns false when the ray is parallel or the hit is in front
 // of the near plane; otherwise (u, v), depth, SDF, boundary weight and alpha.
+// With one_softness (all edges share soft3.x) the active edge is not
+// computed and h.edge is 0.
 struct HexHit {
     float u, v, depth, dist, soft, boundary, alpha_raw, alpha;
     int edge;
@@ -172,7 +174,7 @@ struct HexHit {
 
 __device__ __forceinline__ bool hexel_hit(const float px, const float py, const float3 Tu,
                                           const float3 Tv, const float3 Tw, const float opacity,
-                                          const float3 soft3, HexHit& h) {
+                                          const float3 soft3, const bool one_softness, HexHit& h) {
     const float3 k = {px * Tw.x - Tu.x, px * Tw.y - Tu.y, px * Tw.z - Tu.z};
     const float3 l = {py * Tw.x - Tv.x, py * Tw.y - Tv.y, py * Tw.z - Tv.z};
     const float3 p = cross3(k, l);
@@ -181,8 +183,14 @@ __device__ __forceinline__ bool hexel_hit(const float px, const float py, const 
     h.v = p.y / p.z;
     h.depth = (h.u * Tw.x + h.v * Tw.y) + Tw.z;
     if (h.depth < k3NearPlane) return false;
-    h.dist = hex_sdf3(h.u, h.v, h.edge);
-    h.soft = (h.edge == 0) ? soft3.x : ((h.edge == 1) ? soft3.y : soft3.z);
+    if (one_softness) {  // the edge only selects a softness; not needed here
+        h.dist = hex_sdf_value(h.u, h.v);
+        h.edge = 0;
+        h.soft = soft3.x;
+    } else {
+        h.dist = hex_sdf3(h.u, h.v, h.edge);
+        h.soft = (h.edge == 0) ? soft3.x : ((h.edge == 1) ? soft3.y : soft3.z);
+    }
     h.boundary = sigmoid_neg(h.dist, h.soft);
     h.alpha_raw = opacity * h.boundary;
     h.clamped = h.alpha_raw > 0.99f;

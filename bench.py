@@ -7,7 +7,8 @@ against the view's target -> backward to the surfel parameters, the views'
 gradients summed.  One JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config hexels3d_multiview|hexels3d_single|imagegs_large|imagegs_small]
+                    [--config hexels3d_multiview|hexels3d_single|imagegs_large|imagegs_small|
+                              hexels2d]
 
 Multi-GPU (torchrun, one rank per GPU): the 64 views are dealt round-robin
 over the ranks, surfels are replicated, and the per-surfel gradients are
@@ -398,6 +399,237 @@ def run_e2e(w, args, world, rank):
             "d2h_bytes_per_step": 4,
             "path": "gsplat.project_gaussians_2d_scale_rot + gsplat.rasterize_gaussians_sum"
                     "(topk_norm=True) + L2 loss + backward"}
+
+
+# ---------------------------------------------------------------------------
+# 2D image hexels (1024x1024, 50,000 hexagons, top-10 normalised compositing)
+# ---------------------------------------------------------------------------
+# Algorithmic work (FMA = 2): forward 40 FLOP per (pixel, candidate) pair,
+# backward 110 FLOP per (pixel, stored id).
+HEX2D_FWD_FLOP, HEX2D_BWD_FLOP = 40.0, 110.0
+
+
+def hexels2d_binning(w, xys, radii):
+    """The harness's binning of the hexagons (caller-chosen radii): tile
+    counts, prefix sum, sorted ids and tile bins."""
+    from gsplat.utils import bin_gaussians_fused, compute_cumulative_intersects, \
+        count_tiles_in_rows
+
+    tb = w.tile_bounds
+    nth = count_tiles_in_rows(xys, radii, tb, (0, tb[1]))
+    ni, cum = compute_cumulative_intersects(nth)
+    ids, bins = bin_gaussians_fused(w.num_points, ni, xys, radii, cum, tb)
+    return nth, ni, ids, bins
+
+
+def run_ours_hex2d(args, world, rank, local):
+    """c3: one fit step -- binning, top-10 hexagon compositing, L2 loss,
+    backward to the hexagons' parameters.  The image is small; every rank
+    runs its own replica (no collective), value = ranks x per-GPU rate."""
+    import workloads
+    from gsplat import csrc
+    from gsplat._lib import lib
+
+    w = workloads.hexels2d()
+    dev = torch.device("cuda")
+    xys, scales, rot, col, radii = (t.to(dev) for t in (w.xys, w.scales, w.rotation, w.colors,
+                                                       w.radii))
+    target = w.target.to(dev)
+    e = torch.empty(0, device=dev)
+    H, W, tb = w.height, w.width, w.tile_bounds
+    numel = H * W * 3
+    zero_hw = torch.zeros((H, W), device=dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    stage_names = ("bin", "raster_fwd", "loss", "raster_bwd")
+    stage_ms = {k: 0.0 for k in stage_names}
+    info = {}
+
+    def step(timed):
+        ev[0].record()
+        nth, ni, ids, bins = hexels2d_binning(w, xys, radii)
+        ev[1].record()
+        img, topk, ws, ent = csrc.nd_rasterize_forward_topk_norm_hexels(
+            tb, (16, 16, 1), (W, H, 1), ids, bins, xys, scales, rot, col, w.aa_kernel_size,
+            w.softness, e, e)
+        ev[2].record()
+        d = img - target
+        loss = (d * d).sum() / numel
+        v_out = d * (2.0 / numel)
+        ev[3].record()
+        grads = csrc.nd_rasterize_backward_topk_norm_hexels(
+            H, W, 16, 16, ids, bins, xys, scales, rot, col, v_out, zero_hw, zero_hw, topk,
+            w.aa_kernel_size, w.softness, e, e)
+        ev[4].record()
+        info.update(ni=ni, bins=bins, topk=topk)
+        return loss, grads
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    counts = (info["bins"][:, 1] - info["bins"][:, 0]).to(torch.int64).cpu()
+    tx, ty, _ = tb
+    t_idx = torch.arange(tx * ty)
+    px_in_tile = (torch.clamp(H - (t_idx // tx) * 16, max=16) *
+                  torch.clamp(W - (t_idx % tx) * 16, max=16))
+    pairs = int((counts * px_in_tile).sum())
+    stored = int((info["topk"] >= 0).sum())
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    clocks = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    launches0 = lib.dll.hx_launch_count()
+    total = 0.0
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(args.steps):
+        flush.zero_()
+        st.record()
+        step(True)
+        en.record()
+        torch.cuda.synchronize()
+        total += st.elapsed_time(en)
+        for i, k in enumerate(stage_names):
+            stage_ms[k] += ev[i].elapsed_time(ev[i + 1])
+    launches = lib.dll.hx_launch_count() - launches0
+    barrier(world)
+    clk = clocks.stop()
+    ms = max_over_ranks(total / args.steps, world)
+    stages = {k: round(max_over_ranks(v / args.steps, world), 4) for k, v in stage_ms.items()}
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    fp32_peak = NUM_SMS * FP32_LANES_PER_SM * 2 * peaks["sm_max_mhz"] * 1e6 / 1e12
+    bwd = stored * HEX2D_BWD_FLOP / (stages["raster_bwd"] / 1e3) / 1e12
+    fwd = pairs * HEX2D_FWD_FLOP / (stages["raster_fwd"] / 1e3) / 1e12
+    line = {
+        "metric": METRIC, "value": round(world * H * W / 1e6 / (ms / 1e3), 3), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "frames_per_s": round(world * 1e3 / ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; the reference publishes no dataset)",
+        "config": {"workload": w.name, "height": H, "width": W, "num_hexagons": w.num_points,
+                   "top_k": 10, "tile": 16, "softness": w.softness,
+                   "num_intersects": int(info["ni"]),
+                   "parallelism": f"{world} independent replicas" if world > 1 else "single GPU",
+                   "l2": "flushed between timed steps (256 MB write)"},
+        "stages_ms": stages,
+        "roofline": {"kernel": "hexel_fwd_kernel / hexel_bwd_kernel", "bound": "fp32",
+                     "achieved": round(fwd, 3), "peak": round(fp32_peak, 2), "unit": "TFLOP/s",
+                     "frac": round(fwd / fp32_peak, 4), "traffic": None,
+                     "work": f"forward {pairs} (pixel, candidate) pairs x {HEX2D_FWD_FLOP:.0f} "
+                             f"FLOP; backward {stored} stored ids x {HEX2D_BWD_FLOP:.0f} FLOP",
+                     "backward": {"achieved": round(bwd, 3), "frac": round(bwd / fp32_peak, 4)}},
+        "gpu_launches": int(launches), "clocks": clk, "e2e": None,
+    }
+    if world == 1 and not args.skip_extras:
+        threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(threads)
+        crop = args.cpu_crop_tiles
+        secs, mpix = cpu_sample_run_hex2d(w, crop)
+        line["cpu_baseline"] = {
+            "value": round(mpix / secs, 5), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"one fwd+bwd over a {crop}x{crop}-tile ({mpix:.4f} Mpix) centre crop of "
+                      f"{w.name}: binning of the crop's rows, top-10 hexagon compositing and "
+                      f"backward; {secs:.2f} s", "seconds": round(secs, 3)}
+        ref = ref_cuda_timing_hex2d(args, w)
+        if ref is not None:
+            line["ref_cuda_sm100a"] = ref
+    return line
+
+
+def cpu_sample_run_hex2d(w, crop_tiles: int):
+    """One fwd+bwd of the oracle (2D hexels) over a crop_tiles x crop_tiles
+    tile crop at the image centre; returns (seconds, megapixels)."""
+    import numpy as np
+
+    from oracle import hexels2d as oh
+    from oracle import raster2d as o
+
+    tx, ty, _ = w.tile_bounds
+    x0 = max(0, tx // 2 - crop_tiles // 2)
+    y0 = max(0, ty // 2 - crop_tiles // 2)
+    xs = np.arange(x0, min(tx, x0 + crop_tiles))
+    ys = np.arange(y0, min(ty, y0 + crop_tiles))
+    tiles = (ys[:, None] * tx + xs[None, :]).reshape(-1)
+    t0 = time.perf_counter()
+    keys, ids = o.map_intersects(w.xys.numpy(), w.radii.numpy(), None, w.tile_bounds,
+                                 tile_rows=(int(ys[0]), int(ys[-1]) + 1))
+    _, ids_sorted, bins = o.sort_and_bin(keys, ids.astype(np.int32), tx * ty)
+    p = oh.HexParams(xys=w.xys, colors=w.colors, softness=w.softness, aa=w.aa_kernel_size)
+    p.scales, p.rotation = w.scales, w.rotation
+    img, topk, _, _ = oh.forward(p, torch.from_numpy(ids_sorted), bins, w.height, w.width,
+                                 tile_ids=tiles)
+    rows = slice(int(ys[0]) * 16, min((int(ys[-1]) + 1) * 16, w.height))
+    cols = slice(int(xs[0]) * 16, min((int(xs[-1]) + 1) * 16, w.width))
+    v_img = torch.zeros_like(img)
+    v_img[rows, cols] = 2.0 * (img[rows, cols] - w.target[rows, cols]) / img.numel()
+    topk_crop = torch.full_like(topk, -1)
+    topk_crop[rows, cols] = topk[rows, cols]
+    zero = torch.zeros((w.height, w.width))
+    oh.backward(p, v_img, zero, zero, topk_crop, w.height, w.width)
+    secs = time.perf_counter() - t0
+    return secs, (rows.stop - rows.start) * (cols.stop - cols.start) / 1e6
+
+
+def ref_cuda_timing_hex2d(args, w):
+    """The reference's 2D hexel kernels (compiled from its sources) on the same
+    inputs, with its own binning sequence (map_gaussian_to_intersects,
+    torch.sort, get_tile_bin_edges; gsplat/utils.py:118-162) on the same tile
+    counts."""
+    path = os.path.join(ROOT, "oracle", "_ref", "_ref_gsplat_csrc.so")
+    if not os.path.exists(path):
+        return None
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_ref_gsplat_csrc", path)
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    from gsplat.utils import count_tiles_in_rows
+
+    dev = torch.device("cuda")
+    xys, scales, rot, col, radii = (t.to(dev) for t in (w.xys, w.scales, w.rotation, w.colors,
+                                                       w.radii))
+    target = w.target.to(dev)
+    e = torch.empty(0, device=dev)
+    H, W, tb, n = w.height, w.width, w.tile_bounds, w.num_points
+    numel = H * W * 3
+    zero_hw = torch.zeros((H, W), device=dev)
+    nth = count_tiles_in_rows(xys, radii, tb, (0, tb[1]))
+
+    def step():
+        cum = torch.cumsum(nth, dim=0, dtype=torch.int32)
+        ni = int(cum[-1].item())
+        isect, gids = ref.map_gaussian_to_intersects(n, ni, xys, radii, cum, tb)
+        isect_s, order = torch.sort(isect)
+        gids_s = torch.gather(gids, 0, order)
+        bins = ref.get_tile_bin_edges(ni, tb[0] * tb[1], isect_s)
+        img, topk, ws, ent = ref.nd_rasterize_forward_topk_norm_hexels(
+            tb, (16, 16, 1), (W, H, 1), gids_s, bins, xys, scales, rot, col, w.aa_kernel_size,
+            w.softness, e, e)
+        d = img - target
+        v_out = d * (2.0 / numel)
+        ref.nd_rasterize_backward_topk_norm_hexels(H, W, 16, 16, gids_s, bins, xys, scales, rot,
+                                                   col, v_out, zero_hw, zero_hw, topk,
+                                                   w.aa_kernel_size, w.softness, e, e)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    total = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        st.record()
+        step()
+        en.record()
+        torch.cuda.synchronize()
+        total += st.elapsed_time(en)
+    ms = total / args.steps
+    return {"value": round(H * W / 1e6 / (ms / 1e3), 3), "unit": UNIT,
+            "ms_per_step": round(ms, 4), "steps": args.steps,
+            "what": "reference CUDA kernels compiled from its sources for sm_100a "
+                    "(-O3 --use_fast_math), its own binning sequence, same inputs and loss"}
 
 
 # ---------------------------------------------------------------------------
@@ -931,6 +1163,12 @@ def run_reference(args, world, rank):
                   "width": cam.width, "num_surfels": w.num_points,
                   "outputs": "rgb + depth + alpha + normal + distortion"
                   if args.config == "hexels3d_single" else "rgb"}
+    elif args.config == "hexels2d":
+        w = workloads.hexels2d()
+        crop = max(1, min(args.cpu_crop_tiles, w.tile_bounds[0]))
+        sample = lambda: cpu_sample_run_hex2d(w, crop)  # noqa: E731
+        config = {"workload": w.name, "height": w.height, "width": w.width,
+                  "num_hexagons": w.num_points, "top_k": 10, "tile": 16}
     else:
         w = getattr(workloads, args.config)()
         crop = max(1, min(args.cpu_crop_tiles, w.tile_bounds[0]))
@@ -1028,7 +1266,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="hexels3d_multiview",
                     choices=["hexels3d_multiview", "hexels3d_single", "imagegs_large",
-                             "imagegs_small"])
+                             "imagegs_small", "hexels2d"])
     ap.add_argument("--cpu-crop-tiles", type=int, default=16)
     ap.add_argument("--cpu-crop-tiles-3d", type=int, default=8)
     ap.add_argument("--ref-max-steps", type=int, default=3)
@@ -1052,6 +1290,8 @@ def main():
     try:
         if args.config.startswith("hexels3d"):
             line = run_ours_3d(args, world, rank, local)
+        elif args.config == "hexels2d":
+            line = run_ours_hex2d(args, world, rank, local)
         else:
             line = run_ours(args, world, rank, local)
         if line is not None:

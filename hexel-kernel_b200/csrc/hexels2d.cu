@@ -12,9 +12,10 @@
 //     softness triplet) are computed once per primitive while staging the
 //     batch into shared memory;
 //   * one templated kernel serves all variants;
-//   * the backward accumulates per-primitive partials in a shared-memory hash
-//     table and flushes one global atomic per (primitive, component) per tile
-//     instead of up to ~20 global atomics per (pixel, primitive).
+//   * the backward sums each parameter's partials over the lanes of a warp
+//     that hold the same hexagon (a binary tree of shuffles) and adds one
+//     global atomic per (warp, hexagon, component) instead of one per
+//     (pixel, hexagon, component).
 #include "hx_common.cuh"
 
 namespace hx {
@@ -373,62 +374,80 @@ struct HexBwdArgs {
     float* v_emission;
     float* v_sharpness;
     float* v_softnesses;
-    // shared-memory table layout (component offsets within a slot; -1 = absent)
-    int ncomp, off_col, off_cg, off_em, off_sh, off_soft, table_cap;
 };
 
 namespace {
 
-struct Table {
-    int* keys;
-    float* acc;
-    int cap;
-    int ncomp;
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// Binary summation tree over the lanes of a warp that hold the same key, in
+// lane order: at level l every remaining lane adds the value of the next
+// remaining lane above it, then the lanes of odd rank at that level drop out.
+// After the last level the lowest lane of each key group holds the group's
+// sum.  The tree depends on the keys only, so it is built once per stored id
+// and reused for every gradient component.
+struct KeyTree {
+    int src[5];     // lane read at each level (own lane when nothing is added)
+    unsigned add;   // bit l: this lane adds at level l
+    int levels;     // warp-uniform
+    bool first;     // lowest lane of its key group
 };
 
-__device__ __forceinline__ int table_find(const Table& t, int g) {
-    if (t.cap == 0) return -1;
-    const unsigned mask = (unsigned)t.cap - 1u;
-    const unsigned h = ((unsigned)g * 2654435761u) & mask;
-    volatile int* keys = t.keys;
-#pragma unroll 1
-    for (int probe = 0; probe < 32; ++probe) {
-        const unsigned s = (h + probe) & mask;
-        const int k = keys[s];
-        if (k == g) return (int)s;
-        if (k == -1) {
-            const int prev = atomicCAS(t.keys + s, -1, g);
-            if (prev == -1 || prev == g) return (int)s;
+__device__ __forceinline__ KeyTree key_tree(unsigned lane, int key) {
+    KeyTree t;
+    const unsigned peers = __match_any_sync(kFullMask, key);
+    const unsigned below = (1u << lane) - 1u;
+    unsigned rank = __popc(peers & below);
+    unsigned above = peers & ~below & ~(1u << lane);
+    t.first = rank == 0u;
+    t.add = 0u;
+    t.levels = 0;
+#pragma unroll
+    for (int l = 0; l < 5; ++l) {
+        t.src[l] = (int)lane;
+        if (!__any_sync(kFullMask, above != 0u)) break;
+        const int next = __ffs(above);
+        if (next) {
+            t.src[l] = next - 1;
+            t.add |= 1u << l;
         }
+        above &= ~__ballot_sync(kFullMask, rank & 1u);
+        rank >>= 1;
+        t.levels = l + 1;
     }
-    return -1;
+    return t;
 }
 
-// Adds `v` to component `comp` of slot `slot`, or to global `*gptr` when the
-// primitive has no slot.
-__device__ __forceinline__ void acc_add(const Table& t, int slot, int comp, float* gptr, float v) {
-    if (slot >= 0)
-        atomicAdd(t.acc + slot * t.ncomp + comp, v);
-    else
-        atomicAdd(gptr, v);
+__device__ __forceinline__ float key_sum(const KeyTree& t, float x) {
+#pragma unroll
+    for (int l = 0; l < 5; ++l) {
+        if (l >= t.levels) break;
+        const float y = __shfl_sync(kFullMask, x, t.src[l]);
+        if ((t.add >> l) & 1u) x += y;
+    }
+    return x;
+}
+
+// Sums `v` over the key group; its lowest lane adds the sum to `*dst`.
+// Every lane of the warp calls this with the same arguments but `v`/`dst`.
+__device__ __forceinline__ void group_add(const KeyTree& t, bool lead, float* dst, float v) {
+    const float s = key_sum(t, v);
+    if (lead && s != 0.f) atomicAdd(dst, s);
 }
 
 }  // namespace
 
+// One thread per pixel over 16x16 tiles.  Pass 1 recomputes the stored ids'
+// weights and the normalisation gradient of every slot; pass 2 computes each
+// slot's partials for every parameter, sums them over the lanes of the warp
+// that hold the same id (KeyTree) and adds each group's sum with one global
+// atomic.  Every lane of a warp runs both passes (pixels outside the image or
+// with no stored id contribute zeros) so that the warp-wide sums stay
+// converged.
 template <bool AFFINE, bool CGRAD>
 __global__ void __launch_bounds__(256) hexel_bwd_kernel(const HexBwdArgs a) {
-    extern __shared__ __align__(16) unsigned char s_raw[];
-    Table tab;
-    tab.cap = a.table_cap;
-    tab.ncomp = a.ncomp;
-    tab.keys = reinterpret_cast<int*>(s_raw);
-    tab.acc = reinterpret_cast<float*>(s_raw + sizeof(int) * a.table_cap);
-    const int tid = threadIdx.y * kBlockX + threadIdx.x;
-    for (int s = tid; s < tab.cap; s += kBlockSize) tab.keys[s] = -1;
-    for (int s = tid; s < tab.cap * tab.ncomp; s += kBlockSize) tab.acc[s] = 0.f;
-    __syncthreads();
-
     const int C = a.channels;
+    const unsigned lane = (threadIdx.y * kBlockX + threadIdx.x) & 31u;
     const unsigned i = blockIdx.y * kBlockY + threadIdx.y;
     const unsigned j = blockIdx.x * kBlockX + threadIdx.x;
     const float px = (float)j;
@@ -439,144 +458,124 @@ __global__ void __launch_bounds__(256) hexel_bwd_kernel(const HexBwdArgs a) {
     // Mirrors the reference's early exits: outside pixels and pixels whose
     // first slot is empty contribute nothing.
     const bool active = inside && topk[0] >= 0;
+    const float* v_out = a.v_output + C * pix_id;
 
-    if (active) {
-        const float* v_out = a.v_output + C * pix_id;
-        int ids[kTopK];
-        int slots[kTopK];
-        float d_local[kTopK], u_coord[kTopK], v_coord[kTopK], prim_peak[kTopK];
-        float v_peak_emit[kTopK], v_d_local[kTopK];
-        float denom = (float)kEpsHex;
+    int ids[kTopK];
+    float d_local[kTopK], u_coord[kTopK], v_coord[kTopK], prim_peak[kTopK];
+    float v_peak_emit[kTopK], v_d_local[kTopK];
+    float denom = (float)kEpsHex;
 #pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            int g = topk[k];
-            if (g >= a.num_points) g = -1;
-            ids[k] = g;
-            slots[k] = -1;
-            d_local[k] = u_coord[k] = v_coord[k] = prim_peak[k] = v_peak_emit[k] = 0.f;
-            v_d_local[k] = 0.f;
-            if (g < 0) continue;
-            const HexPrim p = make_prim<AFFINE>(g, a.xys, a.scales, a.rotation, a.affines, a.aa,
-                                                a.softnesses, a.softness_stride,
-                                                a.softness_default, a.sharpness);
-            const HexLocal l = hex_local<AFFINE>(p, p.x - px, p.y - py);
-            int edge;
-            const float dist = hex_sdf(l.u, l.v, edge);
-            const float sig = sigmoid_neg_dist(dist, edge_softness(p, edge));
-            float alpha = sig;
-            if (p.sharp > 0.f) {
-                const float r2 = l.u * l.u + l.v * l.v;
-                const float pk = __expf(-p.sharp * r2);
-                prim_peak[k] = pk;
-                alpha *= pk;
-            }
-            denom += alpha;
-            d_local[k] = alpha;
-            u_coord[k] = l.u;
-            v_coord[k] = l.v;
+    for (int k = 0; k < kTopK; ++k) {
+        int g = active ? topk[k] : -1;
+        if (g >= a.num_points) g = -1;
+        ids[k] = g;
+        d_local[k] = u_coord[k] = v_coord[k] = prim_peak[k] = v_peak_emit[k] = 0.f;
+        v_d_local[k] = 0.f;
+        if (g < 0) continue;
+        const HexPrim p = make_prim<AFFINE>(g, a.xys, a.scales, a.rotation, a.affines, a.aa,
+                                            a.softnesses, a.softness_stride,
+                                            a.softness_default, a.sharpness);
+        const HexLocal l = hex_local<AFFINE>(p, p.x - px, p.y - py);
+        int edge;
+        const float dist = hex_sdf(l.u, l.v, edge);
+        const float sig = sigmoid_neg_dist(dist, edge_softness(p, edge));
+        float alpha = sig;
+        if (p.sharp > 0.f) {
+            const float r2 = l.u * l.u + l.v * l.v;
+            const float pk = __expf(-p.sharp * r2);
+            prim_peak[k] = pk;
+            alpha *= pk;
         }
+        denom += alpha;
+        d_local[k] = alpha;
+        u_coord[k] = l.u;
+        v_coord[k] = l.v;
+    }
 
-        float v_d_sum = 0.f;
+    // pass 1: gradient of each slot's normalised weight
+    float v_d_sum = 0.f;
 #pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            const int g = ids[k];
-            if (g < 0) continue;
-            const int slot = table_find(tab, g);
-            slots[k] = slot;
-            const float alpha = d_local[k];
-            const float norm_d = alpha / denom;
-            float v_norm_d = 0.f;
-            float dx = 0.f, dy = 0.f;
+    for (int k = 0; k < kTopK; ++k) {
+        const int g = ids[k];
+        if (g < 0) continue;
+        float v_norm_d = 0.f;
+        float dx = 0.f, dy = 0.f;
+        if (CGRAD) {
+            const float2 xy = a.xys[g];
+            dx = xy.x - px;
+            dy = xy.y - py;
+        }
+        for (int c = 0; c < C; ++c) {
+            const float vo = v_out[c];
             if (CGRAD) {
-                const float2 xy = a.xys[g];
-                dx = xy.x - px;
-                dy = xy.y - py;
+                const float base = a.colors[C * g + c];
+                const float gx = a.color_grads[(g * 2 + 0) * C + c];
+                const float gy = a.color_grads[(g * 2 + 1) * C + c];
+                const float color = base + a.color_grad_scale * (dx * gx + dy * gy);
+                v_norm_d += color * vo;
+            } else {
+                v_norm_d += a.colors[C * g + c] * vo;
             }
-            for (int c = 0; c < C; ++c) {
-                const float vo = v_out[c];
-                if (CGRAD) {
-                    const float base = a.colors[C * g + c];
-                    const float gx = a.color_grads[(g * 2 + 0) * C + c];
-                    const float gy = a.color_grads[(g * 2 + 1) * C + c];
-                    const float color = base + a.color_grad_scale * (dx * gx + dy * gy);
-                    acc_add(tab, slot, a.off_col + c, a.v_colors + C * g + c, norm_d * vo);
-                    acc_add(tab, slot, a.off_cg + c, a.v_color_grads + (g * 2 + 0) * C + c,
-                            norm_d * vo * a.color_grad_scale * dx);
-                    acc_add(tab, slot, a.off_cg + C + c, a.v_color_grads + (g * 2 + 1) * C + c,
-                            norm_d * vo * a.color_grad_scale * dy);
-                    v_norm_d += color * vo;
-                } else {
-                    acc_add(tab, slot, a.off_col + c, a.v_colors + C * g + c, norm_d * vo);
-                    v_norm_d += a.colors[C * g + c] * vo;
-                }
-            }
-            if (a.emission && a.v_emission) {
-                const float peak = prim_peak[k];
-                if (peak > 0.f) {
-                    float vpe = 0.f;
-                    for (int c = 0; c < C; ++c) {
-                        acc_add(tab, slot, a.off_em + c, a.v_emission + C * g + c,
-                                peak * v_out[c]);
-                        vpe += a.emission[C * g + c] * v_out[c];
-                    }
-                    v_peak_emit[k] = vpe;
-                }
-            }
-            if (CGRAD) {
-                float vdx = 0.f, vdy = 0.f;
-                for (int c = 0; c < C; ++c) {
-                    const float gx = a.color_grads[(g * 2 + 0) * C + c];
-                    const float gy = a.color_grads[(g * 2 + 1) * C + c];
-                    vdx += norm_d * v_out[c] * a.color_grad_scale * gx;
-                    vdy += norm_d * v_out[c] * a.color_grad_scale * gy;
-                }
-                acc_add(tab, slot, 0, a.v_xy + 2 * g + 0, vdx);
-                acc_add(tab, slot, 1, a.v_xy + 2 * g + 1, vdy);
-            }
-            v_d_local[k] = v_norm_d / denom;
-            v_d_sum += -alpha / (denom * denom) * v_norm_d;
         }
+        if (a.emission && a.v_emission && prim_peak[k] > 0.f) {
+            float vpe = 0.f;
+            for (int c = 0; c < C; ++c) vpe += a.emission[C * g + c] * v_out[c];
+            v_peak_emit[k] = vpe;
+        }
+        v_d_local[k] = v_norm_d / denom;
+        v_d_sum += -d_local[k] / (denom * denom) * v_norm_d;
+    }
 #pragma unroll
-        for (int k = 0; k < kTopK; ++k) v_d_local[k] += v_d_sum;
+    for (int k = 0; k < kTopK; ++k) v_d_local[k] += v_d_sum;
 
-        const float v_ws = a.v_weights_sum ? a.v_weights_sum[pix_id] : 0.f;
-        const float v_ent = a.v_entropy ? a.v_entropy[pix_id] : 0.f;
-        if (v_ws != 0.f) {
+    const float v_ws = (active && a.v_weights_sum) ? a.v_weights_sum[pix_id] : 0.f;
+    const float v_ent = (active && a.v_entropy) ? a.v_entropy[pix_id] : 0.f;
+    if (v_ws != 0.f) {
 #pragma unroll
-            for (int k = 0; k < kTopK; ++k)
-                if (ids[k] >= 0) v_d_local[k] += v_ws;
-        }
-        if (v_ent != 0.f) {
-            float dHdp[kTopK];
-            float avg = 0.f;
-#pragma unroll
-            for (int k = 0; k < kTopK; ++k) {
-                dHdp[k] = 0.f;
-                if (ids[k] < 0) continue;
-                const float p = d_local[k] / denom;
-                const float dhdp = -(logf(p + kEntropyEps) + 1.f);
-                dHdp[k] = dhdp;
-                avg += p * dhdp;
-            }
-#pragma unroll
-            for (int k = 0; k < kTopK; ++k) {
-                if (ids[k] < 0) continue;
-                const float dhdw = (dHdp[k] - avg) / denom;
-                v_d_local[k] += v_ent * dhdw;
-            }
-        }
-
+        for (int k = 0; k < kTopK; ++k)
+            if (ids[k] >= 0) v_d_local[k] += v_ws;
+    }
+    if (v_ent != 0.f) {
+        float dHdp[kTopK];
+        float avg = 0.f;
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) {
-            const int g = ids[k];
-            if (g < 0) continue;
-            const int slot = slots[k];
+            dHdp[k] = 0.f;
+            if (ids[k] < 0) continue;
+            const float p = d_local[k] / denom;
+            const float dhdp = -(logf(p + kEntropyEps) + 1.f);
+            dHdp[k] = dhdp;
+            avg += p * dhdp;
+        }
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            if (ids[k] < 0) continue;
+            const float dhdw = (dHdp[k] - avg) / denom;
+            v_d_local[k] += v_ent * dhdw;
+        }
+    }
+
+    // pass 2: per-parameter partials of every slot, summed per id over the warp
+    const bool with_sharp = a.sharpness != nullptr && a.v_sharpness != nullptr;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        const int g = ids[k];
+        const bool valid = g >= 0;
+        const KeyTree t = key_tree(lane, g);
+        const bool lead = t.first && valid;
+        const int gs = valid ? g : 0;  // a safe index for lanes without an id
+        float geo[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float v_sharp = 0.f, v_soft = 0.f, norm_d = 0.f, dx = 0.f, dy = 0.f;
+        int edge = 0;
+        if (valid) {
             const HexPrim p = make_prim<AFFINE>(g, a.xys, a.scales, a.rotation, a.affines, a.aa,
                                                 a.softnesses, a.softness_stride,
                                                 a.softness_default, a.sharpness);
             const float2 delta = {p.x - px, p.y - py};
+            dx = delta.x;
+            dy = delta.y;
+            norm_d = d_local[k] / denom;
             const HexLocal l = hex_local<AFFINE>(p, delta.x, delta.y);
-            int edge;
             const float dist = hex_sdf(l.u, l.v, edge);
             // SDF partials w.r.t. (u, v); |.| has subgradient sign(0) = 0
             // (hexels_backward.cu:15-18, 100-128).
@@ -606,16 +605,9 @@ __global__ void __launch_bounds__(256) hexel_bwd_kernel(const HexBwdArgs a) {
                 const float v_r2 = v_peak * peak * (-p.sharp);
                 v_u_peak = v_r2 * 2.f * u_coord[k];
                 v_v_peak = v_r2 * 2.f * v_coord[k];
-                if (a.v_sharpness) acc_add(tab, slot, a.off_sh, a.v_sharpness + g,
-                                           v_peak * peak * (-r2));
+                v_sharp = v_peak * peak * (-r2);
             }
-            if (a.v_softnesses) {
-                const float v_soft = v_sig * (-dist) * sig * (1.f - sig);
-                if (a.softness_stride == 3)
-                    acc_add(tab, slot, a.off_soft + edge, a.v_softnesses + g * 3 + edge, v_soft);
-                else if (a.softness_stride == 1)
-                    acc_add(tab, slot, a.off_soft, a.v_softnesses + g, v_soft);
-            }
+            v_soft = v_sig * (-dist) * sig * (1.f - sig);
             const float v_dist = v_sig * (-soft) * sig * (1.f - sig);
             float v_u = v_dist * du;
             float v_v = v_dist * dv;
@@ -626,10 +618,8 @@ __global__ void __launch_bounds__(256) hexel_bwd_kernel(const HexBwdArgs a) {
             const float v_s_u = v_u * l.u_base;
             const float v_s_v = v_v * l.v_base;
             if (AFFINE) {
-                const float v_dx = v_u_base * p.g0 + v_v_base * p.g1;
-                const float v_dy = v_u_base * p.g2 + v_v_base * p.g3;
-                acc_add(tab, slot, 0, a.v_xy + 2 * g + 0, v_dx);
-                acc_add(tab, slot, 1, a.v_xy + 2 * g + 1, v_dy);
+                geo[0] = v_u_base * p.g0 + v_v_base * p.g1;
+                geo[1] = v_u_base * p.g2 + v_v_base * p.g3;
                 float v_a00 = delta.x * v_u_base;
                 float v_a01 = delta.x * v_v_base;
                 float v_a10 = delta.y * v_u_base;
@@ -642,10 +632,10 @@ __global__ void __launch_bounds__(256) hexel_bwd_kernel(const HexBwdArgs a) {
                     v_a01 += v_s_v * (-a.aa * p.g1 * sv3);
                     v_a11 += v_s_v * (-a.aa * p.g3 * sv3);
                 }
-                acc_add(tab, slot, 2, a.v_affines + 4 * g + 0, v_a00);
-                acc_add(tab, slot, 3, a.v_affines + 4 * g + 1, v_a01);
-                acc_add(tab, slot, 4, a.v_affines + 4 * g + 2, v_a10);
-                acc_add(tab, slot, 5, a.v_affines + 4 * g + 3, v_a11);
+                geo[2] = v_a00;
+                geo[3] = v_a01;
+                geo[4] = v_a10;
+                geo[5] = v_a11;
             } else {
                 const float inv_sx = 1.f / p.g2;
                 const float inv_sy = 1.f / p.g3;
@@ -660,47 +650,54 @@ __global__ void __launch_bounds__(256) hexel_bwd_kernel(const HexBwdArgs a) {
                     v_sy += v_s_v * ds_v;
                 }
                 const float cos_t = p.g0, sin_t = p.g1;
-                const float v_dx = v_u_rot * cos_t + v_v_rot * (-sin_t);
-                const float v_dy = v_u_rot * sin_t + v_v_rot * cos_t;
-                const float v_rot_angle = v_u_rot * l.v_rot + v_v_rot * (-l.u_rot);
-                acc_add(tab, slot, 0, a.v_xy + 2 * g + 0, v_dx);
-                acc_add(tab, slot, 1, a.v_xy + 2 * g + 1, v_dy);
-                acc_add(tab, slot, 2, a.v_scale + 2 * g + 0, v_sx);
-                acc_add(tab, slot, 3, a.v_scale + 2 * g + 1, v_sy);
-                acc_add(tab, slot, 4, a.v_rot + g, v_rot_angle);
+                geo[0] = v_u_rot * cos_t + v_v_rot * (-sin_t);
+                geo[1] = v_u_rot * sin_t + v_v_rot * cos_t;
+                geo[2] = v_sx;
+                geo[3] = v_sy;
+                geo[4] = v_u_rot * l.v_rot + v_v_rot * (-l.u_rot);
             }
         }
-    }
-
-    __syncthreads();
-    // Flush: one global atomic per (primitive, non-zero component).
-    for (int s = tid; s < tab.cap; s += kBlockSize) {
-        const int g = tab.keys[s];
-        if (g < 0) continue;
-        const float* acc = tab.acc + s * tab.ncomp;
-        auto put = [&](float* dst, float v) {
-            if (v != 0.f) atomicAdd(dst, v);
-        };
-        put(a.v_xy + 2 * g + 0, acc[0]);
-        put(a.v_xy + 2 * g + 1, acc[1]);
-        if (AFFINE) {
-            for (int q = 0; q < 4; ++q) put(a.v_affines + 4 * g + q, acc[2 + q]);
-        } else {
-            put(a.v_scale + 2 * g + 0, acc[2]);
-            put(a.v_scale + 2 * g + 1, acc[3]);
-            put(a.v_rot + g, acc[4]);
+        // colours, colour gradients and their share of the centre gradient
+        for (int c = 0; c < C; ++c) {
+            const float vo = v_out[c];
+            const float w = valid ? norm_d * vo : 0.f;
+            group_add(t, lead, a.v_colors + C * gs + c, w);
+            if (CGRAD) {
+                group_add(t, lead, a.v_color_grads + (gs * 2 + 0) * C + c,
+                          w * a.color_grad_scale * dx);
+                group_add(t, lead, a.v_color_grads + (gs * 2 + 1) * C + c,
+                          w * a.color_grad_scale * dy);
+                if (valid) {
+                    geo[0] += w * a.color_grad_scale * a.color_grads[(g * 2 + 0) * C + c];
+                    geo[1] += w * a.color_grad_scale * a.color_grads[(g * 2 + 1) * C + c];
+                }
+            }
         }
-        for (int c = 0; c < C; ++c) put(a.v_colors + C * g + c, acc[a.off_col + c]);
-        if (a.off_cg >= 0)
-            for (int q = 0; q < 2 * C; ++q) put(a.v_color_grads + 2 * C * g + q, acc[a.off_cg + q]);
-        if (a.off_em >= 0)
-            for (int c = 0; c < C; ++c) put(a.v_emission + C * g + c, acc[a.off_em + c]);
-        if (a.off_sh >= 0) put(a.v_sharpness + g, acc[a.off_sh]);
-        if (a.off_soft >= 0) {
-            if (a.softness_stride == 3)
-                for (int q = 0; q < 3; ++q) put(a.v_softnesses + 3 * g + q, acc[a.off_soft + q]);
-            else
-                put(a.v_softnesses + g, acc[a.off_soft]);
+        if (a.v_emission) {
+            const float peak = prim_peak[k];
+            for (int c = 0; c < C; ++c)
+                group_add(t, lead, a.v_emission + C * gs + c,
+                          (valid && peak > 0.f) ? peak * v_out[c] : 0.f);
+        }
+        group_add(t, lead, a.v_xy + 2 * gs + 0, geo[0]);
+        group_add(t, lead, a.v_xy + 2 * gs + 1, geo[1]);
+        if (AFFINE) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) group_add(t, lead, a.v_affines + 4 * gs + q, geo[2 + q]);
+        } else {
+            group_add(t, lead, a.v_scale + 2 * gs + 0, geo[2]);
+            group_add(t, lead, a.v_scale + 2 * gs + 1, geo[3]);
+            group_add(t, lead, a.v_rot + gs, geo[4]);
+        }
+        if (with_sharp) group_add(t, lead, a.v_sharpness + gs, v_sharp);
+        if (a.v_softnesses) {
+            if (a.softness_stride == 3) {
+#pragma unroll
+                for (int q = 0; q < 3; ++q)
+                    group_add(t, lead, a.v_softnesses + 3 * gs + q, edge == q ? v_soft : 0.f);
+            } else {
+                group_add(t, lead, a.v_softnesses + gs, v_soft);
+            }
         }
     }
 }
@@ -719,24 +716,11 @@ int launch_fwd(const HexFwdArgs& a, int tiles_y, cudaStream_t stream) {
     return HX_OK;
 }
 
-constexpr int kMaxTableComp = 40;
-
 template <bool AFFINE, bool CGRAD>
-int launch_bwd(HexBwdArgs a, cudaStream_t stream) {
-    const size_t smem = sizeof(int) * a.table_cap + sizeof(float) * (size_t)a.table_cap * a.ncomp;
-    static bool attr_set[64] = {};
-    int dev = 0;
-    HX_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        HX_CUDA_TRY(cudaFuncSetAttribute(hexel_bwd_kernel<AFFINE, CGRAD>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)(sizeof(int) * 512 +
-                                               sizeof(float) * 512 * kMaxTableComp)));
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
+int launch_bwd(const HexBwdArgs& a, cudaStream_t stream) {
     dim3 grid(ceil_div((int)a.img_w, kBlockX), ceil_div((int)a.img_h, kBlockY));
     dim3 block(kBlockX, kBlockY);
-    hexel_bwd_kernel<AFFINE, CGRAD><<<grid, block, smem, stream>>>(a);
+    hexel_bwd_kernel<AFFINE, CGRAD><<<grid, block, 0, stream>>>(a);
     HX_LAUNCH_CHECK("hexel_bwd_kernel");
     return HX_OK;
 }
@@ -846,23 +830,6 @@ extern "C" int hx_hexels2d_backward(
     a.v_emission = (emission && v_emission) ? v_emission : nullptr;
     a.v_sharpness = v_sharpness;
     a.v_softnesses = (softnesses && a.softness_stride > 0) ? v_softnesses : nullptr;
-    // slot layout: geometry (5 or 6), colours, [colour gradients], [emission],
-    // [sharpness], [softness]
-    int off = affine ? 6 : 5;
-    a.off_col = off;
-    off += channels;
-    a.off_cg = cg ? off : -1;
-    off += cg ? 2 * channels : 0;
-    a.off_em = a.v_emission ? off : -1;
-    off += a.v_emission ? channels : 0;
-    a.off_sh = (sharpness && v_sharpness) ? off : -1;
-    off += (sharpness && v_sharpness) ? 1 : 0;
-    a.off_soft = a.v_softnesses ? off : -1;
-    off += a.v_softnesses ? a.softness_stride : 0;
-    a.ncomp = off;
-    a.table_cap = off <= kMaxTableComp ? 512 : 0;  // 0: accumulate straight to global
-    if (a.table_cap == 0) a.ncomp = 1;
-    if (!(sharpness && v_sharpness)) a.v_sharpness = v_sharpness;  // unused without sharpness
     if (affine) return cg ? launch_bwd<true, true>(a, stream) : launch_bwd<true, false>(a, stream);
     return cg ? launch_bwd<false, true>(a, stream) : launch_bwd<false, false>(a, stream);
 }

@@ -596,21 +596,32 @@ def ref_cuda_timing_hex2d(args, w):
     zero_hw = torch.zeros((H, W), device=dev)
     nth = count_tiles_in_rows(xys, radii, tb, (0, tb[1]))
 
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    stage_names = ("bin", "raster_fwd", "loss", "raster_bwd")
+    stage_ms = {k: 0.0 for k in stage_names}
+
     def step():
+        ev[0].record()
         cum = torch.cumsum(nth, dim=0, dtype=torch.int32)
         ni = int(cum[-1].item())
         isect, gids = ref.map_gaussian_to_intersects(n, ni, xys, radii, cum, tb)
         isect_s, order = torch.sort(isect)
         gids_s = torch.gather(gids, 0, order)
         bins = ref.get_tile_bin_edges(ni, tb[0] * tb[1], isect_s)
+        ev[1].record()
         img, topk, ws, ent = ref.nd_rasterize_forward_topk_norm_hexels(
             tb, (16, 16, 1), (W, H, 1), gids_s, bins, xys, scales, rot, col, w.aa_kernel_size,
             w.softness, e, e)
+        ev[2].record()
         d = img - target
+        loss = (d * d).sum() / numel
         v_out = d * (2.0 / numel)
+        ev[3].record()
         ref.nd_rasterize_backward_topk_norm_hexels(H, W, 16, 16, gids_s, bins, xys, scales, rot,
                                                    col, v_out, zero_hw, zero_hw, topk,
                                                    w.aa_kernel_size, w.softness, e, e)
+        ev[4].record()
+        return loss
 
     for _ in range(args.warmup):
         step()
@@ -625,9 +636,12 @@ def ref_cuda_timing_hex2d(args, w):
         en.record()
         torch.cuda.synchronize()
         total += st.elapsed_time(en)
+        for i, k in enumerate(stage_names):
+            stage_ms[k] += ev[i].elapsed_time(ev[i + 1])
     ms = total / args.steps
     return {"value": round(H * W / 1e6 / (ms / 1e3), 3), "unit": UNIT,
             "ms_per_step": round(ms, 4), "steps": args.steps,
+            "stages_ms": {k: round(v / args.steps, 4) for k, v in stage_ms.items()},
             "what": "reference CUDA kernels compiled from its sources for sm_100a "
                     "(-O3 --use_fast_math), its own binning sequence, same inputs and loss"}
 

@@ -202,13 +202,53 @@ struct HexFwdArgs {
     float* entropy;
 };
 
+// Index of the smallest of vals[lo, lo + n), the lowest index among equal
+// values, as a pairwise tree (a higher index wins only when strictly
+// smaller, which keeps the first-minimum choice of a left-to-right scan).
+template <int LO, int N>
+struct ArgMin {
+    static __device__ __forceinline__ void run(const float (&vals)[kTopK], int& idx, float& v) {
+        if constexpr (N == 1) {
+            idx = LO;
+            v = vals[LO];
+        } else {
+            int i0, i1;
+            float v0, v1;
+            ArgMin<LO, N / 2>::run(vals, i0, v0);
+            ArgMin<LO + N / 2, N - N / 2>::run(vals, i1, v1);
+            const bool right = v1 < v0;
+            idx = right ? i1 : i0;
+            v = right ? v1 : v0;
+        }
+    }
+};
+
+// Pixel (x, y) within its 16x16 tile for thread `tr`: each warp covers an 8x4
+// block, so that the lanes of a warp see similar candidate rankings.
+__device__ __forceinline__ int2 tile_pixel16(int tr) {
+    const int warp = tr >> 5, lane = tr & 31;
+    return make_int2(((warp & 1) << 3) | (lane & 7), ((warp >> 1) << 2) | (lane >> 3));
+}
+
+// One thread per pixel over 16x16 tiles; the tile's candidates are staged
+// batch by batch in shared memory and every pixel keeps the reference's
+// top-10 (hexels_forward.cu:169-337): the first ten candidates fill slots
+// 0..9 in order, after which a candidate whose weight exceeds the current
+// minimum replaces the minimum's slot (lowest slot among equal minima).  Once
+// the ten slots are full they stay full, so the reference's empty-slot test
+// in the minimum scan never fires and is left out.  Slot ids and peaks live
+// in shared memory ([slot][thread], conflict-free) so that a replacement is
+// two stores; the weights stay in registers for the minimum scan.
 template <bool AFFINE, bool CGRAD>
 __global__ void __launch_bounds__(256) hexel_fwd_kernel(const HexFwdArgs a) {
     __shared__ HexPrim s_prim[kBlockSize];
+    __shared__ int s_ids[kTopK][kBlockSize];
+    __shared__ float s_peaks[kTopK][kBlockSize];
     const int tile_id = blockIdx.y * a.tiles_x + blockIdx.x;
-    const unsigned i = blockIdx.y * kBlockY + threadIdx.y;
-    const unsigned j = blockIdx.x * kBlockX + threadIdx.x;
     const int tr = threadIdx.y * kBlockX + threadIdx.x;
+    const int2 lp = tile_pixel16(tr);
+    const unsigned i = blockIdx.y * kBlockY + lp.y;
+    const unsigned j = blockIdx.x * kBlockX + lp.x;
     const float px = (float)j;
     const float py = (float)i;
     const int pix_id = i * a.img_w + j;
@@ -229,14 +269,12 @@ __global__ void __launch_bounds__(256) hexel_fwd_kernel(const HexFwdArgs a) {
         return;
     }
 
-    int ids[kTopK];
     float vals[kTopK];
-    float peaks[kTopK];
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
-        ids[k] = -1;
         vals[k] = 0.f;
-        peaks[k] = 0.f;
+        s_ids[k][tr] = -1;
+        s_peaks[k][tr] = 0.f;
     }
     int min_id = 0;
     float min_val = -1.f;
@@ -258,38 +296,29 @@ __global__ void __launch_bounds__(256) hexel_fwd_kernel(const HexFwdArgs a) {
                 float peak;
                 const float alpha = hex_alpha<AFFINE>(p, p.x - px, p.y - py, peak);
                 if (alpha > min_val) {
+                    s_ids[min_id][tr] = p.id;
+                    s_peaks[min_id][tr] = peak;
 #pragma unroll
-                    for (int k = 0; k < kTopK; ++k) {
-                        if (k == min_id) {
-                            ids[k] = p.id;
-                            vals[k] = alpha;
-                            peaks[k] = peak;
-                        }
-                    }
+                    for (int k = 0; k < kTopK; ++k)
+                        if (k == min_id) vals[k] = alpha;
                     if (min_val < 0.f && min_id + 1 < kTopK) {
                         ++min_id;
                     } else {
-                        min_val = 1e30f;
-                        bool found_empty = false;
-#pragma unroll
-                        for (int k = 0; k < kTopK; ++k) {
-                            if (!found_empty) {
-                                if (ids[k] < 0) {
-                                    min_id = k;
-                                    min_val = -1.0f;
-                                    found_empty = true;
-                                } else if (vals[k] < min_val) {
-                                    min_id = k;
-                                    min_val = vals[k];
-                                }
-                            }
-                        }
+                        ArgMin<0, kTopK>::run(vals, min_id, min_val);
                     }
                 }
             }
         }
     }
     if (!inside) return;
+
+    int ids[kTopK];
+    float peaks[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        ids[k] = s_ids[k][tr];
+        peaks[k] = s_peaks[k][tr];
+    }
 
     float sum_val = 0.f;
 #pragma unroll
@@ -437,7 +466,7 @@ __device__ __forceinline__ void group_add(const KeyTree& t, bool lead, float* ds
 
 }  // namespace
 
-// One thread per pixel over 16x16 tiles.  Pass 1 recomputes the stored ids'
+// One thread per pixel over 16x16 tiles (8x4 pixels per warp).  Pass 1 recomputes the stored ids'
 // weights and the normalisation gradient of every slot; pass 2 computes each
 // slot's partials for every parameter, sums them over the lanes of the warp
 // that hold the same id (KeyTree) and adds each group's sum with one global
@@ -446,10 +475,15 @@ __device__ __forceinline__ void group_add(const KeyTree& t, bool lead, float* ds
 // converged.
 template <bool AFFINE, bool CGRAD>
 __global__ void __launch_bounds__(256) hexel_bwd_kernel(const HexBwdArgs a) {
+    __shared__ int s_id[kTopK][kBlockSize];
+    __shared__ float s_alpha[kTopK][kBlockSize];
+    __shared__ float s_vn[kTopK][kBlockSize];
     const int C = a.channels;
-    const unsigned lane = (threadIdx.y * kBlockX + threadIdx.x) & 31u;
-    const unsigned i = blockIdx.y * kBlockY + threadIdx.y;
-    const unsigned j = blockIdx.x * kBlockX + threadIdx.x;
+    const int tr = threadIdx.y * kBlockX + threadIdx.x;
+    const unsigned lane = tr & 31;
+    const int2 lp = tile_pixel16(tr);
+    const unsigned i = blockIdx.y * kBlockY + lp.y;
+    const unsigned j = blockIdx.x * kBlockX + lp.x;
     const float px = (float)j;
     const float py = (float)i;
     const bool inside = (i < a.img_h && j < a.img_w);
@@ -460,112 +494,67 @@ __global__ void __launch_bounds__(256) hexel_bwd_kernel(const HexBwdArgs a) {
     const bool active = inside && topk[0] >= 0;
     const float* v_out = a.v_output + C * pix_id;
 
-    int ids[kTopK];
-    float d_local[kTopK], u_coord[kTopK], v_coord[kTopK], prim_peak[kTopK];
-    float v_peak_emit[kTopK], v_d_local[kTopK];
+    // pass 1: weights of the stored ids, their sum, and the gradient of each
+    // slot's normalised weight before normalisation (sum_c colour * v_out)
     float denom = (float)kEpsHex;
-#pragma unroll
+#pragma unroll 1
     for (int k = 0; k < kTopK; ++k) {
         int g = active ? topk[k] : -1;
         if (g >= a.num_points) g = -1;
-        ids[k] = g;
-        d_local[k] = u_coord[k] = v_coord[k] = prim_peak[k] = v_peak_emit[k] = 0.f;
-        v_d_local[k] = 0.f;
-        if (g < 0) continue;
-        const HexPrim p = make_prim<AFFINE>(g, a.xys, a.scales, a.rotation, a.affines, a.aa,
-                                            a.softnesses, a.softness_stride,
-                                            a.softness_default, a.sharpness);
-        const HexLocal l = hex_local<AFFINE>(p, p.x - px, p.y - py);
-        int edge;
-        const float dist = hex_sdf(l.u, l.v, edge);
-        const float sig = sigmoid_neg_dist(dist, edge_softness(p, edge));
-        float alpha = sig;
-        if (p.sharp > 0.f) {
-            const float r2 = l.u * l.u + l.v * l.v;
-            const float pk = __expf(-p.sharp * r2);
-            prim_peak[k] = pk;
-            alpha *= pk;
-        }
-        denom += alpha;
-        d_local[k] = alpha;
-        u_coord[k] = l.u;
-        v_coord[k] = l.v;
-    }
-
-    // pass 1: gradient of each slot's normalised weight
-    float v_d_sum = 0.f;
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-        const int g = ids[k];
-        if (g < 0) continue;
-        float v_norm_d = 0.f;
-        float dx = 0.f, dy = 0.f;
-        if (CGRAD) {
-            const float2 xy = a.xys[g];
-            dx = xy.x - px;
-            dy = xy.y - py;
-        }
-        for (int c = 0; c < C; ++c) {
-            const float vo = v_out[c];
-            if (CGRAD) {
-                const float base = a.colors[C * g + c];
-                const float gx = a.color_grads[(g * 2 + 0) * C + c];
-                const float gy = a.color_grads[(g * 2 + 1) * C + c];
-                const float color = base + a.color_grad_scale * (dx * gx + dy * gy);
-                v_norm_d += color * vo;
-            } else {
-                v_norm_d += a.colors[C * g + c] * vo;
+        float alpha = 0.f, v_norm_d = 0.f;
+        if (g >= 0) {
+            const HexPrim p = make_prim<AFFINE>(g, a.xys, a.scales, a.rotation, a.affines, a.aa,
+                                                a.softnesses, a.softness_stride,
+                                                a.softness_default, a.sharpness);
+            float peak;
+            alpha = hex_alpha<AFFINE>(p, p.x - px, p.y - py, peak);
+            denom += alpha;
+            const float dx = p.x - px, dy = p.y - py;
+            for (int c = 0; c < C; ++c) {
+                const float vo = v_out[c];
+                if (CGRAD) {
+                    const float base = a.colors[C * g + c];
+                    const float gx = a.color_grads[(g * 2 + 0) * C + c];
+                    const float gy = a.color_grads[(g * 2 + 1) * C + c];
+                    const float color = base + a.color_grad_scale * (dx * gx + dy * gy);
+                    v_norm_d += color * vo;
+                } else {
+                    v_norm_d += a.colors[C * g + c] * vo;
+                }
             }
         }
-        if (a.emission && a.v_emission && prim_peak[k] > 0.f) {
-            float vpe = 0.f;
-            for (int c = 0; c < C; ++c) vpe += a.emission[C * g + c] * v_out[c];
-            v_peak_emit[k] = vpe;
-        }
-        v_d_local[k] = v_norm_d / denom;
-        v_d_sum += -d_local[k] / (denom * denom) * v_norm_d;
+        s_id[k][tr] = g;
+        s_alpha[k][tr] = alpha;
+        s_vn[k][tr] = v_norm_d;
     }
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) v_d_local[k] += v_d_sum;
+    float v_d_sum = 0.f;
+#pragma unroll 1
+    for (int k = 0; k < kTopK; ++k)
+        if (s_id[k][tr] >= 0) v_d_sum += -s_alpha[k][tr] / (denom * denom) * s_vn[k][tr];
 
     const float v_ws = (active && a.v_weights_sum) ? a.v_weights_sum[pix_id] : 0.f;
     const float v_ent = (active && a.v_entropy) ? a.v_entropy[pix_id] : 0.f;
-    if (v_ws != 0.f) {
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k)
-            if (ids[k] >= 0) v_d_local[k] += v_ws;
-    }
+    float ent_avg = 0.f;
     if (v_ent != 0.f) {
-        float dHdp[kTopK];
-        float avg = 0.f;
-#pragma unroll
+#pragma unroll 1
         for (int k = 0; k < kTopK; ++k) {
-            dHdp[k] = 0.f;
-            if (ids[k] < 0) continue;
-            const float p = d_local[k] / denom;
-            const float dhdp = -(logf(p + kEntropyEps) + 1.f);
-            dHdp[k] = dhdp;
-            avg += p * dhdp;
-        }
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            if (ids[k] < 0) continue;
-            const float dhdw = (dHdp[k] - avg) / denom;
-            v_d_local[k] += v_ent * dhdw;
+            if (s_id[k][tr] < 0) continue;
+            const float p = s_alpha[k][tr] / denom;
+            ent_avg += p * -(logf(p + kEntropyEps) + 1.f);
         }
     }
 
     // pass 2: per-parameter partials of every slot, summed per id over the warp
     const bool with_sharp = a.sharpness != nullptr && a.v_sharpness != nullptr;
-#pragma unroll
+#pragma unroll 1
     for (int k = 0; k < kTopK; ++k) {
-        const int g = ids[k];
+        const int g = s_id[k][tr];
         const bool valid = g >= 0;
         const KeyTree t = key_tree(lane, g);
         const bool lead = t.first && valid;
         const int gs = valid ? g : 0;  // a safe index for lanes without an id
         float geo[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        float v_sharp = 0.f, v_soft = 0.f, norm_d = 0.f, dx = 0.f, dy = 0.f;
+        float v_sharp = 0.f, v_soft = 0.f, norm_d = 0.f, dx = 0.f, dy = 0.f, peak = 0.f;
         int edge = 0;
         if (valid) {
             const HexPrim p = make_prim<AFFINE>(g, a.xys, a.scales, a.rotation, a.affines, a.aa,
@@ -574,7 +563,17 @@ __global__ void __launch_bounds__(256) hexel_bwd_kernel(const HexBwdArgs a) {
             const float2 delta = {p.x - px, p.y - py};
             dx = delta.x;
             dy = delta.y;
-            norm_d = d_local[k] / denom;
+            const float alpha = s_alpha[k][tr];
+            norm_d = alpha / denom;
+            // gradient of this slot's raw weight: normalisation, then the
+            // weight-sum and entropy statistics
+            float v_d = s_vn[k][tr] / denom;
+            v_d += v_d_sum;
+            if (v_ws != 0.f) v_d += v_ws;
+            if (v_ent != 0.f) {
+                const float dhdp = -(logf(norm_d + kEntropyEps) + 1.f);
+                v_d += v_ent * ((dhdp - ent_avg) / denom);
+            }
             const HexLocal l = hex_local<AFFINE>(p, delta.x, delta.y);
             const float dist = hex_sdf(l.u, l.v, edge);
             // SDF partials w.r.t. (u, v); |.| has subgradient sign(0) = 0
@@ -594,17 +593,19 @@ __global__ void __launch_bounds__(256) hexel_bwd_kernel(const HexBwdArgs a) {
             }
             const float soft = edge_softness(p, edge);
             const float sig = sigmoid_neg_dist(dist, soft);
-            const float v_d = v_d_local[k];
             float v_sig = v_d;
             float v_u_peak = 0.f, v_v_peak = 0.f;
             if (p.sharp > 0.f) {
-                const float r2 = u_coord[k] * u_coord[k] + v_coord[k] * v_coord[k];
-                const float peak = prim_peak[k];
+                const float r2 = l.u * l.u + l.v * l.v;
+                peak = __expf(-p.sharp * r2);
                 v_sig = v_d * peak;
-                const float v_peak = v_d * sig + v_peak_emit[k];
+                float v_peak_emit = 0.f;
+                if (a.v_emission && peak > 0.f)
+                    for (int c = 0; c < C; ++c) v_peak_emit += a.emission[C * g + c] * v_out[c];
+                const float v_peak = v_d * sig + v_peak_emit;
                 const float v_r2 = v_peak * peak * (-p.sharp);
-                v_u_peak = v_r2 * 2.f * u_coord[k];
-                v_v_peak = v_r2 * 2.f * v_coord[k];
+                v_u_peak = v_r2 * 2.f * l.u;
+                v_v_peak = v_r2 * 2.f * l.v;
                 v_sharp = v_peak * peak * (-r2);
             }
             v_soft = v_sig * (-dist) * sig * (1.f - sig);
@@ -674,7 +675,6 @@ __global__ void __launch_bounds__(256) hexel_bwd_kernel(const HexBwdArgs a) {
             }
         }
         if (a.v_emission) {
-            const float peak = prim_peak[k];
             for (int c = 0; c < C; ++c)
                 group_add(t, lead, a.v_emission + C * gs + c,
                           (valid && peak > 0.f) ? peak * v_out[c] : 0.f);

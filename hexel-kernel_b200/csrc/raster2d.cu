@@ -6,16 +6,16 @@
 // with the same fast-math flags, so images and top-K ids match bit for bit.
 // What differs is the schedule:
 //   * forward: candidates are staged per batch as packed float4/float2 in
-//     shared memory, and the top-K minimum is cached and rescanned only after
-//     an insertion instead of for every candidate (same insertion rule: first
-//     empty slot, else first minimum, replace iff strictly greater);
-//   * top-K backward: instead of ~80 global atomics per pixel, each CTA
-//     accumulates per-Gaussian partials in a shared-memory hash table and
-//     flushes one global atomic per (Gaussian, component) per tile;
+//     shared memory; slot ids sit in shared memory and the top-K minimum is
+//     cached and recomputed (as a tree) only after an insertion (same rule:
+//     first empty slot, else first minimum, replace iff strictly greater);
+//   * top-K backward: instead of ~80 global atomics per pixel, the lanes of
+//     a warp that hold the same Gaussian sum their partials with a shuffle
+//     tree and one lane adds each component with a global atomic;
 //   * plain-sum backward: warp shuffle reduction, then shared-memory
 //     accumulation across the CTA's warps, then one global atomic per
 //     candidate component per tile.
-#include "hx_common.cuh"
+#include "hx_topk.cuh"
 
 namespace hx {
 
@@ -85,7 +85,13 @@ __device__ __forceinline__ void topk_insert(int (&ids)[K], float (&vals)[K], int
 }
 
 // ---------------------------------------------------------------------------
-// Top-K forward (forward.cu:172-320), one 16x16 tile per CTA.
+// Top-K forward (forward.cu:172-320), one 16x16 tile per CTA, 8x4 pixels per
+// warp.  The reference's slot rule (first empty slot, else first minimum,
+// replace iff strictly greater) fills slots 0..K-1 in order and, once they are
+// full, never empties one, so the empty-slot search reduces to "next slot"
+// while filling and the minimum scan to a tree over the K weights.  Slot ids
+// live in shared memory ([slot][thread], conflict-free), so a replacement is
+// one store; the weights stay in registers.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) topk_fwd_kernel(
     int tiles_x, unsigned img_w, unsigned img_h, int channels, int num_points, int num_intersects,
@@ -95,23 +101,24 @@ __global__ void __launch_bounds__(256) topk_fwd_kernel(
     float* __restrict__ out_weights_sum, float* __restrict__ out_entropy) {
     __shared__ float4 s_a[kBlockSize];  // xy.x, xy.y, conic.x, conic.y
     __shared__ float2 s_b[kBlockSize];  // conic.z, id bits
+    __shared__ int s_ids[kTopK][kBlockSize];
 
     const int tile_id = blockIdx.y * tiles_x + blockIdx.x;
-    const unsigned i = blockIdx.y * kBlockY + threadIdx.y;
-    const unsigned j = blockIdx.x * kBlockX + threadIdx.x;
     const int tr = threadIdx.y * kBlockX + threadIdx.x;
+    const int2 lp = tile_pixel16(tr);
+    const unsigned i = blockIdx.y * kBlockY + lp.y;
+    const unsigned j = blockIdx.x * kBlockX + lp.x;
     const float px = (float)j;
     const float py = (float)i;
     const int pix_id = i * img_w + j;
     const bool inside = (i < img_h && j < img_w);
 
     const int2 range = clamp_range(tile_bins[tile_id], num_intersects);
-    int ids[kTopK];
     float vals[kTopK];
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
-        ids[k] = -1;
         vals[k] = 0.f;
+        s_ids[k][tr] = -1;
     }
     int min_id = 0;
     float min_val = -1.f;
@@ -136,10 +143,25 @@ __global__ void __launch_bounds__(256) topk_fwd_kernel(
                 const float sigma = gauss_sigma(make_float3(a.z, a.w, b.x), delta);
                 if (sigma_invalid(sigma)) continue;
                 const float alpha = __expf(-sigma);
-                topk_insert<kTopK>(ids, vals, min_id, min_val, __float_as_int(b.y), alpha);
+                if (alpha > min_val) {
+                    s_ids[min_id][tr] = __float_as_int(b.y);
+#pragma unroll
+                    for (int k = 0; k < kTopK; ++k)
+                        if (k == min_id) vals[k] = alpha;
+                    if (min_val < 0.f && min_id + 1 < kTopK)
+                        ++min_id;
+                    else
+                        ArgMin<0, kTopK>::run(vals, min_id, min_val);
+                }
             }
         }
     }
+    if (!inside) return;
+
+    int ids[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) ids[k] = s_ids[k][tr];
+
     if (!inside) return;
 
     float sum_val = 0.f;
@@ -351,195 +373,106 @@ __global__ void __launch_bounds__(256) sum_bwd_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Shared-memory hash table of per-Gaussian gradient partials.
+// Top-K backward (backward.cu:159-316 tiled, 318-438 tile-less).  One thread
+// per pixel, 256-thread CTAs over 16x16 pixel blocks with 8x4 pixels per
+// warp; `eps` is the normaliser offset of the forward.  Pass 1 recomputes
+// the stored ids' weights into shared columns; pass 2 computes every slot's
+// partials, sums them over the lanes of the warp that hold the same Gaussian
+// (KeyTree) and adds each group's sum with one global atomic.  Every lane
+// runs both passes (pixels outside the image contribute zeros) so that the
+// warp-wide sums stay converged.
 // ---------------------------------------------------------------------------
-struct GradTable {
-    int* keys;    // [cap], -1 = free
-    float* acc;   // [cap][ncomp]
-    int cap;      // power of two
-    int ncomp;
-};
-
-// Slot of Gaussian g (inserted on first use), or -1 when a bounded probe
-// sequence finds no room; callers then fall back to global atomics.
-__device__ __forceinline__ int table_slot(const GradTable& t, int g) {
-    const unsigned mask = (unsigned)t.cap - 1u;
-    unsigned h = ((unsigned)g * 2654435761u) & mask;
-    volatile int* keys = t.keys;
-#pragma unroll 1
-    for (int probe = 0; probe < 32; ++probe) {
-        const unsigned s = (h + probe) & mask;
-        const int k = keys[s];
-        if (k == g) return (int)s;
-        if (k == -1) {
-            const int prev = atomicCAS(t.keys + s, -1, g);
-            if (prev == -1 || prev == g) return (int)s;
-        }
-    }
-    return -1;
-}
-
-__device__ __forceinline__ void table_init(const GradTable& t, int tid, int nthreads) {
-    for (int s = tid; s < t.cap; s += nthreads) t.keys[s] = -1;
-    for (int s = tid; s < t.cap * t.ncomp; s += nthreads) t.acc[s] = 0.f;
-}
-
-// ---------------------------------------------------------------------------
-// Top-K backward (backward.cu:159-316 tiled, 318-438 tile-less).  One CTA per
-// BX x BY pixel block; `eps` is the normaliser offset of the forward.
-// ---------------------------------------------------------------------------
-template <int BX, int BY, int SMEM_C>
-__global__ void __launch_bounds__(BX * BY) topk_bwd_kernel(
+__global__ void __launch_bounds__(256) topk_bwd_kernel(
     unsigned img_w, unsigned img_h, int channels, int num_points, float eps,
     const float2* __restrict__ xys, const float3* __restrict__ conics,
     const float* __restrict__ rgbs, const float* __restrict__ v_output,
     const float* __restrict__ v_weights_sum, const float* __restrict__ v_entropy,
     const int* __restrict__ pixel_topk, float* __restrict__ v_xy, float* __restrict__ v_conic,
-    float* __restrict__ v_rgb, int table_cap) {
-    extern __shared__ __align__(16) unsigned char s_raw[];
-    constexpr int NT = BX * BY;
-    const int ncomp = 5 + (channels <= SMEM_C ? channels : 0);
-    GradTable table;
-    table.keys = reinterpret_cast<int*>(s_raw);
-    table.acc = reinterpret_cast<float*>(s_raw + sizeof(int) * table_cap);
-    table.cap = table_cap;
-    table.ncomp = ncomp;
-    const int tid = threadIdx.y * BX + threadIdx.x;
-    table_init(table, tid, NT);
-    __syncthreads();
-
-    const unsigned i = blockIdx.y * BY + threadIdx.y;
-    const unsigned j = blockIdx.x * BX + threadIdx.x;
+    float* __restrict__ v_rgb) {
+    __shared__ int s_id[kTopK][kBlockSize];
+    __shared__ float s_d[kTopK][kBlockSize];
+    __shared__ float s_vn[kTopK][kBlockSize];
+    const int tr = threadIdx.y * kBlockX + threadIdx.x;
+    const unsigned lane = tr & 31;
+    const int2 lp = tile_pixel16(tr);
+    const unsigned i = blockIdx.y * kBlockY + lp.y;
+    const unsigned j = blockIdx.x * kBlockX + lp.x;
     const float px = (float)j;
     const float py = (float)i;
     const bool inside = (i < img_h && j < img_w);
-    if (inside) {
-        const int pix_id = min((int)(i * img_w + j), (int)(img_w * img_h - 1));
-        const float* v_out = v_output + channels * pix_id;
-        int topk[kTopK];
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            const int g = pixel_topk[pix_id * kTopK + k];
-            topk[k] = (g < num_points) ? g : -1;
-        }
-        float d_local[kTopK];
-        float denom = eps;
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            d_local[k] = 0.f;
-            const int g = topk[k];
-            if (g < 0) continue;
-            const float3 conic = conics[g];
+    const int pix_id = min((int)(i * img_w + j), (int)(img_w * img_h - 1));
+    const float* v_out = v_output + channels * pix_id;
+
+    // pass 1: weights of the stored ids, their sum, and sum_c colour * v_out
+    float denom = eps;
+#pragma unroll 1
+    for (int k = 0; k < kTopK; ++k) {
+        int g = inside ? pixel_topk[pix_id * kTopK + k] : -1;
+        if (g >= num_points) g = -1;
+        float d = 0.f, v_norm_d = 0.f;
+        if (g >= 0) {
             const float2 xy = xys[g];
             const float2 delta = {xy.x - px, xy.y - py};
-            const float d = __expf(-gauss_sigma(conic, delta));
+            d = __expf(-gauss_sigma(conics[g], delta));
             denom += d;
-            d_local[k] = d;
+            for (int c = 0; c < channels; ++c) v_norm_d += rgbs[channels * g + c] * v_out[c];
         }
-        float v_d_local[kTopK];
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) v_d_local[k] = 0.f;
-
-        int slots[kTopK];
-#pragma unroll
+        s_id[k][tr] = g;
+        s_d[k][tr] = d;
+        s_vn[k][tr] = v_norm_d;
+    }
+    float v_d_sum = 0.f;
+#pragma unroll 1
+    for (int k = 0; k < kTopK; ++k)
+        if (s_id[k][tr] >= 0) v_d_sum += -s_d[k][tr] / (denom * denom) * s_vn[k][tr];
+    const float v_ws = (inside && v_weights_sum) ? v_weights_sum[pix_id] : 0.f;
+    const float v_ent = (inside && v_entropy) ? v_entropy[pix_id] : 0.f;
+    float ent_avg = 0.f;
+    if (v_ent != 0.f) {
+#pragma unroll 1
         for (int k = 0; k < kTopK; ++k) {
-            slots[k] = -1;
-            const int g = topk[k];
-            if (g < 0) continue;
-            const float d = d_local[k];
-            const float norm_d = d / denom;
-            const int slot = table_slot(table, g);
-            slots[k] = slot;
-            float v_norm_d = 0.f;
-            for (int c = 0; c < channels; ++c) {
-                const float vo = v_out[c];
-                const float contrib = norm_d * vo;
-                if (slot >= 0 && channels <= SMEM_C)
-                    atomicAdd(&table.acc[slot * ncomp + 5 + c], contrib);
-                else
-                    atomicAdd(v_rgb + channels * g + c, contrib);
-                v_norm_d += rgbs[channels * g + c] * vo;
-            }
-            const float tmp = -d / (denom * denom) * v_norm_d;
-#pragma unroll
-            for (int l = 0; l < kTopK; ++l) {
-                if (l == k)
-                    v_d_local[l] += v_norm_d / denom + tmp;
-                else
-                    v_d_local[l] += tmp;
-            }
-        }
-
-        const float v_ws = v_weights_sum ? v_weights_sum[pix_id] : 0.f;
-        if (v_ws != 0.f) {
-#pragma unroll
-            for (int k = 0; k < kTopK; ++k)
-                if (topk[k] >= 0) v_d_local[k] += v_ws;
-        }
-        const float v_ent = v_entropy ? v_entropy[pix_id] : 0.f;
-        if (v_ent != 0.f) {
-            float dHdp[kTopK];
-            float avg = 0.f;
-#pragma unroll
-            for (int k = 0; k < kTopK; ++k) {
-                dHdp[k] = 0.f;
-                if (topk[k] < 0) continue;
-                const float p = d_local[k] / denom;
-                const float dhdp = -(logf(p + 1e-7f) + 1.f);
-                dHdp[k] = dhdp;
-                avg += p * dhdp;
-            }
-#pragma unroll
-            for (int k = 0; k < kTopK; ++k) {
-                if (topk[k] < 0) continue;
-                const float dhdw = (dHdp[k] - avg) / denom;
-                v_d_local[k] += v_ent * dhdw;
-            }
-        }
-
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) {
-            const int g = topk[k];
-            if (g < 0) continue;
-            float v_sigma = v_d_local[k];
-            v_sigma *= -d_local[k];
-            const float3 conic = conics[g];
-            const float2 xy = xys[g];
-            const float2 delta = {xy.x - px, xy.y - py};
-            const float vc0 = 0.5f * v_sigma * delta.x * delta.x;
-            const float vc1 = v_sigma * delta.x * delta.y;
-            const float vc2 = 0.5f * v_sigma * delta.y * delta.y;
-            const float vx = v_sigma * (conic.x * delta.x + conic.y * delta.y);
-            const float vy = v_sigma * (conic.y * delta.x + conic.z * delta.y);
-            const int slot = slots[k];
-            if (slot >= 0) {
-                float* a = table.acc + slot * ncomp;
-                atomicAdd(a + 0, vx);
-                atomicAdd(a + 1, vy);
-                atomicAdd(a + 2, vc0);
-                atomicAdd(a + 3, vc1);
-                atomicAdd(a + 4, vc2);
-            } else {
-                atomicAdd(v_xy + 2 * g + 0, vx);
-                atomicAdd(v_xy + 2 * g + 1, vy);
-                atomicAdd(v_conic + 3 * g + 0, vc0);
-                atomicAdd(v_conic + 3 * g + 1, vc1);
-                atomicAdd(v_conic + 3 * g + 2, vc2);
-            }
+            if (s_id[k][tr] < 0) continue;
+            const float p = s_d[k][tr] / denom;
+            ent_avg += p * -(logf(p + 1e-7f) + 1.f);
         }
     }
-    __syncthreads();
-    for (int s = tid; s < table_cap; s += NT) {
-        const int g = table.keys[s];
-        if (g < 0) continue;
-        const float* a = table.acc + s * ncomp;
-        if (a[0] != 0.f) atomicAdd(v_xy + 2 * g + 0, a[0]);
-        if (a[1] != 0.f) atomicAdd(v_xy + 2 * g + 1, a[1]);
-        if (a[2] != 0.f) atomicAdd(v_conic + 3 * g + 0, a[2]);
-        if (a[3] != 0.f) atomicAdd(v_conic + 3 * g + 1, a[3]);
-        if (a[4] != 0.f) atomicAdd(v_conic + 3 * g + 2, a[4]);
-        for (int c = 5; c < ncomp; ++c)
-            if (a[c] != 0.f) atomicAdd(v_rgb + channels * g + (c - 5), a[c]);
+
+    // pass 2: per-slot partials, summed per Gaussian over the warp
+#pragma unroll 1
+    for (int k = 0; k < kTopK; ++k) {
+        const int g = s_id[k][tr];
+        const bool valid = g >= 0;
+        const KeyTree t = key_tree(lane, g);
+        const bool lead = t.first && valid;
+        const int gs = valid ? g : 0;  // a safe index for lanes without an id
+        float vx = 0.f, vy = 0.f, vc0 = 0.f, vc1 = 0.f, vc2 = 0.f, norm_d = 0.f;
+        if (valid) {
+            const float d = s_d[k][tr];
+            norm_d = d / denom;
+            float v_d = s_vn[k][tr] / denom;
+            v_d += v_d_sum;
+            if (v_ws != 0.f) v_d += v_ws;
+            if (v_ent != 0.f) {
+                const float dhdp = -(logf(norm_d + 1e-7f) + 1.f);
+                v_d += v_ent * ((dhdp - ent_avg) / denom);
+            }
+            const float v_sigma = v_d * -d;
+            const float3 conic = conics[g];
+            const float2 xy = xys[g];
+            const float2 delta = {xy.x - px, xy.y - py};
+            vc0 = 0.5f * v_sigma * delta.x * delta.x;
+            vc1 = v_sigma * delta.x * delta.y;
+            vc2 = 0.5f * v_sigma * delta.y * delta.y;
+            vx = v_sigma * (conic.x * delta.x + conic.y * delta.y);
+            vy = v_sigma * (conic.y * delta.x + conic.z * delta.y);
+        }
+        for (int c = 0; c < channels; ++c)
+            group_add(t, lead, v_rgb + channels * gs + c, valid ? norm_d * v_out[c] : 0.f);
+        group_add(t, lead, v_xy + 2 * gs + 0, vx);
+        group_add(t, lead, v_xy + 2 * gs + 1, vy);
+        group_add(t, lead, v_conic + 3 * gs + 0, vc0);
+        group_add(t, lead, v_conic + 3 * gs + 1, vc1);
+        group_add(t, lead, v_conic + 3 * gs + 2, vc2);
     }
 }
 
@@ -611,29 +544,16 @@ __global__ void __launch_bounds__(1024) no_tiles_fwd_kernel(
     for (int k = 0; k < kTopK; ++k) pixel_topk[pix_id * kTopK + k] = ids[k];
 }
 
-template <int BX, int BY, int SMEM_C>
 int launch_topk_bwd(unsigned img_w, unsigned img_h, int channels, int num_points, float eps,
                     const float* xys, const float* conics, const float* colors,
                     const float* v_output, const float* v_ws, const float* v_ent,
                     const int* pixel_topk, float* v_xy, float* v_conic, float* v_colors,
-                    int table_cap, cudaStream_t stream) {
-    const int ncomp = 5 + (channels <= SMEM_C ? channels : 0);
-    const size_t smem = sizeof(int) * table_cap + sizeof(float) * (size_t)table_cap * ncomp;
-    static bool attr_set[64] = {};
-    int dev = 0;
-    HX_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        HX_CUDA_TRY(cudaFuncSetAttribute(topk_bwd_kernel<BX, BY, SMEM_C>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)(sizeof(int) * table_cap +
-                                               sizeof(float) * (size_t)table_cap * (5 + SMEM_C))));
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
-    dim3 grid(ceil_div((int)img_w, BX), ceil_div((int)img_h, BY));
-    dim3 block(BX, BY);
-    topk_bwd_kernel<BX, BY, SMEM_C><<<grid, block, smem, stream>>>(
+                    cudaStream_t stream) {
+    dim3 grid(ceil_div((int)img_w, kBlockX), ceil_div((int)img_h, kBlockY));
+    dim3 block(kBlockX, kBlockY);
+    topk_bwd_kernel<<<grid, block, 0, stream>>>(
         img_w, img_h, channels, num_points, eps, (const float2*)xys, (const float3*)conics, colors,
-        v_output, v_ws, v_ent, pixel_topk, v_xy, v_conic, v_colors, table_cap);
+        v_output, v_ws, v_ent, pixel_topk, v_xy, v_conic, v_colors);
     HX_LAUNCH_CHECK("topk_bwd_kernel");
     return HX_OK;
 }
@@ -736,10 +656,9 @@ extern "C" int hx_nd_rasterize_backward_topk_norm(
     if (img_width == 0 || img_height == 0 || num_points == 0) return HX_OK;
     HX_REQUIRE(xys && conics && colors && v_output && pixel_topk && v_xy && v_conic && v_colors,
                "nd_rasterize_backward_topk_norm: null pointer");
-    return launch_topk_bwd<16, 16, 4>(img_width, img_height, channels, num_points,
-                                      (float)kEpsTopK, xys, conics, colors, v_output,
-                                      v_weights_sum, v_entropy, pixel_topk, v_xy, v_conic,
-                                      v_colors, 1024, stream);
+    return launch_topk_bwd(img_width, img_height, channels, num_points, (float)kEpsTopK, xys,
+                           conics, colors, v_output, v_weights_sum, v_entropy, pixel_topk, v_xy,
+                           v_conic, v_colors, stream);
 }
 
 extern "C" int hx_nd_rasterize_forward_no_tiles(unsigned img_width, unsigned img_height,
@@ -770,7 +689,7 @@ extern "C" int hx_nd_rasterize_backward_no_tiles(unsigned img_width, unsigned im
     if (img_width == 0 || img_height == 0 || num_points == 0) return HX_OK;
     HX_REQUIRE(xys && conics && colors && v_output && pixel_topk && v_xy && v_conic && v_colors,
                "nd_rasterize_backward_no_tiles: null pointer");
-    return launch_topk_bwd<32, 32, 4>(img_width, img_height, channels, num_points,
-                                      (float)kEpsNoTiles, xys, conics, colors, v_output, nullptr,
-                                      nullptr, pixel_topk, v_xy, v_conic, v_colors, 2048, stream);
+    return launch_topk_bwd(img_width, img_height, channels, num_points, (float)kEpsNoTiles, xys,
+                           conics, colors, v_output, nullptr, nullptr, pixel_topk, v_xy, v_conic,
+                           v_colors, stream);
 }

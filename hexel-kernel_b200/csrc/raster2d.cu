@@ -92,6 +92,14 @@ __device__ __forceinline__ void topk_insert(int (&ids)[K], float (&vals)[K], int
 // while filling and the minimum scan to a tree over the K weights.  Slot ids
 // live in shared memory ([slot][thread], conflict-free), so a replacement is
 // one store; the weights stay in registers.
+//
+// Candidates are visited in list order, 32 at a time per warp: each lane
+// bounds one candidate's weight over the warp's 8x4 pixel block from below
+// in sigma (half the conic's smallest eigenvalue times the squared distance
+// from the centre to the block, less rounding margins) and the warp skips
+// every candidate whose bound cannot beat the smallest current top-K minimum
+// of its lanes.  Minima only grow, so a skipped candidate would have been
+// rejected by every lane; the result is the reference's, bit for bit.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) topk_fwd_kernel(
     int tiles_x, unsigned img_w, unsigned img_h, int channels, int num_points, int num_intersects,
@@ -100,11 +108,12 @@ __global__ void __launch_bounds__(256) topk_fwd_kernel(
     const float* __restrict__ colors, float* __restrict__ out_img, int* __restrict__ pixel_topk,
     float* __restrict__ out_weights_sum, float* __restrict__ out_entropy) {
     __shared__ float4 s_a[kBlockSize];  // xy.x, xy.y, conic.x, conic.y
-    __shared__ float2 s_b[kBlockSize];  // conic.z, id bits
+    __shared__ float4 s_b[kBlockSize];  // conic.z, id bits, eigenvalue lower bound, -
     __shared__ int s_ids[kTopK][kBlockSize];
 
     const int tile_id = blockIdx.y * tiles_x + blockIdx.x;
     const int tr = threadIdx.y * kBlockX + threadIdx.x;
+    const unsigned lane = tr & 31;
     const int2 lp = tile_pixel16(tr);
     const unsigned i = blockIdx.y * kBlockY + lp.y;
     const unsigned j = blockIdx.x * kBlockX + lp.x;
@@ -112,6 +121,9 @@ __global__ void __launch_bounds__(256) topk_fwd_kernel(
     const float py = (float)i;
     const int pix_id = i * img_w + j;
     const bool inside = (i < img_h && j < img_w);
+    // the warp's pixel block [rx0, rx0 + 7] x [ry0, ry0 + 3]
+    const float rx0 = (float)(blockIdx.x * kBlockX + ((tr >> 5) & 1) * 8);
+    const float ry0 = (float)(blockIdx.y * kBlockY + (tr >> 6) * 4);
 
     const int2 range = clamp_range(tile_bins[tile_id], num_intersects);
     float vals[kTopK];
@@ -130,15 +142,41 @@ __global__ void __launch_bounds__(256) topk_fwd_kernel(
             const int g = clamp_id(gaussian_ids_sorted[idx], num_points);
             const float2 xy = xys[g];
             const float3 c = conics[g];
+            // smallest eigenvalue of [[c.x, c.y], [c.y, c.z]], lowered by a
+            // margin that covers its own rounding and that of sigma
+            const float hd = 0.5f * (c.x - c.z);
+            const float lam = 0.5f * (c.x + c.z) - sqrtf(hd * hd + c.y * c.y);
+            const float lam_lo = lam - 1e-5f * (fabsf(c.x) + fabsf(c.z) + 2.f * fabsf(c.y));
             s_a[tr] = make_float4(xy.x, xy.y, c.x, c.y);
-            s_b[tr] = make_float2(c.z, __int_as_float(g));
+            s_b[tr] = make_float4(c.z, __int_as_float(g), lam_lo, 0.f);
         }
         __syncthreads();
         const int batch_size = min(kBlockSize, range.y - batch_start);
-        if (inside) {
-            for (int t = 0; t < batch_size; ++t) {
+        for (int c0 = 0; c0 < batch_size; c0 += 32) {
+            // smallest top-K minimum over the warp's pixels (-1 while any is
+            // still filling; the int order of the bits is the float order
+            // for the non-negative values, and any negative stays negative)
+            const int wmin_bits = __reduce_min_sync(
+                kFullMask, inside ? __float_as_int(min_val) : 0x7f800000);
+            const float wmin = __int_as_float(wmin_bits);
+            const float s_max = wmin > 0.f ? -__logf(wmin) * 1.0001f + 1e-3f : -1.f;
+            const int tc = c0 + (int)lane;
+            bool pass = tc < batch_size;
+            if (pass && s_max >= 0.f) {
+                const float4 a = s_a[tc];
+                const float lam_lo = s_b[tc].z;
+                const float ddx = fmaxf(fmaxf(rx0 - a.x, a.x - (rx0 + 7.f)), 0.f);
+                const float ddy = fmaxf(fmaxf(ry0 - a.y, a.y - (ry0 + 3.f)), 0.f);
+                const float sigma_lb = 0.5f * lam_lo * (ddx * ddx + ddy * ddy);
+                pass = !(sigma_lb > s_max);
+            }
+            unsigned todo = __ballot_sync(kFullMask, pass);
+            while (todo) {
+                const int t = c0 + __ffs(todo) - 1;
+                todo &= todo - 1;
+                if (!inside) continue;
                 const float4 a = s_a[t];
-                const float2 b = s_b[t];
+                const float4 b = s_b[t];
                 const float2 delta = {a.x - px, a.y - py};
                 const float sigma = gauss_sigma(make_float3(a.z, a.w, b.x), delta);
                 if (sigma_invalid(sigma)) continue;

@@ -87,6 +87,11 @@ class ClockSampler:
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        # nvidia-smi takes a moment to start: wait (bounded) for its first
+        # sample so that short timed regions are covered too
+        deadline = time.time() + 5.0
+        while not self.lines and time.time() < deadline and self.proc.poll() is None:
+            time.sleep(0.01)
 
     def _read(self):
         for line in self.proc.stdout:

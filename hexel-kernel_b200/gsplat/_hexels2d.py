@@ -13,7 +13,7 @@ from __future__ import annotations
 
 import torch
 
-from ._lib import check_input, lib, ptr, stream
+from ._lib import check_input, lib, ptr, stream, zero_views
 
 TOP_K = 10
 
@@ -78,10 +78,12 @@ def _forward(tile_bounds, block, img_size, ids, bins, xys, colors, *, scales=Non
     em = _emission(emission, n, channels)
     sh = None if sharpness is None or sharpness.numel() == 0 else sharpness.contiguous()
     dev = xys.device
-    out_img = torch.zeros((h, w, channels), dtype=torch.float32, device=dev)
-    pixel_topk = torch.zeros((h, w, TOP_K), dtype=torch.int32, device=dev)
-    weights_sum = torch.zeros((h, w), dtype=torch.float32, device=dev)
-    entropy = torch.zeros((h, w), dtype=torch.float32, device=dev)
+    # the kernel writes every pixel when the tile grid is non-empty
+    alloc = torch.empty if tb[0] > 0 and tb[1] > 0 else torch.zeros
+    out_img = alloc((h, w, channels), dtype=torch.float32, device=dev)
+    pixel_topk = alloc((h, w, TOP_K), dtype=torch.int32, device=dev)
+    weights_sum = alloc((h, w), dtype=torch.float32, device=dev)
+    entropy = alloc((h, w), dtype=torch.float32, device=dev)
     with torch.cuda.device(dev):
         lib.call("hx_hexels2d_forward", tb[0], tb[1], w, h, channels, n, ids.numel(), ptr(ids),
                  ptr(bins),
@@ -127,18 +129,22 @@ def _backward(img_height, img_width, block_h, block_w, xys, colors, v_output, v_
     soft, stride = _softness_stride(softnesses, n)
     em = _emission(emission, n, channels)
     sh = None if sharpness is None or sharpness.numel() == 0 else sharpness.contiguous()
-    z = lambda *s: torch.zeros(s, dtype=torch.float32, device=dev)  # noqa: E731
-    v_xy = z(n, 2)
-    v_scale = z(n, 2) if affines is None else None
-    v_rot = z(n, 1) if affines is None else None
-    v_affines = z(n, 2, 2) if affines is not None else None
-    v_colors = z(n, channels)
-    v_color_grads = z(n, 2, channels) if color_grads is not None else None
-    v_sharpness = z(n, 1)
-    emission_shape = tuple(emission.shape) if emission is not None else (0,)
-    v_emission = torch.zeros(emission_shape, dtype=torch.float32, device=dev)
-    v_softnesses = (torch.zeros(tuple(softnesses.shape), dtype=torch.float32, device=dev)
-                    if softnesses is not None else None)
+    # all gradient outputs zeroed by one fill of one allocation
+    shapes = {"v_xy": (n, 2), "v_colors": (n, channels), "v_sharpness": (n, 1),
+              "v_emission": tuple(emission.shape) if emission is not None else (0,)}
+    if affines is None:
+        shapes.update(v_scale=(n, 2), v_rot=(n, 1))
+    else:
+        shapes.update(v_affines=(n, 2, 2))
+    if color_grads is not None:
+        shapes.update(v_color_grads=(n, 2, channels))
+    if softnesses is not None:
+        shapes.update(v_softnesses=tuple(softnesses.shape))
+    g = dict(zip(shapes, zero_views(dev, list(shapes.values()))))
+    v_xy, v_colors, v_sharpness, v_emission = (g["v_xy"], g["v_colors"], g["v_sharpness"],
+                                               g["v_emission"])
+    v_scale, v_rot, v_affines = g.get("v_scale"), g.get("v_rot"), g.get("v_affines")
+    v_color_grads, v_softnesses = g.get("v_color_grads"), g.get("v_softnesses")
     with torch.cuda.device(dev):
         lib.call("hx_hexels2d_backward", int(img_width), int(img_height), channels, n, ptr(xys),
                  ptr(scales), ptr(rotation), ptr(affines), ptr(colors), ptr(color_grads),

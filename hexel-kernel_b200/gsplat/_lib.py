@@ -11,6 +11,7 @@ importing this module fails.
 from __future__ import annotations
 
 import ctypes
+import math
 import os
 import re
 from typing import Optional
@@ -98,6 +99,20 @@ def stream(device: torch.device) -> int:
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     """Caller-owned scratch memory from PyTorch's caching allocator."""
     return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def zero_views(device: torch.device, shapes) -> list:
+    """Zero-filled float32 tensors of the given shapes carved out of one
+    allocation (one fill launch instead of one per tensor); each view starts
+    on a 16-byte boundary so the kernels' vector loads stay aligned."""
+    sizes = [int(math.prod(s)) for s in shapes]
+    padded = [(n + 3) // 4 * 4 for n in sizes]
+    buf = torch.zeros(max(1, sum(padded)), dtype=torch.float32, device=device)
+    out, o = [], 0
+    for shape, n, pn in zip(shapes, sizes, padded):
+        out.append(buf[o:o + n].view(shape))
+        o += pn
+    return out
 
 
 def check_input(t: torch.Tensor, name: str) -> None:

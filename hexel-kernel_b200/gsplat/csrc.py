@@ -15,7 +15,7 @@ from typing import Tuple
 
 import torch
 
-from ._lib import check_input, lib, ptr, stream, workspace
+from ._lib import check_input, lib, ptr, stream, workspace, zero_views
 from . import _hexels2d
 
 TOP_K = 10
@@ -175,9 +175,7 @@ def nd_rasterize_backward(img_height, img_width, BLOCK_H, BLOCK_W, gaussians_ids
     _check_xys_colors(xys, colors)
     tx, ty = _tile_bounds_for(int(img_height), int(img_width), int(BLOCK_H), int(BLOCK_W))
     n, channels, dev = xys.size(0), colors.size(1), xys.device
-    v_xy = torch.zeros((n, 2), dtype=torch.float32, device=dev)
-    v_conic = torch.zeros((n, 3), dtype=torch.float32, device=dev)
-    v_colors = torch.zeros((n, channels), dtype=torch.float32, device=dev)
+    v_xy, v_conic, v_colors = zero_views(dev, [(n, 2), (n, 3), (n, channels)])
     v_output = v_output.contiguous()
     with torch.cuda.device(dev):
         lib.call("hx_nd_rasterize_backward", tx, ty, int(img_width), int(img_height), channels,
@@ -202,10 +200,12 @@ def _topk_forward(tile_bounds, block, img_size, gaussian_ids_sorted, tile_bins, 
     tb, (w, h, _) = _dims(tile_bounds), _dims(img_size)
     channels = colors.size(1)
     dev = xys.device
-    out_img = torch.zeros((h, w, channels), dtype=torch.float32, device=dev)
-    pixel_topk = torch.zeros((h, w, TOP_K), dtype=torch.int32, device=dev)
-    weights_sum = torch.zeros((h, w), dtype=torch.float32, device=dev) if stats else None
-    entropy = torch.zeros((h, w), dtype=torch.float32, device=dev) if stats else None
+    # the kernel writes every pixel when the tile grid is non-empty
+    alloc = torch.empty if tb[0] > 0 and tb[1] > 0 else torch.zeros
+    out_img = alloc((h, w, channels), dtype=torch.float32, device=dev)
+    pixel_topk = alloc((h, w, TOP_K), dtype=torch.int32, device=dev)
+    weights_sum = alloc((h, w), dtype=torch.float32, device=dev) if stats else None
+    entropy = alloc((h, w), dtype=torch.float32, device=dev) if stats else None
     with torch.cuda.device(dev):
         lib.call("hx_nd_rasterize_forward_topk_norm", tb[0], tb[1], w, h, channels, xys.size(0),
                  gaussian_ids_sorted.numel(), ptr(gaussian_ids_sorted), ptr(tile_bins), ptr(xys), ptr(conics), ptr(colors),
@@ -233,9 +233,7 @@ def _topk_backward(img_height, img_width, BLOCK_H, BLOCK_W, xys, conics, colors,
     check_input(pixel_topk, "pixel_topk")
     _tile_bounds_for(int(img_height), int(img_width), int(BLOCK_H), int(BLOCK_W))
     n, channels, dev = xys.size(0), colors.size(1), xys.device
-    v_xy = torch.zeros((n, 2), dtype=torch.float32, device=dev)
-    v_conic = torch.zeros((n, 3), dtype=torch.float32, device=dev)
-    v_colors = torch.zeros((n, channels), dtype=torch.float32, device=dev)
+    v_xy, v_conic, v_colors = zero_views(dev, [(n, 2), (n, 3), (n, channels)])
     v_output = v_output.contiguous()
     with torch.cuda.device(dev):
         lib.call("hx_nd_rasterize_backward_topk_norm", int(img_width), int(img_height), channels,

@@ -22,7 +22,7 @@ from typing import Optional
 
 import torch
 
-from .._lib import check_input, lib, ptr, stream, workspace
+from .._lib import check_input, lib, ptr, stream, workspace, zero_views
 
 kNumChannels = 3
 _EMPTY_CACHE: dict = {}
@@ -39,17 +39,7 @@ def _mark(name: str) -> None:
 
 
 def _zero_views(dev, shapes):
-    """Zero-filled float32 tensors of the given shapes carved out of one
-    allocation (one fill launch instead of one per tensor); each view starts
-    on a 16-byte boundary so the kernels' vector loads stay aligned."""
-    sizes = [int(math.prod(s)) for s in shapes]
-    padded = [(n + 3) // 4 * 4 for n in sizes]
-    buf = torch.zeros(max(1, sum(padded)), dtype=torch.float32, device=dev)
-    out, o = [], 0
-    for shape, n, pn in zip(shapes, sizes, padded):
-        out.append(buf[o:o + n].view(shape))
-        o += pn
-    return out
+    return zero_views(dev, shapes)
 
 
 def _empty(x: torch.Tensor, dtype=None) -> torch.Tensor:

@@ -747,7 +747,8 @@ class Hexels3DStep:
                                  1.0, 1, 1, True, -1, False, False, False, o["saved"],
                                  surf_state=o["surf_state"],
                                  surf_normals=o["normals"] if self.surface else None,
-                                 accumulate_into=dict(zip(names, self.acc)))
+                                 accumulate_into=dict(zip(names, self.acc)),
+                                 blend_mask=o["blend_mask"])
         if keep_info:
             saved = o["saved"]
             self.info.setdefault("num_rendered", []).append(o["num_rendered"])

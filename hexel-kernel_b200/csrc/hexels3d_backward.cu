@@ -432,6 +432,8 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
     __shared__ int s_max_visit;
     // per warp: the batch slots whose pixel box meets the warp's block
     __shared__ unsigned char s_list[kThreads / 32][kBatch];
+    // the forward's blend-mask bytes of the batch's list entries
+    __shared__ unsigned char s_bm[kBatch];
 
     // N == 32 uses the fixed slot layout (compile-time indices keep the
     // gradient vector in registers); N == 64 takes the host-computed layout
@@ -459,6 +461,7 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
     const int wx0 = (int)(blockIdx.x * k3BlockX) + ((warp & 1) << 3);
     const int wy0 = (int)(blockIdx.y * k3BlockY) + (warp >> 1) * kWarpRows;
     const int HW = H * W;
+    const unsigned my_bits = blend_bits(warp, PPT);
 
     uint2 range = a.ranges[blockIdx.y * hblocks + blockIdx.x];
     range.y = min(range.y, (unsigned)a.num_rendered);
@@ -534,6 +537,7 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
         for (int t = tr; bstart + t < bend; t += kThreads) {
             int g = a.point_list[range.x + bstart + t];
             g = min(max(g, 0), a.P - 1);
+            s_bm[t] = a.blend_mask ? a.blend_mask[range.x + bstart + t] : (unsigned char)0xff;
             Surfel3D& s = s_prim[t];
             s.id = g;
             const float* Tm = a.transMats + 9 * g;
@@ -593,13 +597,14 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
         __syncthreads();
 
         // compact the batch slots below this warp's pixels' last indices to the
-        // surfels whose box meets the warp's block: no pixel of a block a box
-        // misses blends that surfel, so nothing of the pair changes there
+        // surfels whose box meets the warp's block and whose blend-mask bits
+        // for the block are set: no pixel of the block blends any other, so
+        // nothing of those pairs changes there
         const int n_slots = min(bend, warp_max) - bstart;
         int n_mine = 0;
         for (int base = 0; base < n_slots; base += 32) {
             const int t = base + lane;
-            const bool hit = t < n_slots &&
+            const bool hit = t < n_slots && (s_bm[t] & my_bits) != 0u &&
                              (PREFILTER || !box_misses(s_prim[t].q.box, wx0, wy0, wx0 + 7,
                                                        wy0 + kWarpRows - 1));
             const unsigned m = __ballot_sync(0xffffffffu, hit);
@@ -914,7 +919,7 @@ extern "C" int hx_hexels3d_render_backward(
     float* grad_normals, int overdraw_base_count, int color_model, int use_view_grads,
     const float* final_T, const int32_t* last_index, const float* final_T_surf,
     const int32_t* last_index_surf, const float* m1_surf, const float* m2_surf,
-    const int32_t* median_index, cudaStream_t stream) {
+    const int32_t* median_index, const uint8_t* blend_mask, cudaStream_t stream) {
     HX_REQUIRE(image_width > 0 && image_height > 0, "invalid image dimensions");
     HX_REQUIRE(color_model >= 0 && color_model <= 3, "color_model must be 0..3");
     HX_REQUIRE(view_model >= 0 && view_model <= 2, "view_model must be 0..2");
@@ -980,6 +985,7 @@ extern "C" int hx_hexels3d_render_backward(
     a.m1_surf = m1_surf;
     a.m2_surf = m2_surf;
     a.median_index = median_index;
+    a.blend_mask = blend_mask;
 
     BwdLayout L;
     const bool explicit_vd = view_model == 2 || (use_view_grads && prefilter);

@@ -33,13 +33,14 @@ struct FwdPixel {
 };
 
 // One (pixel, surfel) pair at list index `idx` (batch slot j): the
-// reference's per-pair arithmetic (hexels3d_forward.cu:690-1000).
+// reference's per-pair arithmetic (hexels3d_forward.cu:690-1000).  Returns
+// whether the pair's alpha reached k3BlendMarkAlpha (the blend-mask test).
 template <bool SURF, bool PREFILTER, bool OWNER>
-__device__ __forceinline__ void fwd_pair(const Render3DArgs& a, const Surfel3D& s, int idx, int j,
+__device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& s, int idx, int j,
                                          FwdPixel& q, float* s_contrib) {
     const int g_id = s.id;
     const bool is_base = g_id < a.overdraw_base;
-    if (SURF && q.done_color && !is_base) return;
+    if (SURF && q.done_color && !is_base) return false;
     const float px = q.px, py = q.py;
     const float3 Tu = {s.tu[0], s.tu[1], s.tu[2]};
     const float3 Tv = {s.tv[0], s.tv[1], s.tv[2]};
@@ -47,11 +48,11 @@ __device__ __forceinline__ void fwd_pair(const Render3DArgs& a, const Surfel3D& 
     const float3 k = {px * Tw.x - Tu.x, px * Tw.y - Tu.y, px * Tw.z - Tu.z};
     const float3 l = {py * Tw.x - Tv.x, py * Tw.y - Tv.y, py * Tw.z - Tv.z};
     const float3 p = cross3(k, l);
-    if (p.z == 0.0f) return;
+    if (p.z == 0.0f) return false;
     const float sx = p.x / p.z;
     const float sy = p.y / p.z;
     const float depth_sdf = (sx * Tw.x + sy * Tw.y) + Tw.z;
-    if (depth_sdf < k3NearPlane) return;
+    if (depth_sdf < k3NearPlane) return false;
     float dist, soft;
     if (a.softness_stride == 1) {  // one softness for all edges: no edge needed
         dist = hex_sdf_value(sx, sy);
@@ -74,7 +75,8 @@ __device__ __forceinline__ void fwd_pair(const Render3DArgs& a, const Surfel3D& 
         use_filter = alpha_filter > alpha_sdf;
         alpha = use_filter ? alpha_filter : alpha_sdf;
     }
-    if (alpha < 1.0f / 255.0f) return;
+    const bool mark = alpha >= k3BlendMarkAlpha;
+    if (alpha < 1.0f / 255.0f) return mark;
     const float depth = use_filter ? Tw.z : depth_sdf;
 
     if (!q.done_color) {
@@ -161,6 +163,7 @@ __device__ __forceinline__ void fwd_pair(const Render3DArgs& a, const Surfel3D& 
             q.n_visited_surf = idx + 1;
         }
     }
+    return mark;
 }
 
 // One CTA per 16x16 tile, 256 / PPT threads, PPT pixels per thread: warps
@@ -175,6 +178,8 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const R
     __shared__ float s_contrib[k3BlockSize];
     // per warp: the batch slots whose pixel box meets the warp's block
     __shared__ unsigned char s_list[kThreads / 32][k3BlockSize];
+    // per warp and batch slot: whether a pixel of the warp marked the pair
+    __shared__ __align__(4) unsigned char s_wmark[kThreads / 32][k3BlockSize];
 
     const int W = a.W, H = a.H;
     const unsigned hblocks = (W + k3BlockX - 1) / k3BlockX;
@@ -220,6 +225,9 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const R
 
     for (int i = 0; i < rounds; ++i, to_do -= k3BlockSize) {
         if (__syncthreads_count(thread_done) == kThreads) break;
+        if (a.blend_mask)
+            for (int t = tr; t < (kThreads / 32) * k3BlockSize / 4; t += kThreads)
+                reinterpret_cast<unsigned*>(&s_wmark[0][0])[t] = 0u;
         for (int t = tr; t < k3BlockSize; t += kThreads) {
             s_contrib[t] = 0.f;
             const int progress = i * k3BlockSize + t;
@@ -302,20 +310,30 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const R
         for (int jj = 0; !thread_done && jj < n_mine; ++jj) {
             const int j = s_list[warp][jj];
             const Surfel3D& s = s_prim[j];
-            bool all_done = true;
+            bool all_done = true, mark = false;
 #pragma unroll
             for (int k = 0; k < PPT; ++k) {
                 if (!(q[k].done_color && q[k].done_surf))
-                    fwd_pair<SURF, PREFILTER, OWNER>(a, s, i * k3BlockSize + j, j, q[k],
-                                                     s_contrib);
+                    mark |= fwd_pair<SURF, PREFILTER, OWNER>(a, s, i * k3BlockSize + j, j, q[k],
+                                                             s_contrib);
                 all_done = all_done && q[k].done_color && q[k].done_surf;
             }
+            if (mark) s_wmark[warp][j] = 1;  // same value from every marking lane
             thread_done = all_done;
         }
+        if (a.contrib || a.blend_mask) __syncthreads();
         if (a.contrib) {
-            __syncthreads();
             for (int t = tr; t < batch_size; t += kThreads)
                 if (s_contrib[t] != 0.f) atomicAdd(&a.contrib[s_prim[t].id], s_contrib[t]);
+        }
+        if (a.blend_mask) {
+            for (int t = tr; t < batch_size; t += kThreads) {
+                unsigned bits = 0u;
+#pragma unroll
+                for (int w = 0; w < kThreads / 32; ++w)
+                    if (s_wmark[w][t]) bits |= blend_bits(w, PPT);
+                a.blend_mask[range.x + i * k3BlockSize + t] = (unsigned char)bits;
+            }
         }
     }
 
@@ -396,7 +414,8 @@ extern "C" int hx_hexels3d_render_forward(
     float* out_alpha, float* out_surface, int64_t* owner_id, float* owner_weight,
     float* owner_uv, float* owner_sdf, float* owner_depth, float* total_alpha, float* final_T,
     int32_t* last_index, float* final_T_surf, int32_t* last_index_surf, float* m1_surf,
-    float* m2_surf, int32_t* median_index, int32_t* contrib_count, cudaStream_t stream) {
+    float* m2_surf, int32_t* median_index, int32_t* contrib_count, uint8_t* blend_mask,
+    cudaStream_t stream) {
     HX_REQUIRE(image_width > 0 && image_height > 0, "invalid image dimensions");
     HX_REQUIRE(color_model >= 0 && color_model <= 3, "color_model must be 0..3");
     HX_REQUIRE(view_model >= 0 && view_model <= 2, "view_model must be 0..2");
@@ -466,6 +485,7 @@ extern "C" int hx_hexels3d_render_forward(
     a.m2_surf = m2_surf;
     a.median_index = median_index;
     a.contrib_count = contrib_count;
+    a.blend_mask = blend_mask;
     if (surf) return prefilter ? launch_render<true, true, false>(a, stream)
                                : launch_render<true, false, false>(a, stream);
     if (owner) return prefilter ? launch_render<false, true, true>(a, stream)

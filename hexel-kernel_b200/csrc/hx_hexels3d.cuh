@@ -18,6 +18,19 @@ constexpr float k3FilterSize = 0.707106f;
 constexpr float k3FilterInvSquare = 2.0f;
 constexpr float k3HexRadius = 1.15470053838f;
 constexpr float k3Log254 = 5.537334267f;
+// alpha from which the forward marks a (pixel block, list entry) pair as
+// blending: 1/255 lowered by a relative 1e-4, far more than the few ulp by
+// which the forward's and the backward's alpha of a pair can differ
+constexpr float k3BlendMarkAlpha = (1.0f / 255.0f) * (1.0f - 1e-4f);
+
+// Bits of the forward's blend mask covered by the warp `warp` of a CTA whose
+// warps cover 8 x (4 ppt) pixel blocks, two across: bit 2 q + x-half for each
+// 4-row quarter q of the 16x16 tile the warp's rows span.
+__host__ __device__ constexpr unsigned blend_bits(int warp, int ppt) {
+    unsigned bits = 0u;
+    for (int k = 0; k < ppt; ++k) bits |= 1u << (2 * ((warp >> 1) * ppt + k) + (warp & 1));
+    return bits;
+}
 
 // min/max with the reference's matrix-library semantics (ties and NaN pick x).
 __device__ __forceinline__ float glm_min(float x, float y) { return (y < x) ? y : x; }
@@ -177,6 +190,9 @@ struct Render3DArgs {
     int* median_index;
     // optional per-pixel count of blended (contributing) pairs, or null
     int* contrib_count;
+    // optional per-intersection mask of the 8x4 pixel blocks that met the
+    // surfel with alpha >= kBlendMarkAlpha while compositing, or null
+    unsigned char* blend_mask;
 };
 
 struct Backward3DArgs {
@@ -229,6 +245,8 @@ struct Backward3DArgs {
     const float* m1_surf;
     const float* m2_surf;
     const int* median_index;
+    // the forward's blend_mask, or null (no list entry skipped)
+    const unsigned char* blend_mask;
 };
 
 }  // namespace hx

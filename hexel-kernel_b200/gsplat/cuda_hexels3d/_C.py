@@ -194,6 +194,10 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
         else:
             surf_depth = surf_alpha = surf_maps = torch.empty((0,), **f32)
         contrib_count = torch.empty((H, W), **i32) if count_contrib else None
+        # per intersection: the 8x4 pixel blocks that may blend it (lets the
+        # backward skip the list entries no pixel of its block blends)
+        blend_mask = (torch.empty((max(num_rendered, 1),), dtype=torch.uint8, device=dev)
+                      if save else None)
         final_T = torch.empty((H, W), **f32) if save else torch.empty((0,), **f32)
         last_index = torch.empty((H, W), **i32) if save else torch.empty((0,), **i32)
         surf_state = None
@@ -228,7 +232,7 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                  *(ptr(t) for t in own) if own else (None,) * 6,
                  ptr(final_T) if save else None, ptr(last_index) if save else None,
                  *(ptr(t) for t in surf_state) if surf_state else (None,) * 5,
-                 ptr(contrib_count) if count_contrib else None, s)
+                 ptr(contrib_count) if count_contrib else None, ptr(blend_mask), s)
         _mark("render_fwd")
         if debug:
             torch.cuda.synchronize(dev)
@@ -240,7 +244,8 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
     return dict(out_color=out_color, radii=radii, contrib=contrib, overdraw=overdraw,
                 overdraw_hits=overdraw_hits, surf_depth=surf_depth, surf_alpha=surf_alpha,
                 surf_maps=surf_maps, saved=saved, surf_state=surf_state, normals=normals,
-                owner=own, num_rendered=num_rendered, contrib_count=contrib_count)
+                owner=own, num_rendered=num_rendered, contrib_count=contrib_count,
+                blend_mask=blend_mask)
 
 
 def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, color_quads,
@@ -250,13 +255,14 @@ def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, col
                    image_height, tan_fovx, tan_fovy, softness, scale_modifier, color_model,
                    view_model, use_view_grads, overdraw_base_count, prefilter_edge_on,
                    conservative_bounds, debug, saved, surf_state=None, surf_normals=None,
-                   accumulate_into=None):
+                   accumulate_into=None, blend_mask=None):
     """rasterize_hexels3d_backward_impl (hexels3d_forward.cu:4882-5582) on the
     forward's saved state.  With `accumulate_into` (a dict from parameter
     name -- means3d, scales, rotations, colors, color_grads, view_grads,
     opacities -- to float32 buffers of the parameters' shapes) those gradients
     are added into the given buffers instead of returned fresh: gradient
-    accumulation over views without a separate pass."""
+    accumulation over views without a separate pass.  `blend_mask` is the
+    forward's per-intersection mask of the same binning (or None)."""
     W, H = int(image_width), int(image_height)
     P, stride = _checks(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
                         specular_ks, specular_log_s, opacities, softnesses, viewmatrix,
@@ -288,6 +294,10 @@ def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, col
     (radii, transMats, opacities_out, softnesses_out, view_dirs, normals_saved, points_xy_center,
      ranges, values_sorted, final_T, last_index) = saved
     num_rendered = values_sorted.numel()
+    if blend_mask is not None:
+        check_input(blend_mask, "blend_mask")
+        _check(blend_mask.dtype == torch.uint8 and blend_mask.numel() >= num_rendered,
+               "blend_mask must be uint8 with one entry per intersection")
     stride2d = means2d.size(1) if means2d.numel() > 0 else 3
     has_surface = (grad_out_surf_depth.numel() > 0 or grad_out_surf_alpha.numel() > 0 or
                    grad_out_surf_normals.numel() > 0)
@@ -358,7 +368,8 @@ def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, col
                      means2d.numel() > 0 else None, ptr(grad_view_dirs), ptr(grad_normals),
                      int(overdraw_base_count), int(color_model), int(bool(use_view_grads)),
                      ptr(final_T), ptr(last_index),
-                     *(ptr(t) for t in surf_state) if has_surface else (None,) * 5, s)
+                     *(ptr(t) for t in surf_state) if has_surface else (None,) * 5,
+                     ptr(blend_mask), s)
             _mark("render_bwd")
             lib.call("hx_hexels3d_geometry_backward", P, num_rendered, ptr(means3d), ptr(scales),
                      float(scale_modifier), ptr(rotations), ptr(projmatrix), ptr(campos), W, H,
@@ -479,7 +490,8 @@ def rasterize_hexels3d_backward(*args):
                       False, return_surface=surface, overdraw_base_count=odb,
                       return_median_depth=median, save=True, save_surface=surface)
     return _backward_core(*args, o["saved"], surf_state=o["surf_state"],
-                          surf_normals=o["normals"] if surface else None)
+                          surf_normals=o["normals"] if surface else None,
+                          blend_mask=o["blend_mask"])
 
 
 def _not_provided(name: str):

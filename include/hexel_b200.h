@@ -321,7 +321,13 @@ HX_API int hx_hexels3d_bin(int P, int num_rendered, int image_width, int image_h
  * (H,W) for the surface backward.  points_xy_center non-NULL selects the
  * prefilter path.  contrib_count (H,W int32, may be NULL; no reference
  * counterpart) receives the number of blended (pixel, surfel) pairs per pixel,
- * the work unit of the backward traversal. */
+ * the work unit of the backward traversal.  blend_mask (num_rendered uint8,
+ * may be NULL; no reference counterpart) receives, per sorted intersection of
+ * every list entry the traversal staged, bit w (w = 2 * (y / 4) + x / 8 for
+ * the pixel (x, y) within its 16x16 tile) set when a pixel of that 8x4 block
+ * still compositing met the surfel with alpha >= (1 - 1e-4) / 255: a superset
+ * of the pairs the backward blends, which hx_hexels3d_render_backward uses to
+ * skip the others. */
 HX_API int hx_hexels3d_render_forward(
     int P, int num_rendered, const int32_t* ranges, const int32_t* point_list,
     const float* points_xy_center, int image_width, int image_height, const float* colors,
@@ -334,14 +340,17 @@ HX_API int hx_hexels3d_render_forward(
     float* out_alpha, float* out_surface, int64_t* owner_id, float* owner_weight,
     float* owner_uv, float* owner_sdf, float* owner_depth, float* total_alpha, float* final_T,
     int32_t* last_index, float* final_T_surf, int32_t* last_index_surf, float* m1_surf,
-    float* m2_surf, int32_t* median_index, int32_t* contrib_count, cudaStream_t stream);
+    float* m2_surf, int32_t* median_index, int32_t* contrib_count, uint8_t* blend_mask,
+    cudaStream_t stream);
 
 /* Reverse traversal VJP; replaces render_hexels3d_backward<S,F> and its
  * launches (hexels3d_forward.cu:1749-2492, 5323-5505).  Uses the forward's
  * saved final_T/last_index (and the surface state when surface gradients are
  * given).  All gradient outputs are ACCUMULATED (clear them first);
  * grad_transMats (P,9), grad_view_dirs (P,3) and grad_normals (P,3) are
- * intermediates for hx_hexels3d_geometry_backward. */
+ * intermediates for hx_hexels3d_geometry_backward.  blend_mask (may be NULL)
+ * is the forward's per-intersection mask of the same call's lists: list
+ * entries whose bits are clear for a warp's pixel block are skipped. */
 HX_API int hx_hexels3d_render_backward(
     int P, int num_rendered, const int32_t* ranges, const int32_t* point_list,
     const float* points_xy_center, float* grad_points_xy_center, int image_width,
@@ -358,7 +367,7 @@ HX_API int hx_hexels3d_render_backward(
     float* grad_normals, int overdraw_base_count, int color_model, int use_view_grads,
     const float* final_T, const int32_t* last_index, const float* final_T_surf,
     const int32_t* last_index_surf, const float* m1_surf, const float* m2_surf,
-    const int32_t* median_index, cudaStream_t stream);
+    const int32_t* median_index, const uint8_t* blend_mask, cudaStream_t stream);
 
 /* VJP from transforms (and view directions / normals) to means3d, scales and
  * WXYZ rotations, plus the screen-gradient proxy for means2d and the

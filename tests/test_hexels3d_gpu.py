@@ -122,6 +122,37 @@ def test_cached_forward_backward_matches_reference(ref, cm, vm, soft, pre, cons)
         assert_grad_parity(a, b, None, n)
 
 
+@pytest.mark.parametrize("surface", [False, True])
+@pytest.mark.parametrize("cm,vm,soft,pre,cons", CASES)
+def test_blend_mask_backward_equals_unmasked(cm, vm, soft, pre, cons, surface):
+    """The forward's blend mask only lets the backward skip list entries no
+    pixel of a warp's block blends: gradients with and without it agree (to
+    the order of the float atomics), and the mask does skip entries."""
+    from gsplat.cuda_hexels3d import _C
+
+    w, cam, extra = _scene(seed=8)
+    t, s = _args(w, cam, extra, cm, vm, soft)
+    H, W = cam.height, cam.width
+    f = _C._forward_core(*t, *s, pre, cons, False, return_surface=surface, save=True,
+                         save_surface=surface)
+    n = f["num_rendered"]
+    mask = f["blend_mask"]
+    assert mask.dtype == torch.uint8 and mask.numel() >= n
+    assert bool((mask[:n] != 0xFF).any())
+    gc, surf = _grad_outputs(H, W, seed=3, surf_channels=4 if surface else 0)
+    e = torch.empty(0, device="cuda")
+    gd, ga, gn = surf if surface else (e, e, e)
+
+    def run(bm):
+        return _C._backward_core(t[0], e, *t[1:], gc, e, gd, ga, gn, *s, -1, pre, cons, False,
+                                 f["saved"], surf_state=f["surf_state"],
+                                 surf_normals=f["normals"] if surface else None, blend_mask=bm)
+
+    for name, a, b in zip(GRAD_NAMES, run(mask), run(None)):
+        assert a.shape == b.shape, name
+        assert_grad_parity(a, b, None, name)
+
+
 @pytest.mark.parametrize("median", [False, True])
 def test_surface_forward_backward_matches_reference(ref, median):
     if ref is None:

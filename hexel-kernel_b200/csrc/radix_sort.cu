@@ -1,12 +1,14 @@
 // Stable LSD radix sort of (key, int32 value) pairs, 8-bit digits.
 //
 // Each pass is reduce-then-scan and waits on nothing across CTAs:
-//   1. upsweep  — per-CTA digit histogram of a 4096-key tile,
+//   1. upsweep  — per-CTA digit histogram of a tile of 256 x ITEMS keys
+//      (ITEMS = 16 for large inputs, 4 below 2M keys so that a pass over a
+//      million keys still spreads over ~1000 CTAs),
 //   2. scan     — per-digit exclusive scan over CTAs (digit-major layout),
 //   3. downsweep — stable in-tile ranking (warp match + per-warp running
 //      counters), reorder through shared memory, coalesced scatter.
-// Stability: within a tile, warp w owns keys [512w, 512w+512) and processes
-// them 32 at a time in index order, so equal digits keep their input order;
+// Stability: within a tile, warp w owns keys [32 ITEMS w, 32 ITEMS (w + 1))
+// and processes them 32 at a time in index order, so equal digits keep their input order;
 // tiles are ordered by the scan.  This replaces the stable CUB / PyTorch radix
 // sorts the reference calls (gsplat/utils.py:159, hexels3d_forward.cu:3013).
 #include "hx_common.cuh"
@@ -16,16 +18,17 @@ namespace hx {
 
 constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
-constexpr int kSortItems = 16;
-constexpr int kSortTile = kSortThreads * kSortItems;  // 4096 keys per CTA
 constexpr int kRadix = 256;
+constexpr int kSmallSortN = 1 << 21;  // below: 4 keys per thread, else 16
+
+inline int sort_items(int n) { return n < kSmallSortN ? 4 : 16; }
 
 template <typename K>
 __device__ __forceinline__ unsigned digit_of(K key, int shift, unsigned mask) {
     return (unsigned)(key >> shift) & mask;
 }
 
-template <typename K>
+template <typename K, int ITEMS>
 __global__ void __launch_bounds__(kSortThreads) sort_upsweep_kernel(const K* __restrict__ keys,
                                                                     int n, int shift,
                                                                     unsigned mask,
@@ -37,9 +40,10 @@ __global__ void __launch_bounds__(kSortThreads) sort_upsweep_kernel(const K* __r
     for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads)
         (&s_hist[0][0])[i] = 0;
     __syncthreads();
-    const int base = blockIdx.x * kSortTile + warp * (kSortTile / kSortWarps);
+    constexpr int kTile = kSortThreads * ITEMS;
+    const int base = blockIdx.x * kTile + warp * (kTile / kSortWarps);
 #pragma unroll 4
-    for (int i = 0; i < kSortItems; ++i) {
+    for (int i = 0; i < ITEMS; ++i) {
         const int idx = base + i * 32 + lane;
         if (idx < n) atomicAdd(&s_hist[warp][digit_of(keys[idx], shift, mask)], 1);
     }
@@ -91,15 +95,16 @@ __global__ void __launch_bounds__(256) sort_scan_kernel(int* __restrict__ hist, 
     if (threadIdx.x == 0) digit_totals[d] = s_carry;
 }
 
-template <typename K>
+template <typename K, int ITEMS>
 __global__ void __launch_bounds__(kSortThreads) sort_downsweep_kernel(
     const K* __restrict__ keys_in, const int* __restrict__ vals_in, K* __restrict__ keys_out,
     int* __restrict__ vals_out, int n, int shift, unsigned mask, const int* __restrict__ hist,
     const int* __restrict__ digit_totals, int num_tiles) {
+    constexpr int kTile = kSortThreads * ITEMS;
     extern __shared__ __align__(16) unsigned char s_raw[];
     K* s_keys = reinterpret_cast<K*>(s_raw);
-    int* s_vals = reinterpret_cast<int*>(s_raw + sizeof(K) * kSortTile);
-    int* s_cnt = s_vals + kSortTile;              // [kSortWarps][kRadix]
+    int* s_vals = reinterpret_cast<int*>(s_raw + sizeof(K) * kTile);
+    int* s_cnt = s_vals + kTile;                  // [kSortWarps][kRadix]
     int* s_local_start = s_cnt + kSortWarps * kRadix;  // [kRadix]
     int* s_global = s_local_start + kRadix;       // [kRadix]
     __shared__ int s_warp_sums[kSortWarps];
@@ -107,8 +112,8 @@ __global__ void __launch_bounds__(kSortThreads) sort_downsweep_kernel(
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const unsigned lanemask_lt = (1u << lane) - 1u;
-    const int tile_base = blockIdx.x * kSortTile;
-    const int tile_n = min(kSortTile, n - tile_base);
+    const int tile_base = blockIdx.x * kTile;
+    const int tile_n = min(kTile, n - tile_base);
 
     for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) s_cnt[i] = 0;
 
@@ -132,13 +137,13 @@ __global__ void __launch_bounds__(kSortThreads) sort_downsweep_kernel(
         s_global[d] = wpre + inc - tot + hist[(size_t)d * num_tiles + blockIdx.x];
     }
 
-    K key[kSortItems];
-    int val[kSortItems];
-    int rank[kSortItems];
-    unsigned dig[kSortItems];
-    const int wbase = tile_base + warp * (kSortTile / kSortWarps);
+    K key[ITEMS];
+    int val[ITEMS];
+    int rank[ITEMS];
+    unsigned dig[ITEMS];
+    const int wbase = tile_base + warp * (kTile / kSortWarps);
 #pragma unroll
-    for (int i = 0; i < kSortItems; ++i) {
+    for (int i = 0; i < ITEMS; ++i) {
         const int idx = wbase + i * 32 + lane;
         const bool ok = idx < n;
         key[i] = ok ? keys_in[idx] : K(0);
@@ -151,7 +156,7 @@ __global__ void __launch_bounds__(kSortThreads) sort_downsweep_kernel(
     // before this 32-key step + number of lower lanes with the same digit.
     int* my_cnt = s_cnt + warp * kRadix;
 #pragma unroll
-    for (int i = 0; i < kSortItems; ++i) {
+    for (int i = 0; i < ITEMS; ++i) {
         const bool ok = dig[i] != 0xFFFFu;
         const unsigned active = __ballot_sync(0xffffffffu, ok);
         unsigned peers = __match_any_sync(0xffffffffu, dig[i]);
@@ -199,7 +204,7 @@ __global__ void __launch_bounds__(kSortThreads) sort_downsweep_kernel(
     __syncthreads();
 
 #pragma unroll
-    for (int i = 0; i < kSortItems; ++i) {
+    for (int i = 0; i < ITEMS; ++i) {
         if (dig[i] != 0xFFFFu) {
             const int pos = s_local_start[dig[i]] + s_cnt[warp * kRadix + dig[i]] + rank[i];
             s_keys[pos] = key[i];
@@ -219,9 +224,55 @@ __global__ void __launch_bounds__(kSortThreads) sort_downsweep_kernel(
 
 template <typename K>
 size_t sort_workspace_bytes(int n) {
-    const int tiles = ceil_div(n > 0 ? n : 1, kSortTile);
+    // histogram sized for the smaller tiles, which need the most rows
+    const int tiles = ceil_div(n > 0 ? n : 1, kSortThreads * 4);
     return align256(sizeof(K) * (size_t)n) + align256(sizeof(int) * (size_t)n) +
            align256(sizeof(int) * (size_t)kRadix * tiles) + align256(sizeof(int) * kRadix);
+}
+
+template <typename K, int ITEMS>
+int sort_passes(const K* keys_in, const int* vals_in, K* keys_out, int* vals_out, int n,
+                int begin_bit, int end_bit, K* alt_keys, int* alt_vals, int* hist, int* totals,
+                cudaStream_t stream) {
+    constexpr int kTile = kSortThreads * ITEMS;
+    const int tiles = ceil_div(n, kTile);
+    const size_t smem = sizeof(K) * kTile + sizeof(int) * kTile +
+                        sizeof(int) * (kSortWarps * kRadix + 2 * kRadix);
+    static bool attr_set[64] = {};
+    int dev = 0;
+    HX_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        HX_CUDA_TRY(cudaFuncSetAttribute(sort_downsweep_kernel<K, ITEMS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    const int bits = end_bit - begin_bit;
+    const int passes = (bits + 7) / 8;
+    int shift = begin_bit;
+    const K* src_k = keys_in;
+    const int* src_v = vals_in;
+    for (int p_i = 0; p_i < passes; ++p_i) {
+        // Spread the bits evenly over the passes.
+        const int remaining = end_bit - shift;
+        const int pass_bits = (remaining + (passes - p_i) - 1) / (passes - p_i);
+        const unsigned mask = (1u << pass_bits) - 1u;
+        // The last pass writes the caller's output buffers.
+        const bool to_out = ((passes - 1 - p_i) % 2) == 0;
+        K* dst_k = to_out ? keys_out : alt_keys;
+        int* dst_v = to_out ? vals_out : alt_vals;
+        sort_upsweep_kernel<K, ITEMS><<<tiles, kSortThreads, 0, stream>>>(src_k, n, shift, mask,
+                                                                         hist, tiles);
+        HX_LAUNCH_CHECK("sort_upsweep_kernel");
+        sort_scan_kernel<<<kRadix, 256, 0, stream>>>(hist, tiles, totals);
+        HX_LAUNCH_CHECK("sort_scan_kernel");
+        sort_downsweep_kernel<K, ITEMS><<<tiles, kSortThreads, smem, stream>>>(
+            src_k, src_v, dst_k, dst_v, n, shift, mask, hist, totals, tiles);
+        HX_LAUNCH_CHECK("sort_downsweep_kernel");
+        src_k = dst_k;
+        src_v = dst_v;
+        shift += pass_bits;
+    }
+    return HX_OK;
 }
 
 template <typename K>
@@ -243,53 +294,20 @@ int sort_pairs(const K* keys_in, const int* vals_in, K* keys_out, int* vals_out,
                                     cudaMemcpyDeviceToDevice, stream));
         return HX_OK;
     }
-    const int tiles = ceil_div(n, kSortTile);
+    const int max_tiles = ceil_div(n, kSortThreads * 4);
     char* p = (char*)ws;
     K* alt_keys = (K*)p;
     p += align256(sizeof(K) * (size_t)n);
     int* alt_vals = (int*)p;
     p += align256(sizeof(int) * (size_t)n);
     int* hist = (int*)p;
-    p += align256(sizeof(int) * (size_t)kRadix * tiles);
+    p += align256(sizeof(int) * (size_t)kRadix * max_tiles);
     int* totals = (int*)p;
-
-    const size_t smem = sizeof(K) * kSortTile + sizeof(int) * kSortTile +
-                        sizeof(int) * (kSortWarps * kRadix + 2 * kRadix);
-    static bool attr_set[64] = {};
-    int dev = 0;
-    HX_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        HX_CUDA_TRY(cudaFuncSetAttribute(sort_downsweep_kernel<K>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
-
-    const int passes = (bits + 7) / 8;
-    int shift = begin_bit;
-    const K* src_k = keys_in;
-    const int* src_v = vals_in;
-    for (int p_i = 0; p_i < passes; ++p_i) {
-        // Spread the bits evenly over the passes.
-        const int remaining = end_bit - shift;
-        const int pass_bits = (remaining + (passes - p_i) - 1) / (passes - p_i);
-        const unsigned mask = (1u << pass_bits) - 1u;
-        // The last pass writes the caller's output buffers.
-        const bool to_out = ((passes - 1 - p_i) % 2) == 0;
-        K* dst_k = to_out ? keys_out : alt_keys;
-        int* dst_v = to_out ? vals_out : alt_vals;
-        sort_upsweep_kernel<K><<<tiles, kSortThreads, 0, stream>>>(src_k, n, shift, mask, hist,
-                                                                  tiles);
-        HX_LAUNCH_CHECK("sort_upsweep_kernel");
-        sort_scan_kernel<<<kRadix, 256, 0, stream>>>(hist, tiles, totals);
-        HX_LAUNCH_CHECK("sort_scan_kernel");
-        sort_downsweep_kernel<K><<<tiles, kSortThreads, smem, stream>>>(
-            src_k, src_v, dst_k, dst_v, n, shift, mask, hist, totals, tiles);
-        HX_LAUNCH_CHECK("sort_downsweep_kernel");
-        src_k = dst_k;
-        src_v = dst_v;
-        shift += pass_bits;
-    }
-    return HX_OK;
+    if (sort_items(n) == 4)
+        return sort_passes<K, 4>(keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit,
+                                 alt_keys, alt_vals, hist, totals, stream);
+    return sort_passes<K, 16>(keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit,
+                              alt_keys, alt_vals, hist, totals, stream);
 }
 
 template int sort_pairs<uint32_t>(const uint32_t*, const int*, uint32_t*, int*, int, int, int,

@@ -619,9 +619,13 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
 #pragma unroll
             for (int c = 0; c < N; ++c) acc[c] = 0.f;
             bool contributed = false;
+            // the mask has one bit per 8x4 half of the block: a half whose
+            // bit is clear blends nothing of this entry (warp-uniform skip)
+            const unsigned bm = s_bm[idx - bstart];
 #pragma unroll
             for (int k = 0; k < PPT; ++k)
-                contributed |= bwd_pair<SURF, PREFILTER, N>(a, L, O, s, idx, q[k], acc);
+                if (bm & (1u << (2 * ((warp >> 1) * PPT + k) + (warp & 1))))
+                    contributed |= bwd_pair<SURF, PREFILTER, N>(a, L, O, s, idx, q[k], acc);
             if (__any_sync(0xffffffffu, contributed)) {
                 float* dst = s_acc + (idx - bstart) * L.ncomp;
                 if constexpr (N == 24) {

@@ -430,6 +430,8 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
     Surfel3D* s_prim = reinterpret_cast<Surfel3D*>(s_raw);
     float* s_acc = reinterpret_cast<float*>(s_raw + sizeof(Surfel3D) * kBatch);
     __shared__ int s_max_visit;
+    // the staged records' pixel boxes, packed (the compaction reads one per lane)
+    __shared__ short4 s_box[kBatch];
     // per warp: the batch slots whose pixel box meets the warp's block
     __shared__ unsigned char s_list[kThreads / 32][kBatch];
     // the forward's blend-mask bytes of the batch's list entries
@@ -538,60 +540,7 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
             int g = a.point_list[range.x + bstart + t];
             g = min(max(g, 0), a.P - 1);
             s_bm[t] = a.blend_mask ? a.blend_mask[range.x + bstart + t] : (unsigned char)0xff;
-            Surfel3D& s = s_prim[t];
-            s.id = g;
-            const float* Tm = a.transMats + 9 * g;
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                s.tu[c] = Tm[c];
-                s.tv[c] = Tm[3 + c];
-                s.tw[c] = Tm[6 + c];
-            }
-            s.opacity = a.opacities[g];
-            if (a.softness_stride == 3) {
-                s.s0 = a.softnesses[3 * g];
-                s.s1 = a.softnesses[3 * g + 1];
-                s.s2 = a.softnesses[3 * g + 2];
-            } else {
-                s.s0 = s.s1 = s.s2 = a.softnesses[g];
-            }
-#pragma unroll
-            for (int c = 0; c < 3; ++c) s.cb[c] = a.colors[3 * g + c];
-            if (a.color_model >= kColorLinear) {
-#pragma unroll
-                for (int c = 0; c < 3; ++c) {
-                    s.gu[c] = a.color_grads[6 * g + c];
-                    s.gv[c] = a.color_grads[6 * g + 3 + c];
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < 3; ++c) s.gu[c] = s.gv[c] = 0.f;
-            }
-            if (a.use_view_grads) {
-                const float* vd = a.view_dirs + 3 * g;
-                const float* vg = a.view_grads + 9 * g;
-                s.cv[0] = vd[0] * vg[0] + vd[1] * vg[1] + vd[2] * vg[2];
-                s.cv[1] = vd[0] * vg[3] + vd[1] * vg[4] + vd[2] * vg[5];
-                s.cv[2] = vd[0] * vg[6] + vd[1] * vg[7] + vd[2] * vg[8];
-            } else {
-                s.cv[0] = s.cv[1] = s.cv[2] = 0.f;
-            }
-            if (SURF && a.normals) {
-                float3 n = {a.normals[3 * g], a.normals[3 * g + 1], a.normals[3 * g + 2]};
-                const float sg = normal_sign(n, a.view_dirs + 3 * g);
-                s.n[0] = sg * n.x;
-                s.n[1] = sg * n.y;
-                s.n[2] = sg * n.z;
-                s.nsign = sg;
-            } else {
-                s.n[0] = s.n[1] = s.n[2] = 0.f;
-                s.nsign = 1.f;
-            }
-            if (PREFILTER) {
-                s.q.ctr = a.points_xy_center[g];
-            } else {
-                s.q.box = surfel_pixel_box(s, W, H);
-            }
+            s_box[t] = stage_surfel<SURF, PREFILTER>(a, g, W, H, &s_prim[t]);
         }
         for (int t = tr; t < kBatch * L.ncomp; t += kThreads) s_acc[t] = 0.f;
         __syncthreads();
@@ -605,7 +554,7 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
         for (int base = 0; base < n_slots; base += 32) {
             const int t = base + lane;
             const bool hit = t < n_slots && (s_bm[t] & my_bits) != 0u &&
-                             (PREFILTER || !box_misses(s_prim[t].q.box, wx0, wy0, wx0 + 7,
+                             (PREFILTER || !box_misses(s_box[t], wx0, wy0, wx0 + 7,
                                                        wy0 + kWarpRows - 1));
             const unsigned m = __ballot_sync(0xffffffffu, hit);
             if (hit) s_list[warp][n_mine + __popc(m & ((1u << lane) - 1u))] = (unsigned char)t;

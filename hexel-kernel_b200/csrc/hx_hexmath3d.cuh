@@ -23,6 +23,7 @@ struct __align__(16) Surfel3D {
     float nsign;     // the sign applied to that normal
     int id;
 };
+static_assert(sizeof(Surfel3D) == 128, "a staged surfel is eight 16-byte chunks");
 
 // The staged surfel's pixel box: the screen bounds of the hexagon outside
 // which its alpha is below 1/255 (the bound the reference's preprocess uses
@@ -159,6 +160,78 @@ __device__ __forceinline__ void bounded_coords_vjp(const float u, const float v,
 
 __device__ __forceinline__ float normal_sign(const float3 n, const float* vd) {
     return n.x * vd[0] + n.y * vd[1] + n.z * vd[2] > 0.f ? -1.f : 1.f;
+}
+
+// Stages surfel g into its shared-memory row `row` (the per-surfel terms of
+// both compositing kernels) and returns its pixel box (unbounded with the
+// prefilter).  The record is written as eight 16-byte chunks, each as soon as
+// its fields are loaded: a quarter-warp of such stores (one record per lane)
+// is 8-way bank conflicted where field-by-field stores were 32-way, and the
+// record is never held in registers whole.
+template <bool SURF, bool PREFILTER, typename Args>
+__device__ __forceinline__ short4 stage_surfel(const Args& a, int g, int W, int H,
+                                               Surfel3D* row) {
+    float4* dst = reinterpret_cast<float4*>(row);
+    Surfel3D s;  // the fields the box needs
+    const float* Tm = a.transMats + 9 * g;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        s.tu[c] = Tm[c];
+        s.tv[c] = Tm[3 + c];
+        s.tw[c] = Tm[6 + c];
+    }
+    s.opacity = a.opacities[g];
+    if (a.softness_stride == 3) {
+        s.s0 = a.softnesses[3 * g];
+        s.s1 = a.softnesses[3 * g + 1];
+        s.s2 = a.softnesses[3 * g + 2];
+    } else {
+        s.s0 = s.s1 = s.s2 = a.softnesses[g];
+    }
+    dst[0] = make_float4(s.tu[0], s.tu[1], s.tu[2], s.tv[0]);
+    dst[1] = make_float4(s.tv[1], s.tv[2], s.tw[0], s.tw[1]);
+    dst[2] = make_float4(s.tw[2], s.opacity, s.s0, s.s1);
+    union {
+        short4 box;
+        float2 f;
+    } q;
+    short4 box;
+    if (PREFILTER) {
+        q.f = a.points_xy_center[g];
+        box = make_short4(-32768, -32768, 32767, 32767);
+    } else {
+        box = surfel_pixel_box(s, W, H);
+        q.box = box;
+    }
+    dst[3] = make_float4(s.s2, a.colors[3 * g], a.colors[3 * g + 1], a.colors[3 * g + 2]);
+    float cv0 = 0.f, cv1 = 0.f, cv2 = 0.f;
+    if (a.use_view_grads) {
+        const float* vd = a.view_dirs + 3 * g;
+        const float* vg = a.view_grads + 9 * g;
+        cv0 = vd[0] * vg[0] + vd[1] * vg[1] + vd[2] * vg[2];
+        cv1 = vd[0] * vg[3] + vd[1] * vg[4] + vd[2] * vg[5];
+        cv2 = vd[0] * vg[6] + vd[1] * vg[7] + vd[2] * vg[8];
+    }
+    float gu[3] = {0.f, 0.f, 0.f}, gv[3] = {0.f, 0.f, 0.f};
+    if (a.color_model >= kColorLinear) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            gu[c] = a.color_grads[6 * g + c];
+            gv[c] = a.color_grads[6 * g + 3 + c];
+        }
+    }
+    dst[4] = make_float4(cv0, cv1, cv2, gu[0]);
+    dst[5] = make_float4(gu[1], gu[2], gv[0], gv[1]);
+    float3 n = {0.f, 0.f, 0.f};
+    float nsign = 1.f;
+    if (SURF && a.normals) {
+        n = {a.normals[3 * g], a.normals[3 * g + 1], a.normals[3 * g + 2]};
+        nsign = normal_sign(n, a.view_dirs + 3 * g);
+        n = {nsign * n.x, nsign * n.y, nsign * n.z};
+    }
+    dst[6] = make_float4(gv[2], n.x, n.y, n.z);
+    dst[7] = make_float4(q.f.x, q.f.y, nsign, __int_as_float(g));
+    return box;
 }
 
 // Ray-splat intersection of pixel (px, py) with a surfel of transform rows

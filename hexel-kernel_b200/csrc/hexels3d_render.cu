@@ -234,60 +234,7 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const R
             if ((int)range.x + progress >= (int)range.y) continue;
             int g = a.point_list[range.x + progress];
             g = min(max(g, 0), a.P - 1);
-            Surfel3D& s = s_prim[t];
-            s.id = g;
-            const float* Tm = a.transMats + 9 * g;
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                s.tu[c] = Tm[c];
-                s.tv[c] = Tm[3 + c];
-                s.tw[c] = Tm[6 + c];
-            }
-            s.opacity = a.opacities[g];
-            if (a.softness_stride == 3) {
-                s.s0 = a.softnesses[3 * g];
-                s.s1 = a.softnesses[3 * g + 1];
-                s.s2 = a.softnesses[3 * g + 2];
-            } else {
-                s.s0 = s.s1 = s.s2 = a.softnesses[g];
-            }
-#pragma unroll
-            for (int c = 0; c < 3; ++c) s.cb[c] = a.colors[3 * g + c];
-            if (a.color_model >= kColorLinear) {
-#pragma unroll
-                for (int c = 0; c < 3; ++c) {
-                    s.gu[c] = a.color_grads[6 * g + c];
-                    s.gv[c] = a.color_grads[6 * g + 3 + c];
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < 3; ++c) s.gu[c] = s.gv[c] = 0.f;
-            }
-            if (a.use_view_grads) {
-                const float* vd = a.view_dirs + 3 * g;
-                const float* vg = a.view_grads + 9 * g;
-                s.cv[0] = vd[0] * vg[0] + vd[1] * vg[1] + vd[2] * vg[2];
-                s.cv[1] = vd[0] * vg[3] + vd[1] * vg[4] + vd[2] * vg[5];
-                s.cv[2] = vd[0] * vg[6] + vd[1] * vg[7] + vd[2] * vg[8];
-            } else {
-                s.cv[0] = s.cv[1] = s.cv[2] = 0.f;
-            }
-            if (SURF) {
-                float3 n = {a.normals[3 * g], a.normals[3 * g + 1], a.normals[3 * g + 2]};
-                const float sg = normal_sign(n, a.view_dirs + 3 * g);
-                s.n[0] = sg * n.x;
-                s.n[1] = sg * n.y;
-                s.n[2] = sg * n.z;
-                s.nsign = sg;
-            } else {
-                s.n[0] = s.n[1] = s.n[2] = 0.f;
-                s.nsign = 1.f;
-            }
-            if (PREFILTER) {
-                s.q.ctr = a.points_xy_center[g];
-            } else {
-                s.q.box = surfel_pixel_box(s, W, H);
-            }
+            stage_surfel<SURF, PREFILTER>(a, g, W, H, &s_prim[t]);
         }
         __syncthreads();
 

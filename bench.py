@@ -41,7 +41,7 @@ sys.path.insert(0, ROOT)
 
 import torch  # noqa: E402
 
-from sharding import GradBuffer, stripe_rows, view_split  # noqa: E402
+from sharding import GradBuffer, balance_views, stripe_rows, view_split  # noqa: E402
 
 METRIC = "fwd+bwd Mpix/s"
 UNIT = "Mpix/s"
@@ -782,6 +782,41 @@ class Hexels3DStep:
         for (_, a), (name, b) in zip(self.marks[:-1], self.marks[1:]):
             self.stage_ms[name] += a.elapsed_time(b)
 
+    def view_ms(self):
+        """Device time of each of this rank's views in the last run (from the
+        previous view's end, or the step's start, to the view's end)."""
+        out, start = [], None
+        for name, ev in self.marks:
+            if name == "start":
+                start = ev
+            elif name == "accumulate":
+                out.append(start.elapsed_time(ev))
+                start = ev
+        return out
+
+    def rebalance(self):
+        """Re-deal the views over the ranks by the device time each took in
+        the last run (one all-reduce of a per-view vector; every rank computes
+        the same split), then load the cameras and targets of the new set."""
+        if self.world == 1:
+            return
+        import torch.distributed as dist
+
+        nviews = len(self.w.cameras)
+        costs = torch.zeros(nviews, dtype=torch.float64, device=self.dev)
+        for v, ms in zip(self.views, self.view_ms()):
+            costs[v] = ms
+        dist.all_reduce(costs)
+        views = balance_views(costs.tolist(), self.world)[self.rank]
+        if views == self.views:
+            return
+        have = dict(zip(self.views, self.targets))
+        new = [v for v in views if v not in have]
+        have.update(zip(new, make_targets(self.w, new, self.dev)))
+        self.views = views
+        self.cams = [self.w.cameras[v].to(self.dev) for v in views]
+        self.targets = [have[v] for v in views]
+
 
 def time_step_3d(step, steps, warmup, world):
     """Warm-up (the first one collects the work counts), then `steps` timed
@@ -792,7 +827,12 @@ def time_step_3d(step, steps, warmup, world):
 
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     for i in range(warmup):
-        step.run(keep_info=(i == 0))
+        step.run(keep_info=(i == warmup - 1))
+        if i == 1 and world > 1:
+            # deal the views by the device time each took in this run (the
+            # first run pays one-time set-up and is not representative)
+            torch.cuda.synchronize()
+            step.rebalance()
     torch.cuda.synchronize()
     step.stage_ms = {k: 0.0 for k in step.STAGES}
     barrier(world)
@@ -852,7 +892,7 @@ def run_ours_3d(args, world, rank, local):
     clk = clocks.stop()
     nviews = len(w.cameras)
     rendered_rank = sum(step.info.get("num_rendered", [0]))
-    e2e = None if args.skip_extras else run_e2e_3d(w, args, world, rank, surface)
+    e2e = None if args.skip_extras else run_e2e_3d(w, args, world, rank, surface, step.views)
     secondary = None
     if world == 1 and not args.skip_extras and not surface:
         secondary = single_view_comparison(args)
@@ -879,8 +919,10 @@ def run_ours_3d(args, world, rank, local):
             "outputs": "rgb + depth + alpha + normal + distortion" if surface else "rgb",
             "color_model": "linear", "view_model": "linear",
             "intersections_per_view": round(rendered_rank / max(1, len(step.views))),
-            "parallelism": (f"views dealt round-robin over {world} GPUs, surfels replicated, "
-                            "gradients NCCL all-reduced") if world > 1 else "single GPU",
+            "parallelism": (f"views dealt over {world} GPUs by the device time each took in "
+                            "the second warm-up step (longest first to the least-loaded rank), "
+                            "surfels replicated, gradients NCCL all-reduced")
+                           if world > 1 else "single GPU",
             "l2": "flushed between timed steps (256 MB write)",
         },
         "stages_ms": {k: round(v, 4) for k, v in stage_ms.items()},
@@ -920,13 +962,15 @@ def single_view_comparison(args):
     return out
 
 
-def run_e2e_3d(w, args, world, rank, surface):
+def run_e2e_3d(w, args, world, rank, surface, views=None):
     """The step through gsplat.rasterize_hexels3d (autograd), the surfel
     parameters and this rank's target images copied from pinned host memory
-    every step and the loss read back."""
+    every step and the loss read back.  `views`: this rank's views (default:
+    round-robin)."""
     import gsplat
 
-    views = view_split(len(w.cameras), world, rank)
+    if views is None:
+        views = view_split(len(w.cameras), world, rank)
     host_params = [t.pin_memory() for t in (w.means3d, w.scales, w.rotations, w.colors,
                                            w.color_grads, w.view_grads, w.opacities)]
     host_targets = [t.pin_memory() for t in make_targets(w, views, "cpu")]

@@ -1,8 +1,9 @@
 """Multi-GPU partitioning of the rasteriser workloads (one process per GPU).
 
-* 3D multi-view: views are dealt round-robin, rank g renders the views
-  v = g (mod world); surfels are replicated and each rank sums its views'
-  per-surfel gradients into one flat buffer, all-reduced once per step.
+* 3D multi-view: views are dealt round-robin (rank g renders the views
+  v = g (mod world)), or by measured cost (balance_views); surfels are
+  replicated and each rank sums its views' per-surfel gradients into one
+  flat buffer, all-reduced once per step.
 * 2D Image-GS: horizontal stripes of 16-pixel tile rows, rank g renders
   rows [tiles_y g / world, tiles_y (g+1) / world); Gaussians are replicated
   and their gradients all-reduced.
@@ -21,6 +22,21 @@ import torch
 def view_split(num_views: int, world: int, rank: int) -> List[int]:
     """Views of `rank`: v = rank, rank + world, ..."""
     return [v for v in range(num_views) if v % world == rank]
+
+
+def balance_views(costs: Sequence[float], world: int) -> List[List[int]]:
+    """Views dealt to `world` ranks by cost, longest first, each to the rank
+    with the least cost so far (ties: lower rank; equal costs: lower view
+    index first).  Deterministic, so every rank computes the same split from
+    the same cost vector.  Returns each rank's views in ascending order."""
+    order = sorted(range(len(costs)), key=lambda v: (-float(costs[v]), v))
+    loads = [0.0] * world
+    out: List[List[int]] = [[] for _ in range(world)]
+    for v in order:
+        r = min(range(world), key=lambda i: (loads[i], i))
+        out[r].append(v)
+        loads[r] += float(costs[v])
+    return [sorted(x) for x in out]
 
 
 def stripe_rows(tiles_y: int, world: int, rank: int) -> Optional[Tuple[int, int]]:

@@ -80,6 +80,53 @@ def test_view_split_partitions_views():
         assert max(sizes) - min(sizes) <= 1
 
 
+def test_balance_views_partitions_and_balances():
+    rng = np.random.default_rng(5)
+    for world in (1, 2, 3, 8):
+        costs = (1.0 + rng.random(64) * 3.0).tolist()
+        split = sharding.balance_views(costs, world)
+        assert len(split) == world
+        assert sorted(v for part in split for v in part) == list(range(64))
+        assert all(part == sorted(part) for part in split)
+        assert split == sharding.balance_views(list(costs), world)  # deterministic
+        loads = [sum(costs[v] for v in part) for part in split]
+        # longest-first greedy: the heaviest rank exceeds the mean by at most one view's cost
+        assert max(loads) <= sum(costs) / world + max(costs) + 1e-9
+    # equal costs: a round-robin-like split, sizes within one
+    sizes = [len(p) for p in sharding.balance_views([1.0] * 64, 8)]
+    assert sizes == [8] * 8
+
+
+def _worker_balance(rank, port, out):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        # each rank knows only the costs of its round-robin views; after the
+        # all-reduce of the per-view vector every rank computes the same split
+        truth = [1.0 + (7 * v % 11) for v in range(16)]
+        costs = torch.zeros(16, dtype=torch.float64)
+        for v in sharding.view_split(16, WORLD, rank):
+            costs[v] = truth[v]
+        dist.all_reduce(costs)
+        split = sharding.balance_views(costs.tolist(), WORLD)
+        torch.save(split, out + f".{rank}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_balanced_split_agrees_across_ranks(tmp_path):
+    out = str(tmp_path / "split")
+    mp.start_processes(_worker_balance, args=(_free_port(), out), nprocs=WORLD,
+                       start_method="spawn")
+    s0, s1 = torch.load(out + ".0"), torch.load(out + ".1")
+    assert s0 == s1
+    truth = [1.0 + (7 * v % 11) for v in range(16)]
+    assert s0 == sharding.balance_views(truth, WORLD)
+
+
 def test_multiview_allreduce_equals_single_process(tmp_path):
     out = str(tmp_path / "grads3d.pt")
     mp.start_processes(_worker3d, args=(_free_port(), out), nprocs=WORLD, start_method="spawn")

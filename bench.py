@@ -43,6 +43,14 @@ import torch  # noqa: E402
 
 from sharding import GradBuffer, balance_views, stripe_rows, view_split  # noqa: E402
 
+def l2_loss_grad(*args, **kwargs):
+    """gsplat.loss.l2_loss_grad, imported on first use (the reference arm never
+    loads this build's library)."""
+    from gsplat.loss import l2_loss_grad as fn
+
+    return fn(*args, **kwargs)
+
+
 METRIC = "fwd+bwd Mpix/s"
 UNIT = "Mpix/s"
 L2_FLUSH_BYTES = 256 << 20
@@ -213,10 +221,12 @@ class ImageGSStep:
         img, topk = csrc.nd_rasterize_forward_topk_norm(
             w.tile_bounds, (16, 16, 1), (self.W, self.H, 1), ids, bins, xys, conics, self.c)
         ev[4].record()
-        diff = img[self.r0:self.r1] - self.target[self.r0:self.r1]
-        loss = (diff * diff).sum() / self.numel
-        v_img = torch.zeros_like(img)
-        v_img[self.r0:self.r1] = diff * (2.0 / self.numel)
+        if self.rows is None:
+            loss, v_img = l2_loss_grad(img, self.target)
+        else:
+            v_img = torch.zeros_like(img)
+            loss, _ = l2_loss_grad(img[self.r0:self.r1], self.target[self.r0:self.r1],
+                                   inv_n=1.0 / self.numel, grad=v_img[self.r0:self.r1])
         ev[5].record()
         v_xy, v_conic, v_colors = csrc.nd_rasterize_backward_topk_norm(
             self.H, self.W, 16, 16, ids, bins, xys, conics, self.c, v_img, topk)
@@ -457,9 +467,7 @@ def run_ours_hex2d(args, world, rank, local):
             tb, (16, 16, 1), (W, H, 1), ids, bins, xys, scales, rot, col, w.aa_kernel_size,
             w.softness, e, e)
         ev[2].record()
-        d = img - target
-        loss = (d * d).sum() / numel
-        v_out = d * (2.0 / numel)
+        loss, v_out = l2_loss_grad(img, target)
         ev[3].record()
         grads = csrc.nd_rasterize_backward_topk_norm_hexels(
             H, W, 16, 16, ids, bins, xys, scales, rot, col, v_out, zero_hw, zero_hw, topk,
@@ -726,14 +734,14 @@ class Hexels3DStep:
                             cam.tan_fovy, self.w.softness, 1.0, 1, 1, True, False, False, False,
                             return_surface=self.surface, save=True, save_surface=self.surface,
                             count_contrib=keep_info)
-        diff = o["out_color"] - target
-        loss = (diff * diff).sum() / self.numel
-        g_color = diff * (2.0 / self.numel)
+        # the view's mean-squared colour error is added into the step's loss slot
+        _, g_color = l2_loss_grad(o["out_color"], target, loss=self.grads.loss)
         gd = ga = gn = e
+        loss = None
         if self.surface:
             hw = float(self.H * self.W)
             depth, normals = o["surf_depth"], o["surf_maps"][:3]
-            loss = loss + LAMBDA_DEPTH2 * (depth * depth).sum() / hw + \
+            loss = LAMBDA_DEPTH2 * (depth * depth).sum() / hw + \
                 LAMBDA_NORMAL2 * (normals * normals).sum() / (3 * hw)
             gd = depth * (2 * LAMBDA_DEPTH2 / hw)
             ga = self.zero_hw
@@ -769,7 +777,8 @@ class Hexels3DStep:
             for cam, tgt in zip(self.cams, self.targets):
                 # the backward adds this view's gradients into self.acc
                 loss, _ = self._view(cam, tgt, keep_info)
-                self.grads.loss.add_(loss)
+                if loss is not None:  # surface terms of the loss
+                    self.grads.loss.add_(loss)
                 self._mark("accumulate")
             self.grads.all_reduce_(self.world)
             total = self.grads.loss

@@ -386,6 +386,14 @@ HX_API int hx_hexels3d_geometry_backward(
     float* grad_means3d, float* grad_means2d, int means2d_stride, float* grad_scales,
     float* grad_rotations, int accumulate, cudaStream_t stream);
 
+/* Mean-squared-error loss of a fit step in one pass (no reference
+ * counterpart; the reference's training loops form it with torch ops):
+ * grad[i] = (pred[i] - target[i]) * 2 inv_n, and sum_i (pred[i] - target[i])^2
+ * inv_n is ADDED to *loss (clear it first; the order of the float additions
+ * across CTAs is not fixed).  n >= 0; 16-byte aligned inputs take a vector path. */
+HX_API int hx_l2_loss_grad(const float* pred, const float* target, int64_t n, float inv_n,
+                           float* grad, float* loss, cudaStream_t stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

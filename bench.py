@@ -51,6 +51,13 @@ def l2_loss_grad(*args, **kwargs):
     return fn(*args, **kwargs)
 
 
+def mse_loss(pred, target):
+    """gsplat.loss.mse_loss (differentiable), imported on first use."""
+    from gsplat.loss import mse_loss as fn
+
+    return fn(pred, target)
+
+
 METRIC = "fwd+bwd Mpix/s"
 UNIT = "Mpix/s"
 L2_FLUSH_BYTES = 256 << 20
@@ -1014,9 +1021,8 @@ def run_e2e_3d(w, args, world, rank, surface, views=None):
             out = gsplat.rasterize_hexels3d(
                 *params[:7], cam.viewmatrix, cam.projmatrix, cam.campos, bg, cam.width,
                 cam.height, cam.tan_fovx, cam.tan_fovy, w.softness, return_surface=surface)
-            d = out[0] - tgt
-            free[b].record(main)  # the target is read only by the subtraction
-            loss = (d * d).mean()
+            loss = mse_loss(out[0], tgt)
+            free[b].record(main)  # the target is read only by the loss kernel
             if surface:
                 depth, normals = out[2], out[4]
                 loss = loss + LAMBDA_DEPTH2 * (depth * depth).mean() + \

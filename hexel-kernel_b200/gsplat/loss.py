@@ -42,3 +42,23 @@ def l2_loss_grad(pred: torch.Tensor, target: torch.Tensor, *, inv_n: Optional[fl
         lib.call("hx_l2_loss_grad", ptr(pred), ptr(target), n, scale, ptr(grad), ptr(loss),
                  stream(dev))
     return loss, grad
+
+
+class _MSELoss(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, pred, target):
+        loss, grad = l2_loss_grad(pred.contiguous(), target.contiguous())
+        ctx.save_for_backward(grad)
+        return loss.view(())
+
+    @staticmethod
+    def backward(ctx, g):
+        (grad,) = ctx.saved_tensors
+        return grad * g, None
+
+
+def mse_loss(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+    """Differentiable mean((pred - target)^2) (gradient with respect to pred
+    only) computed by l2_loss_grad: one kernel forms the loss and the
+    gradient the backward returns."""
+    return _MSELoss.apply(pred, target)

@@ -58,3 +58,18 @@ def test_l2_loss_grad_empty_and_errors():
     with pytest.raises(RuntimeError):
         l2_loss_grad(torch.zeros(4, device="cuda", dtype=torch.float64),
                      torch.zeros(4, device="cuda", dtype=torch.float64))
+
+
+def test_mse_loss_autograd():
+    from gsplat.loss import mse_loss
+
+    g = torch.Generator().manual_seed(11)
+    p = torch.rand((3, 40, 56), generator=g).cuda().requires_grad_()
+    t = torch.rand((3, 40, 56), generator=g).cuda()
+    loss = mse_loss(p * 1.5, t)
+    loss.backward()
+    q = p.detach().clone().requires_grad_()
+    want = ((q * 1.5 - t) ** 2).mean()
+    want.backward()
+    assert loss.shape == () and abs(float(loss) - float(want)) <= 1e-5 * float(want)
+    torch.testing.assert_close(p.grad, q.grad, rtol=1e-5, atol=1e-9)

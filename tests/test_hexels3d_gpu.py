@@ -482,3 +482,35 @@ def test_preprocess_matches_oracle():
     _, plist = _lists(saved)
     keys, ids, ranges = o.bin_surfels(pre)
     assert abs(len(ids) - len(plist)) <= max(4, len(plist) // 200)
+
+
+@pytest.mark.parametrize("streams", [2, 3])
+def test_pipelined_views_equal_sequential(streams):
+    """multiview.fit_step_views with the views spread over several streams
+    gives the gradients and loss of the same views run in order (to the
+    order of the float atomics)."""
+    import multiview
+    import workloads
+
+    w = workloads.hexels3d_tiny(11, 2000, 96, 80, 5, 0.06).to("cuda")
+    params = [w.means3d, w.scales, w.rotations, w.colors, w.color_grads, w.view_grads,
+              w.opacities]
+    g = torch.Generator().manual_seed(5)
+    cams = w.cameras
+    targets = [torch.rand((3, c.height, c.width), generator=g).cuda() for c in cams]
+
+    def step(pipe):
+        grads = [torch.zeros_like(p) for p in params]
+        loss = torch.zeros(1, device="cuda")
+        multiview.fit_step_views(params, cams, targets, w.background, w.softness, grads, loss,
+                                 pipe)
+        torch.cuda.synchronize()
+        return grads, loss
+
+    want_g, want_l = step(None)
+    pipe = multiview.ViewPipeline(params, streams=streams)
+    for _ in range(2):  # the private accumulators are cleared between steps
+        got_g, got_l = step(pipe)
+        assert abs(float(got_l) - float(want_l)) <= 1e-5 * abs(float(want_l))
+        for name, a, b in zip(multiview.PARAM_NAMES, got_g, want_g):
+            assert_grad_parity(a, b, None, name)

@@ -59,6 +59,12 @@ def mse_loss(pred, target):
     return fn(pred, target)
 
 
+# DRAM bytes per launch of the roofline kernels, from the committed ncu
+# captures of these configurations (read + write)
+TRAFFIC_R3D_BWD_1080 = int((401.384192 + 67.767296) * 1e6)   # render3d_bwd, one 1080p view
+TRAFFIC_TOPK_FWD_2048 = int((45.213952 + 163.590144) * 1e6)  # topk_fwd, 2048^2 / 100k
+TRAFFIC_HEX_FWD_1024 = int((2.483712 + 7.526656) * 1e6)      # hexel_fwd, 1024^2 / 50k
+
 METRIC = "fwd+bwd Mpix/s"
 UNIT = "Mpix/s"
 L2_FLUSH_BYTES = 256 << 20
@@ -324,7 +330,10 @@ def run_ours(args, world, rank, local):
         "peak": round(fp32_peak_tflops, 2),
         "unit": "TFLOP/s",
         "frac": round(fwd_flops / (fwd_ms / 1e3) / 1e12 / fp32_peak_tflops, 4),
-        "traffic": None,
+        "traffic": TRAFFIC_TOPK_FWD_2048 if args.config == "imagegs_large" else None,
+        "traffic_source": ("dram__bytes_read.sum + dram__bytes_write.sum per launch, one ncu "
+                           "capture of this configuration (profiles/imagegs_topk_2048_n100k.md)"
+                           if args.config == "imagegs_large" else None),
         "peak_source": "nominal FP32 FMA rate, 148 SMs x 128 lanes x 2 x max SM clock "
                        "(no measured FP32 peak in MEASURED_PEAKS.json)",
         "work": f"{pairs} (pixel, candidate) pairs x 14 FLOP",
@@ -536,7 +545,10 @@ def run_ours_hex2d(args, world, rank, local):
         "stages_ms": stages,
         "roofline": {"kernel": "hexel_fwd_kernel / hexel_bwd_kernel", "bound": "fp32",
                      "achieved": round(fwd, 3), "peak": round(fp32_peak, 2), "unit": "TFLOP/s",
-                     "frac": round(fwd / fp32_peak, 4), "traffic": None,
+                     "frac": round(fwd / fp32_peak, 4), "traffic": TRAFFIC_HEX_FWD_1024,
+                     "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum per "
+                                       "launch, one ncu capture of this configuration "
+                                       "(profiles/hexels2d_1024_n50k.md)",
                      "work": f"forward {pairs} (pixel, candidate) pairs x {HEX2D_FWD_FLOP:.0f} "
                              f"FLOP; backward {stored} stored ids x {HEX2D_BWD_FLOP:.0f} FLOP",
                      "backward": {"achieved": round(bwd, 3), "frac": round(bwd / fp32_peak, 4)}},
@@ -909,7 +921,10 @@ def roofline_3d(step, stage_ms):
         "peak": round(fp32_peak, 2),
         "unit": "TFLOP/s",
         "frac": round(bwd / fp32_peak, 4),
-        "traffic": None,
+        "traffic": TRAFFIC_R3D_BWD_1080 if nv and step.H == 1080 and not step.surface else None,
+        "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum per launch (one view), "
+                          "one ncu capture of this configuration "
+                          "(profiles/render3d_bwd_64views.md)",
         "peak_source": "nominal FP32 FMA rate, 148 SMs x 128 lanes x 2 x max SM clock "
                        "(MEASURED_PEAKS.json has no FP32 figure)",
         "work": f"{blended} blended (pixel, surfel) pairs over {nv} views x "

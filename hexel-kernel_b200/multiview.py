@@ -20,7 +20,7 @@ outputs only.
 
 from __future__ import annotations
 
-from typing import List, Optional, Sequence
+from typing import Optional, Sequence
 
 import torch
 
@@ -44,15 +44,17 @@ def fit_step_views(params: Sequence[torch.Tensor], cams: Sequence, targets: Sequ
                    background: torch.Tensor, softness: float, grads: Sequence[torch.Tensor],
                    loss: torch.Tensor, pipeline: Optional[ViewPipeline] = None, *,
                    color_model: int = 1, view_model: int = 1,
-                   use_view_grads: bool = True) -> List[dict]:
+                   use_view_grads: bool = True) -> None:
     """Forward, loss and backward of every view in `cams` (objects with
     viewmatrix, projmatrix, campos, width, height, tan_fovx, tan_fovy), the
     gradients of `params` (means3d, scales, rotations, colors, color_grads,
     view_grads, opacities) ADDED into `grads` (same order and shapes) and the
     summed per-view colour losses ADDED into `loss` (one element).  With a
     `pipeline` of several streams the views run overlapped; without one they
-    run in order on the current stream.  Returns each view's forward record
-    (kept alive until the step's work is done)."""
+    run in order on the current stream.  Each view's intermediate tensors are
+    made and used on one stream only, so the caching allocator reuses them in
+    that stream's order; the accumulators are the caller's and the current
+    stream waits for every view before this returns."""
     from gsplat.cuda_hexels3d import _C
     from gsplat.loss import l2_loss_grad
 
@@ -70,7 +72,6 @@ def fit_step_views(params: Sequence[torch.Tensor], cams: Sequence, targets: Sequ
                 t.zero_()
         for s in streams:
             s.wait_stream(main)
-    records = []
     for i, (cam, tgt) in enumerate(zip(cams, targets)):
         k = i % len(streams)
         acc = dict(zip(PARAM_NAMES, grads))
@@ -87,26 +88,10 @@ def fit_step_views(params: Sequence[torch.Tensor], cams: Sequence, targets: Sequ
                               cam.width, cam.height, cam.tan_fovx, cam.tan_fovy, softness, 1.0,
                               color_model, view_model, use_view_grads, -1, False, False, False,
                               o["saved"], accumulate_into=acc, blend_mask=o["blend_mask"])
-        records.append(o)
+            del o, g_color
     if pipeline is not None:
         for s in streams:
             main.wait_stream(s)
         for acc in pipeline.geo:
             for dst, src in zip(grads[:3], acc):
                 dst.add_(src)
-        # the per-view tensors were made on the side streams and are freed by
-        # the caller on the current one: tie their reuse to this stream
-        for o in records:
-            for t in _tensors(o):
-                t.record_stream(main)
-    return records
-
-
-def _tensors(o: dict):
-    for v in o.values():
-        if isinstance(v, torch.Tensor):
-            yield v
-        elif isinstance(v, (list, tuple)):
-            for t in v:
-                if isinstance(t, torch.Tensor):
-                    yield t

@@ -738,11 +738,7 @@ class Hexels3DStep:
         self.grads = GradBuffer([p.shape for p in self.params], dev)
         self.acc = self.grads.views
         # the RGB step's views are pipelined over two streams (multiview.py)
-        # on one GPU; with several ranks the views run in order on one stream
-        # (the pipelined step measured 48 ms instead of 21 ms per step with 8
-        # ranks on one node, against 99 % of the one-GPU rate with 2)
-        self.pipeline = (ViewPipeline(self.params, streams=2)
-                         if not surface and world == 1 else None)
+        self.pipeline = None if surface else ViewPipeline(self.params, streams=2)
         self.marks: list = []
         self.stage_ms = {k: 0.0 for k in self.STAGES}
         self.info: dict = {}
@@ -987,8 +983,7 @@ def run_ours_3d(args, world, rank, local):
         "stages_note": ("one step with CUDA events between stages, views in order on one "
                         "stream; the timed steps pipeline the views over two streams"
                         if step.pipeline is not None else
-                        "one step with CUDA events between stages, views in order on one "
-                        "stream, as in the timed steps"),
+                        "CUDA events between stages of the timed steps"),
         "roofline": roofline_3d(step, stage_ms),
         "e2e": e2e,
         "gpu_launches": int(launches),

@@ -77,3 +77,22 @@ def test_cpu_tensors_rejected_like_reference():
                                             torch.zeros(4, dtype=torch.int32),
                                             torch.zeros(1, 2, dtype=torch.int32), x,
                                             torch.zeros(4, 3), torch.zeros(4, 3))
+
+
+def test_loss_and_multiview_check_arguments_before_any_launch():
+    """The fused loss and the multi-view step reject bad arguments on the
+    host, before anything reaches a GPU."""
+    import torch
+
+    import multiview
+    from gsplat.loss import l2_loss_grad
+
+    with pytest.raises(RuntimeError, match="pred must be a CUDA tensor"):
+        l2_loss_grad(torch.zeros(8), torch.zeros(8))
+    with pytest.raises(ValueError, match="streams must be >= 1"):
+        multiview.ViewPipeline([torch.zeros(3)], streams=0)
+    p = [torch.zeros(2)] * 7
+    with pytest.raises(ValueError, match="params and grads"):
+        multiview.fit_step_views(p[:6], [], [], torch.zeros(3), 10.0, p, torch.zeros(1))
+    with pytest.raises(ValueError, match="one target per camera"):
+        multiview.fit_step_views(p, [object()], [], torch.zeros(3), 10.0, p, torch.zeros(1))

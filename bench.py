@@ -1296,7 +1296,8 @@ def run_reference(args, world, rank):
         sample = lambda: cpu_sample_run(w, crop)  # noqa: E731
         config = {"workload": w.name, "height": w.height, "width": w.width,
                   "num_gaussians": w.num_points, "top_k": 10, "tile": 16}
-    for _ in range(min(args.warmup, 1)):
+    warm = min(args.warmup, 3)  # a CPU sample takes seconds: at most 3 untimed
+    for _ in range(warm):
         sample()
     secs_total, mpix_total = 0.0, 0.0
     steps = max(1, min(args.steps, args.ref_max_steps))
@@ -1307,7 +1308,7 @@ def run_reference(args, world, rank):
     value = mpix_total / secs_total
     return {
         "metric": METRIC, "value": round(value, 5), "unit": UNIT, "impl": "reference",
-        "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 1),
+        "n_gpus": world, "steps": steps, "warmup": warm,
         "ms_per_step": round(secs_total / steps * 1e3, 2),
         "higher_is_better": True, "scaling": "strong" if three_d else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",

@@ -40,8 +40,10 @@ __device__ __forceinline__ float sign_subgrad(float x) {
 // index of the active edge (ties prefer edge 2 over 1, and 1/2 over 0).
 __device__ __forceinline__ float hex_sdf(float u, float v, int& edge) {
     const float d0 = fabsf(v);
-    const float t1 = kHexA * u + kHexB * v;
-    const float t2 = kHexA * u - kHexB * v;
+    // hexels_forward.cu:31-32: a u fused, b v = v / 2 exact (the rounding the
+    // reference's build gives these lines)
+    const float t1 = __fmaf_rn(kHexA, u, kHexB * v);
+    const float t2 = __fmaf_rn(kHexA, u, -(kHexB * v));
     const float d1 = fabsf(t1);
     const float d2 = fabsf(t2);
     float m = d1;
@@ -143,8 +145,12 @@ __device__ __forceinline__ HexLocal hex_local(const HexPrim& p, float dx, float 
         l.u_base = dx * p.g0 + dy * p.g2;
         l.v_base = dx * p.g1 + dy * p.g3;
     } else {
-        l.u_rot = dx * p.g0 + dy * p.g1;
-        l.v_rot = -dx * p.g1 + dy * p.g0;
+        // The reference's expressions (hexels_forward.cu:62-63) with the
+        // fused multiply-adds its fast-math build forms, written out so that
+        // this build rounds the same way: weights tie-break the top-10 by
+        // exact comparison, so one ulp here can reorder a pixel's slots.
+        l.u_rot = __fmaf_rn(dy, p.g1, __fmul_rn(dx, p.g0));
+        l.v_rot = __fmaf_rn(dy, p.g0, -__fmul_rn(dx, p.g1));
         l.u_base = l.u_rot / p.g2;
         l.v_base = l.v_rot / p.g3;
     }

@@ -19,6 +19,8 @@
 //     surfel at flush time from the accumulated colour gradient;
 //   * with surface outputs the forward's saved per-pixel state replaces the
 //     reference's forward re-walk.
+#include <atomic>
+
 #include "hx_cmat.cuh"
 #include "hx_hexmath3d.cuh"
 
@@ -42,6 +44,9 @@ constexpr int kFixCg = 3, kFixOp = 9, kFixSoft = 10, kFixTm = 13, kFixN = 22, kF
 // gradients): colour 0-2, colour gradients 3-8, opacity 9, transform 10-18;
 // padded to 24 slots.
 constexpr int kLiteCg = 3, kLiteOp = 9, kLiteTm = 10, kLiteComp = 19;
+// Packed plain-RGB path: list entries with at most this many blended pairs
+// in a warp skip the warp reduction (their lanes add into shared memory).
+constexpr int kPackDirect = 2;
 
 // Sum of a 24-slot vector over the warp: three reduce-scatter halvings
 // (over lane bits 4, 3, 2) leave each lane 3 slots summed over 8 lanes, then
@@ -416,11 +421,110 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
     return true;
 }
 
+// ---------------------------------------------------------------------------
+// Packed plain-RGB pairs.  On the training path (flat or linear colour, no
+// or linear view model, no surface, prefilter, overdraw or softness
+// gradients) a list entry's work splits into a cheap per-pixel part that
+// must run in list order (hit test, alpha, and the reverse recursion of the
+// transmittance and the colour behind) and the VJP proper, which depends
+// only on a few numbers of the pair.  The warp runs the first part for all
+// its pixels, writes each blended pair's numbers into consecutive slots of a
+// warp-private shared buffer, and runs the VJP with one pair per lane, so
+// that ~17 blended pairs of the 64 pixels take one pass of the VJP instead
+// of one per 8x4 half at a quarter of the lanes.
+// ---------------------------------------------------------------------------
+struct PairRec {
+    float4 a;  // w * v_out (3), v_alpha (the alpha VJP of the colour term)
+    float4 b;  // u, v, boundary weight (negative: alpha clamped), source lane | half << 5
+};
+
+// First part for one pixel: returns whether the pair blends and fills rec.
+__device__ __forceinline__ bool rgb_pair_forward(const Backward3DArgs& a, const Surfel3D& s,
+                                                 const int idx, BwdPixel& q, PairRec& rec) {
+    if (idx >= q.n_color) return false;
+    const float3 Tu = {s.tu[0], s.tu[1], s.tu[2]};
+    const float3 Tv = {s.tv[0], s.tv[1], s.tv[2]};
+    const float3 Tw = {s.tw[0], s.tw[1], s.tw[2]};
+    const float3 soft3 = {s.s0, s.s1, s.s2};
+    HexHit h;
+    if (!hexel_hit(q.px, q.py, Tu, Tv, Tw, s.opacity, soft3, a.softness_stride == 1, h))
+        return false;
+    const float alpha = h.alpha;
+    if (alpha < 1.0f / 255.0f) return false;
+    const float u = h.u, v = h.v;
+    const float T_before = q.T_after * (1.f / (1.f - alpha));
+    const float w = alpha * T_before;
+    const float cx = s.cb[0] + u * s.gu[0] + v * s.gv[0] + s.cv[0];
+    const float cy = s.cb[1] + u * s.gu[1] + v * s.gv[1] + s.cv[1];
+    const float cz = s.cb[2] + u * s.gu[2] + v * s.gv[2] + s.cv[2];
+    const float v_alpha = T_before * (q.v_r * (cx - q.behind.x) + q.v_g * (cy - q.behind.y) +
+                                      q.v_b * (cz - q.behind.z));
+    rec.a = make_float4(w * q.v_r, w * q.v_g, w * q.v_b, v_alpha);
+    rec.b = make_float4(u, v, h.clamped ? -1.f : h.boundary, 0.f);
+    q.behind = {alpha * cx + (1.f - alpha) * q.behind.x, alpha * cy + (1.f - alpha) * q.behind.y,
+                alpha * cz + (1.f - alpha) * q.behind.z};
+    q.T_after = T_before;
+    return true;
+}
+
+// The VJP of one packed pair at pixel (px, py), added into the 24-slot
+// plain-RGB vector (colour 0-2, colour gradients 3-8, opacity 9, transform
+// 10-18).  Same terms as bwd_pair's for this configuration.
+__device__ __forceinline__ void rgb_pair_vjp(const Surfel3D& s, const PairRec& rec,
+                                             const float px, const float py, float (&acc)[24]) {
+    const float wr = rec.a.x, wg = rec.a.y, wb = rec.a.z, v_alpha = rec.a.w;
+    const float u = rec.b.x, v = rec.b.y, bnd = rec.b.z;
+    acc[0] += wr;
+    acc[1] += wg;
+    acc[2] += wb;
+    acc[kLiteCg + 0] += wr * u;
+    acc[kLiteCg + 1] += wg * u;
+    acc[kLiteCg + 2] += wb * u;
+    acc[kLiteCg + 3] += wr * v;
+    acc[kLiteCg + 4] += wg * v;
+    acc[kLiteCg + 5] += wb * v;
+    float v_u = wr * s.gu[0] + wg * s.gu[1] + wb * s.gu[2];
+    float v_v = wr * s.gv[0] + wg * s.gv[1] + wb * s.gv[2];
+    if (bnd >= 0.f) {  // alpha not clamped: opacity and SDF terms
+        acc[kLiteOp] += v_alpha * bnd;
+        float dist_g, ddu, ddv;
+        int edge_g;
+        hex_sdf3_grad(u, v, dist_g, ddu, ddv, edge_g);
+        const float soft_g = (edge_g == 0) ? s.s0 : ((edge_g == 1) ? s.s1 : s.s2);
+        const float v_ad = v_alpha * s.opacity * (-soft_g * bnd * (1.f - bnd));
+        v_u += v_ad * ddu;
+        v_v += v_ad * ddv;
+    }
+    const float3 Tu = {s.tu[0], s.tu[1], s.tu[2]};
+    const float3 Tv = {s.tv[0], s.tv[1], s.tv[2]};
+    const float3 Tw = {s.tw[0], s.tw[1], s.tw[2]};
+    const float3 k = {px * Tw.x - Tu.x, px * Tw.y - Tu.y, px * Tw.z - Tu.z};
+    const float3 l = {py * Tw.x - Tv.x, py * Tw.y - Tv.y, py * Tw.z - Tv.z};
+    const float3 p = cross3(k, l);
+    if (p.z != 0.f) {
+        const float inv_pz = 1.f / p.z;
+        const float dsx = v_u * inv_pz;
+        const float dsy = v_v * inv_pz;
+        const float3 v_p = {dsx, dsy, -(dsx * u + dsy * v)};
+        const float3 v_k = cross3(l, v_p);
+        const float3 v_l = cross3(v_p, k);
+        acc[kLiteTm + 0] += -v_k.x;
+        acc[kLiteTm + 1] += -v_k.y;
+        acc[kLiteTm + 2] += -v_k.z;
+        acc[kLiteTm + 3] += -v_l.x;
+        acc[kLiteTm + 4] += -v_l.y;
+        acc[kLiteTm + 5] += -v_l.z;
+        acc[kLiteTm + 6] += px * v_k.x + py * v_l.x;
+        acc[kLiteTm + 7] += px * v_k.y + py * v_l.y;
+        acc[kLiteTm + 8] += px * v_k.z + py * v_l.z;
+    }
+}
+
 // One CTA per 16x16 tile, 256 / PPT threads, PPT pixels per thread: warps
 // cover 8 x (4 PPT) pixel blocks (two across, 4 / PPT down), lane l owns
 // pixels (l % 8, l / 8 + 4 k), k < PPT.  Per list index the PPT pairs of a
 // thread are added into one gradient vector before the warp reduction.
-template <bool SURF, bool PREFILTER, int N, int PPT>
+template <bool SURF, bool PREFILTER, int N, int PPT, bool PACK>
 __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_bwd_kernel(const Backward3DArgs a,
                                                                         const BwdLayout L) {
     constexpr int kThreads = k3BlockSize / PPT;
@@ -436,6 +540,9 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
     __shared__ unsigned char s_list[kThreads / 32][kBatch];
     // the forward's blend-mask bytes of the batch's list entries
     __shared__ unsigned char s_bm[kBatch];
+    // per warp: the packed pairs of the list entry in hand (PACK)
+    __shared__ PairRec s_pairs[PACK ? kThreads / 32 : 1][PACK ? 32 * PPT : 1];
+    static_assert(!PACK || (N == 24 && !SURF && !PREFILTER), "packed pairs: plain RGB only");
 
     // N == 32 uses the fixed slot layout (compile-time indices keep the
     // gradient vector in registers); N == 64 takes the host-computed layout
@@ -564,6 +671,76 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
         for (int jj = n_mine - 1; jj >= 0; --jj) {
             const int idx = bstart + s_list[warp][jj];
             const Surfel3D& s = s_prim[idx - bstart];
+            if constexpr (PACK) {
+                // per-pixel part in list order, then the blended pairs packed
+                // one per lane for the VJP
+                const unsigned bm = s_bm[idx - bstart];
+                PairRec rec[PPT];
+                unsigned m[PPT];
+                int n_pairs = 0;
+#pragma unroll
+                for (int k = 0; k < PPT; ++k) {
+                    bool bl = false;
+                    if (bm & (1u << (2 * ((warp >> 1) * PPT + k) + (warp & 1))))
+                        bl = rgb_pair_forward(a, s, idx, q[k], rec[k]);
+                    m[k] = __ballot_sync(0xffffffffu, bl);
+                    rec[k].b.w = __int_as_float(lane | (k << 5));
+                    n_pairs += __popc(m[k]);
+                }
+                if (n_pairs == 0) continue;
+                float acc[24];
+#pragma unroll
+                for (int c = 0; c < 24; ++c) acc[c] = 0.f;
+                int halves = 0;
+                unsigned holders = 0u;  // lanes holding at least one pair
+#pragma unroll
+                for (int k = 0; k < PPT; ++k) {
+                    halves += m[k] != 0u;
+                    holders |= m[k];
+                }
+                if (halves > 1 && n_pairs <= 32) {
+                    holders = n_pairs == 32 ? 0xffffffffu : ((1u << n_pairs) - 1u);
+                    // pairs of both halves: packed one per lane (one pass)
+                    __syncwarp();  // the previous entry's pairs have been read
+                    int base = 0;
+#pragma unroll
+                    for (int k = 0; k < PPT; ++k) {
+                        if (m[k] & (1u << lane))
+                            s_pairs[warp][base + __popc(m[k] & ((1u << lane) - 1u))] = rec[k];
+                        base += __popc(m[k]);
+                    }
+                    __syncwarp();
+                    if (lane < n_pairs) {
+                        const PairRec r = s_pairs[warp][lane];
+                        const int code = __float_as_int(r.b.w);
+                        const float px = (float)(wx0 + (code & 7));
+                        const float py = (float)(wy0 + ((code & 31) >> 3) + 4 * (code >> 5));
+                        rgb_pair_vjp(s, r, px, py, acc);
+                    }
+                } else {
+                    // one half holds every pair, or more than a warp of
+                    // pairs: each lane takes its own, in place
+#pragma unroll
+                    for (int k = 0; k < PPT; ++k)
+                        if (m[k] != 0u && (m[k] & (1u << lane)))
+                            rgb_pair_vjp(s, rec[k], q[k].px, q[k].py, acc);
+                }
+                float* dst = s_acc + (idx - bstart) * kLiteComp;
+                if (n_pairs <= kPackDirect) {
+                    // a few pairs: the lanes holding them add straight into the
+                    // batch accumulator (at most kPackDirect-way address conflicts)
+                    if (holders & (1u << lane)) {
+#pragma unroll
+                        for (int c = 0; c < kLiteComp; ++c) atomicAdd(dst + c, acc[c]);
+                    }
+                } else {
+                    const int start = warp_reduce_scatter24(acc, lane);
+                    const int c = lane & 3;
+                    const float val = c == 0 ? acc[0] : (c == 1 ? acc[1] : acc[2]);
+                    const int comp = start + c;
+                    if (c < 3 && comp < kLiteComp && val != 0.f) atomicAdd(dst + comp, val);
+                }
+            } else {
             float acc[N];
 #pragma unroll
             for (int c = 0; c < N; ++c) acc[c] = 0.f;
@@ -591,6 +768,7 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
                         if (comp < L.ncomp && acc[c] != 0.f) atomicAdd(dst + comp, acc[c]);
                     }
                 }
+            }
             }
         }
         __syncthreads();
@@ -822,36 +1000,44 @@ using namespace hx;
 
 namespace {
 
-template <bool SURF, bool PREFILTER, int N, int PPT>
+template <bool SURF, bool PREFILTER, int N, int PPT, bool PACK>
 int launch_bwd3d(const Backward3DArgs& a, const BwdLayout& L, cudaStream_t stream) {
     constexpr int kBatch = k3BlockSize / PPT;
     const size_t smem = sizeof(Surfel3D) * kBatch + sizeof(float) * kBatch * L.ncomp;
-    static bool attr_set[64] = {};
+    // the dynamic shared-memory limit is raised once per device (host threads
+    // may launch concurrently: the flags are atomic)
+    static std::atomic<bool> attr_set[64];
     int dev = 0;
     HX_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        HX_CUDA_TRY(cudaFuncSetAttribute(render3d_bwd_kernel<SURF, PREFILTER, N, PPT>,
+    if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
+        HX_CUDA_TRY(cudaFuncSetAttribute(render3d_bwd_kernel<SURF, PREFILTER, N, PPT, PACK>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)(sizeof(Surfel3D) * kBatch +
                                                sizeof(float) * kBatch * N)));
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+        if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
     }
     dim3 grid(ceil_div(a.W, k3BlockX), ceil_div(a.H, k3BlockY));
-    render3d_bwd_kernel<SURF, PREFILTER, N, PPT><<<grid, k3BlockSize / PPT, smem, stream>>>(a, L);
+    render3d_bwd_kernel<SURF, PREFILTER, N, PPT, PACK>
+        <<<grid, k3BlockSize / PPT, smem, stream>>>(a, L);
     HX_LAUNCH_CHECK("render3d_bwd_kernel");
     return HX_OK;
 }
 
 // Two pixels per thread on the RGB path; one with surface gradients, whose
 // larger per-pixel state costs more in occupancy (167 registers at two
-// pixels) than the shared per-surfel work saves.
+// pixels) than the shared per-surfel work saves.  The plain-RGB layout
+// without overdraw gradients (the training path) takes the packed pairs.
 template <bool SURF, bool PREFILTER>
 int launch_bwd3d_n(const Backward3DArgs& a, const BwdLayout& L, int slots,
                    cudaStream_t stream) {
     constexpr int kPPT = SURF ? 1 : 2;
-    if (slots == 24 && !SURF && !PREFILTER) return launch_bwd3d<SURF, PREFILTER, 24, kPPT>(a, L, stream);
-    if (slots <= 32) return launch_bwd3d<SURF, PREFILTER, 32, kPPT>(a, L, stream);
-    return launch_bwd3d<SURF, PREFILTER, 64, kPPT>(a, L, stream);
+    if constexpr (!SURF && !PREFILTER) {
+        if (slots == 24 && a.grad_out_overdraw == nullptr)
+            return launch_bwd3d<false, false, 24, kPPT, true>(a, L, stream);
+        if (slots == 24) return launch_bwd3d<false, false, 24, kPPT, false>(a, L, stream);
+    }
+    if (slots <= 32) return launch_bwd3d<SURF, PREFILTER, 32, kPPT, false>(a, L, stream);
+    return launch_bwd3d<SURF, PREFILTER, 64, kPPT, false>(a, L, stream);
 }
 
 }  // namespace
@@ -1024,6 +1210,11 @@ extern "C" int hx_hexels3d_geometry_backward(
                    grad_transMats && grad_view_dirs && grad_means3d && grad_scales &&
                    grad_rotations,
                "hexels3d_geometry_backward: null pointer");
+    // rotations are read and written as float4, scales as float2
+    HX_REQUIRE(((uintptr_t)rotations | (uintptr_t)grad_rotations) % 16 == 0 &&
+                   ((uintptr_t)scales | (uintptr_t)grad_scales) % 8 == 0,
+               "hexels3d_geometry_backward: rotations (and their gradients) must start on a "
+               "16-byte boundary, scales (and theirs) on an 8-byte boundary");
     const int blocks = ceil_div(P, 256);
     if (grad_means2d) {
         HX_REQUIRE(transMats && (means2d_stride == 3 || means2d_stride == 4),

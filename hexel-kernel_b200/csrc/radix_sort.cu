@@ -11,6 +11,7 @@
 // and processes them 32 at a time in index order, so equal digits keep their input order;
 // tiles are ordered by the scan.  This replaces the stable CUB / PyTorch radix
 // sorts the reference calls (gsplat/utils.py:159, hexels3d_forward.cu:3013).
+#include <atomic>
 #include "hx_common.cuh"
 #include "hx_sort.cuh"
 
@@ -238,13 +239,15 @@ int sort_passes(const K* keys_in, const int* vals_in, K* keys_out, int* vals_out
     const int tiles = ceil_div(n, kTile);
     const size_t smem = sizeof(K) * kTile + sizeof(int) * kTile +
                         sizeof(int) * (kSortWarps * kRadix + 2 * kRadix);
-    static bool attr_set[64] = {};
+    // the dynamic shared-memory limit is raised once per device (host threads
+    // may sort concurrently: the flags are atomic)
+    static std::atomic<bool> attr_set[64];
     int dev = 0;
     HX_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
         HX_CUDA_TRY(cudaFuncSetAttribute(sort_downsweep_kernel<K, ITEMS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+        if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
     }
     const int bits = end_bit - begin_bit;
     const int passes = (bits + 7) / 8;

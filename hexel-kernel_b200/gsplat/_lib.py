@@ -115,6 +115,15 @@ def zero_views(device: torch.device, shapes) -> list:
     return out
 
 
+def check_same_device(ref: torch.Tensor, ref_name: str, **others) -> None:
+    """Raises RuntimeError unless every tensor in `others` (name=tensor, None
+    allowed) lives on `ref`'s device: the kernels take raw pointers and run
+    on `ref`'s device, where another GPU's address would be invalid."""
+    for name, t in others.items():
+        if t is not None and t.device != ref.device:
+            raise RuntimeError(f"{name} is on {t.device} but {ref_name} is on {ref.device}")
+
+
 def check_input(t: torch.Tensor, name: str) -> None:
     """Mirrors the reference's CHECK_INPUT (gsplat/cuda/csrc/bindings.h:10-15)."""
     if not isinstance(t, torch.Tensor) or not t.is_cuda:

@@ -320,6 +320,12 @@ def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, col
         check_input(t, k)
         _check(t.dtype == torch.float32 and tuple(t.shape) == shapes[k],
                f"accumulation buffer {k} must be float32 of shape {shapes[k]}")
+        _check(t.device == dev, f"accumulation buffer {k} must be on {dev}")
+        # the geometry backward reads and writes rotations as float4 and
+        # scales as float2
+        align = {"rotations": 16, "scales": 8}.get(k, 4)
+        _check(t.data_ptr() % align == 0,
+               f"accumulation buffer {k} must start on a {align}-byte boundary")
     fresh = [k for k in shapes if k not in acc]
     g = dict(zip(fresh, _zero_views(dev, [shapes[k] for k in fresh])))
     g.update(acc)

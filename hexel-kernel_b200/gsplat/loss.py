@@ -7,7 +7,7 @@ from typing import Optional, Tuple
 
 import torch
 
-from ._lib import check_input, lib, ptr, stream
+from ._lib import check_input, check_same_device, lib, ptr, stream
 
 
 def l2_loss_grad(pred: torch.Tensor, target: torch.Tensor, *, inv_n: Optional[float] = None,
@@ -36,6 +36,7 @@ def l2_loss_grad(pred: torch.Tensor, target: torch.Tensor, *, inv_n: Optional[fl
         loss = torch.zeros((1,), dtype=torch.float32, device=dev)
     elif not (loss.is_cuda and loss.dtype == torch.float32 and loss.numel() == 1):
         raise RuntimeError("loss must be a one-element float32 CUDA tensor")
+    check_same_device(pred, "pred", target=target, grad=grad, loss=loss)
     n = pred.numel()
     scale = (1.0 / n if n else 0.0) if inv_n is None else float(inv_n)
     with torch.cuda.device(dev):

@@ -96,3 +96,35 @@ def test_loss_and_multiview_check_arguments_before_any_launch():
         multiview.fit_step_views(p[:6], [], [], torch.zeros(3), 10.0, p, torch.zeros(1))
     with pytest.raises(ValueError, match="one target per camera"):
         multiview.fit_step_views(p, [object()], [], torch.zeros(3), 10.0, p, torch.zeros(1))
+
+
+def test_geometry_backward_rejects_misaligned_buffers():
+    """The geometry backward reads rotations as float4 and scales as float2:
+    a buffer that does not start on that boundary is rejected by the C-ABI
+    before any launch (fake addresses; nothing is dereferenced)."""
+    from gsplat._lib import lib
+
+    ok16, ok8, bad16, bad8 = 0x10000, 0x20000, 0x30008, 0x40004
+    fn = lib.dll.hx_hexels3d_geometry_backward
+
+    def call(scales, rotations, grad_scales, grad_rotations):
+        return fn(1, 1, ok16, scales, 1.0, rotations, ok16, ok16, 8, 8, ok16, ok16, ok16, ok16,
+                  None, None, ok16, None, 3, grad_scales, grad_rotations, 1, None)
+
+    for args in ((ok8, bad16, ok8, ok16), (ok8, ok16, ok8, bad16), (bad8, ok16, ok8, ok16),
+                 (ok8, ok16, bad8, ok16)):
+        assert call(*args) != 0
+        assert b"boundary" in lib.dll.hx_last_error()
+
+
+def test_tensors_on_another_device_are_rejected():
+    """Raw pointers run on the first tensor's device, so a tensor on another
+    device is rejected on the host (metadata only: cpu against meta)."""
+    import torch
+
+    from gsplat._lib import check_same_device
+
+    a = torch.zeros(4)
+    check_same_device(a, "pred", target=torch.zeros(4), grad=None)
+    with pytest.raises(RuntimeError, match="target is on meta but pred is on cpu"):
+        check_same_device(a, "pred", target=torch.zeros(4, device="meta"))

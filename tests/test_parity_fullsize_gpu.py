@@ -12,12 +12,14 @@ its sources) at the sizes the benchmark configurations are quoted on:
 Tolerances: integer outputs (radii, tile counts, intersection counts, keys,
 sorted lists, tile ranges, last indices, top-K ids) and the projection's
 float outputs bit-exact; images and per-pixel float state 1e-5 absolute
-(scaled by the channel's largest magnitude for depth); gradients per
-conftest.grad_parity_at_size (1e-4 relative, 1e-6 absolute near zero, or
-twice the reference's own run-to-run spread where that is larger).  The
-upstream gradients are seeded U[-1,1) per pixel so that every gradient is of
-order one and the absolute floor is tight.  Each test prints its figures
-(run with -rP to see them).
+(scaled by the channel's largest magnitude for depth).  Gradients: the stated
+criterion (1e-4 relative, 1e-6 absolute near zero) is not met by the
+reference against a second run of itself at these sizes (float32 atomics in
+another order), so conftest.assert_grad_at_size gates ours by the
+reference's own count of entries outside it and settles the worst entries
+against the float64 oracle.  The upstream gradients are seeded U[-1,1) per
+pixel so that every gradient is of order one and the absolute floor is
+tight.  Each test prints its figures (run with -rP to see them).
 """
 
 from __future__ import annotations

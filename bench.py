@@ -991,6 +991,8 @@ def run_ours_3d(args, world, rank, local):
     }
     if secondary is not None:
         line["single_view_surface"] = secondary
+    if world == 1 and not args.skip_extras and not surface:
+        line["configs_2d"] = other_configs_2d(args)
     if world == 1 and not args.skip_extras:
         cpu = cpu_baseline_3d(args, w)
         if cpu is not None:
@@ -999,6 +1001,37 @@ def run_ours_3d(args, world, rank, local):
         if ref is not None:
             line["ref_cuda_sm100a"] = ref
     return line
+
+
+def other_configs_2d(args):
+    """The 2D configurations measured in the same run, device-timed, each
+    beside the reference's CUDA kernels on the same inputs: Image-GS
+    256x256 / 4,096 and 2048x2048 / 100,000 Gaussians (top-10), 2D hexels
+    1024x1024 / 50,000 (top-10).  Each: device-resident fit step
+    (projection or binning, compositing, L2 loss, backward), L2 flushed
+    between steps."""
+    import workloads
+
+    out = {}
+    for cfg in ("imagegs_small", "imagegs_large", "hexels2d"):
+        sub = argparse.Namespace(**vars(args))
+        sub.config, sub.skip_extras = cfg, True
+        sub.steps, sub.warmup = max(args.steps, 20), max(args.warmup, 3)
+        line = (run_ours_hex2d if cfg == "hexels2d" else run_ours)(sub, 1, 0, 0)
+        w = workloads.hexels2d() if cfg == "hexels2d" else getattr(workloads, cfg)()
+        ref = ref_cuda_timing_hex2d(sub, w) if cfg == "hexels2d" else ref_cuda_timing(sub, w)
+        rl = line.get("roofline", {})
+        entry = {"workload": line["config"]["workload"], "value": line["value"],
+                 "unit": line["unit"], "ms_per_step": line["ms_per_step"],
+                 "steps": line["steps"], "stages_ms": line.get("stages_ms"),
+                 "roofline": {k: rl.get(k) for k in ("kernel", "achieved", "peak", "unit",
+                                                     "frac")},
+                 "clocks": line.get("clocks")}
+        if ref is not None:
+            entry["ref_cuda_sm100a"] = {"value": ref["value"], "ms_per_step": ref["ms_per_step"]}
+            entry["speedup_vs_ref_cuda"] = round(ref["ms_per_step"] / line["ms_per_step"], 3)
+        out[cfg] = entry
+    return out
 
 
 def single_view_comparison(args):
@@ -1186,25 +1219,30 @@ def workload_3d(name):
 def cpu_baseline_3d(args, w):
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    secs, mpix, desc = cpu_sample_run_3d(w, args.cpu_crop_tiles_3d)
+    secs, mpix, desc, parts = cpu_sample_run_3d(w, args.cpu_crop_tiles_3d)
     return {"value": round(mpix / secs, 5), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": desc, "seconds": round(secs, 3)}
+            "sample": desc, "seconds": round(secs, 3), **parts}
 
 
 def cpu_sample_run_3d(w, crop_tiles: int):
-    """One fwd+bwd of the oracle over a crop_tiles x crop_tiles tile crop at
-    the centre of view 0: preprocess of all surfels, binning of those meeting
-    the crop, RGB compositing and its backward through the geometry."""
+    """One view's fwd+bwd by the oracle, timed in two parts: the per-view
+    fixed work (preprocess of all surfels, binning of the whole frame,
+    geometry VJP of all surfels) in full, and the per-pixel work (compositing
+    and its backward) over a crop_tiles x crop_tiles tile crop at the centre
+    of view 0, extrapolated to the frame by pixel count.  Returns (frame
+    seconds, frame megapixels, description, parts)."""
     from oracle import hexels3d as o
 
     cam = w.cameras[0]
-    t0 = time.perf_counter()
-    mpix = o.sample_fwd_bwd(w, cam, crop_tiles, make_targets(w, [0], "cpu")[0])
-    secs = time.perf_counter() - t0
-    desc = (f"one fwd+bwd over a {crop_tiles}x{crop_tiles}-tile ({mpix:.4f} Mpix) centre crop "
-            f"of view 0 of {w.name}: preprocess of all surfels, binning of those meeting the "
-            f"crop, compositing, loss and backward to the surfel parameters; {secs:.2f} s")
-    return secs, mpix, desc
+    r = o.sample_fwd_bwd_split(w, cam, crop_tiles, make_targets(w, [0], "cpu")[0])
+    desc = (f"view 0 of {w.name}: per-view fixed work timed in full ({r['fixed_s']:.2f} s: "
+            f"preprocess of all surfels, binning of the frame, geometry VJP), compositing "
+            f"fwd+bwd timed over a {crop_tiles}x{crop_tiles}-tile ({r['crop_mpix']:.4f} Mpix) "
+            f"centre crop ({r['pixel_s']:.2f} s) and scaled to the frame by pixel count: "
+            f"{r['frame_s']:.1f} s per frame")
+    parts = {"fixed_s": round(r["fixed_s"], 3), "crop_pixel_s": round(r["pixel_s"], 3),
+             "crop_mpix": round(r["crop_mpix"], 5), "frame_s": round(r["frame_s"], 2)}
+    return r["frame_s"], r["frame_mpix"], desc, parts
 
 
 # ---------------------------------------------------------------------------
@@ -1315,9 +1353,13 @@ def run_reference(args, world, rank):
         "config": config,
         "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads,
                          "kind": "port",
-                         "sample": f"each step: one fwd+bwd over a {crop}x{crop}-tile centre "
-                                   f"crop ({mpix_total / steps:.4f} Mpix)"
-                                   + (" of view 0" if three_d else "")
+                         "sample": (f"each step: one view (view 0) fwd+bwd, its fixed work "
+                                    f"(preprocess of all surfels, binning of the frame, "
+                                    f"geometry VJP) timed in full and its compositing fwd+bwd "
+                                    f"timed over a {crop}x{crop}-tile centre crop and scaled to "
+                                    f"the frame by pixel count" if three_d else
+                                    f"each step: one fwd+bwd over a {crop}x{crop}-tile centre "
+                                    f"crop ({mpix_total / steps:.4f} Mpix)")
                                    + "; the reference ships CUDA only, so this is its "
                                    "algorithm restated on the CPU"},
         "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0,

@@ -809,3 +809,47 @@ def sample_fwd_bwd(w, cam, crop_tiles: int, target: torch.Tensor) -> float:
     npx = sum(min(BLOCK, H - int(t // gx) * BLOCK) * min(BLOCK, W - int(t % gx) * BLOCK)
               for t in tiles)
     return npx / 1e6
+
+
+def sample_fwd_bwd_split(w, cam, crop_tiles: int, target: torch.Tensor) -> Dict:
+    """The CPU baseline sample timed in its two parts, so that a full frame
+    can be extrapolated honestly: the per-view fixed part (preprocess of all
+    surfels, binning of the whole frame, geometry VJP of all surfels) is timed
+    in full, and the per-pixel part (compositing and its backward) over a
+    crop_tiles x crop_tiles tile crop at the image centre, with the RGB fit
+    loss mean((rgb - target)^2).  Returns seconds of each part, the crop's
+    and the frame's megapixels, and the frame time fixed + per-pixel x
+    frame / crop."""
+    import time
+
+    W, H = cam.width, cam.height
+    gx, gy = (W + BLOCK - 1) // BLOCK, (H + BLOCK - 1) // BLOCK
+    x0 = max(0, gx // 2 - crop_tiles // 2)
+    y0 = max(0, gy // 2 - crop_tiles // 2)
+    xs = np.arange(x0, min(gx, x0 + crop_tiles))
+    ys = np.arange(y0, min(gy, y0 + crop_tiles))
+    tiles = (ys[:, None] * gx + xs[None, :]).reshape(-1)
+    numel = 3 * H * W
+    tgt = target.reshape(3, H * W)
+
+    def loss_fn(out, pix):
+        d = out["color"] - tgt[:, pix].T.to(f32)
+        return (d * d).sum() / numel
+
+    t0 = time.perf_counter()
+    pre = preprocess(w.means3d, w.scales, w.rotations, w.opacities, cam.viewmatrix,
+                     cam.projmatrix, cam.campos, W, H, w.softness)
+    _, point_list, ranges = bin_surfels(pre, None)
+    t1 = time.perf_counter()
+    r = render(pre, ranges, point_list, w.colors, w.background, w.color_grads, None,
+               w.view_grads, tiles=tiles, loss_fn=loss_fn)
+    t2 = time.perf_counter()
+    G = r["grads"]
+    geometry_backward(w.means3d, w.scales, w.rotations, cam.projmatrix, cam.campos, W, H,
+                      pre["radii"], G["transMats"], G["view_dirs"])
+    t3 = time.perf_counter()
+    crop_px = sum(min(BLOCK, H - int(t // gx) * BLOCK) * min(BLOCK, W - int(t % gx) * BLOCK)
+                  for t in tiles)
+    fixed, pixel = (t1 - t0) + (t3 - t2), t2 - t1
+    return {"fixed_s": fixed, "pixel_s": pixel, "crop_mpix": crop_px / 1e6,
+            "frame_mpix": W * H / 1e6, "frame_s": fixed + pixel * (W * H) / crop_px}

@@ -65,8 +65,27 @@ def _compile(src: str, obj: str, extra: list[str]) -> None:
         raise RuntimeError(f"nvcc failed for {os.path.basename(src)}:\n{res.stderr}")
 
 
+ABI_TABLE = os.path.join(PKG, "gsplat", "_abi_table.py")
+
+
+def write_abi_table() -> None:
+    """gsplat/_abi_table.py from include/hexel_b200.h (the loader binds this
+    table, so an installed package needs no header)."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_hx_abi", os.path.join(PKG, "gsplat",
+                                                                         "_abi.py"))
+    abi = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(abi)
+    text = abi.render_table(abi.parse_header(os.path.join(INCLUDE, "hexel_b200.h")))
+    if not os.path.exists(ABI_TABLE) or open(ABI_TABLE).read() != text:
+        with open(ABI_TABLE, "w") as f:
+            f.write(text)
+
+
 def build(force: bool = False, jobs: int | None = None, verbose_ptxas: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
+    write_abi_table()
     sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     deps = _deps()
     extra = ["-Xptxas", "-v"] if verbose_ptxas else []

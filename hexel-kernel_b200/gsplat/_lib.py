@@ -21,36 +21,15 @@ import torch
 ABI_VERSION = 1
 _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libhexel_b200.so")
 
-_HEADER = os.path.join(
-    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
-    "include", "hexel_b200.h",
-)
-
 _RET = {"int": ctypes.c_int, "size_t": ctypes.c_size_t, "const char*": ctypes.c_char_p,
         "void": None, "unsigned long long": ctypes.c_ulonglong}
+_ARG = {"ptr": ctypes.c_void_p, "int": ctypes.c_int, "unsigned": ctypes.c_uint,
+        "float": ctypes.c_float, "size_t": ctypes.c_size_t, "int32_t": ctypes.c_int32,
+        "int64_t": ctypes.c_int64}
 
 
-def _arg_type(decl: str):
-    decl = decl.strip()
-    if "*" in decl or decl.startswith("cudaStream_t"):
-        return ctypes.c_void_p
-    base = decl.rsplit(" ", 1)[0].replace("const ", "").strip()
-    return {"int": ctypes.c_int, "unsigned": ctypes.c_uint, "float": ctypes.c_float,
-            "size_t": ctypes.c_size_t, "int32_t": ctypes.c_int32,
-            "int64_t": ctypes.c_int64}[base]
-
-
-def parse_header(path: str = _HEADER) -> dict:
-    """{name: (restype, [argtypes])} for every HX_API function of the header."""
-    text = re.sub(r"/\*.*?\*/", "", open(path).read(), flags=re.S)
-    out = {}
-    for m in re.finditer(r"HX_API\s+(int|size_t|const char\*|void|unsigned long long)\s+"
-                         r"(hx_\w+)\s*\((.*?)\);",
-                         text, flags=re.S):
-        ret, name, args = m.group(1), m.group(2), " ".join(m.group(3).split())
-        argv = [] if args in ("", "void") else [_arg_type(a) for a in args.split(",")]
-        out[name] = (_RET[ret], argv)
-    return out
+def _ctypes_signatures(table: dict) -> dict:
+    return {name: (_RET[ret], [_ARG[k] for k in args]) for name, (ret, args) in table.items()}
 
 
 class _Lib:
@@ -62,7 +41,9 @@ class _Lib:
             )
         self.path = path
         self.dll = ctypes.CDLL(path)
-        self.signatures = parse_header()
+        from ._abi_table import SIGNATURES
+
+        self.signatures = _ctypes_signatures(SIGNATURES)
         for name, (res, args) in self.signatures.items():
             fn = getattr(self.dll, name)
             fn.restype = res

@@ -8,7 +8,6 @@ from typing import Callable
 
 def _make_lazy_cuda_func(name: str) -> Callable:
     def call_cuda(*args, **kwargs):
-        # pylint: disable=import-outside-toplevel
         from ._backend import _C
 
         return getattr(_C, name)(*args, **kwargs)

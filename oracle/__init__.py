@@ -13,9 +13,11 @@ intrinsics, so floating-point results agree to tolerance, and integer outputs
 (binning, sorted lists, tile ranges) are exact given identical inputs.
 
 Parity pinning: the reference ships no tests, fixtures or golden vectors.
-The restatement is pinned by (a) ``tests/golden/`` vectors generated from it
-and reviewed against hand-computed cases, (b) fp64 finite-difference checks of
-its backward passes, and (c) on a GPU, comparison with the reference's own
-CUDA kernels compiled from its sources (``oracle/build_ref.py`` ->
-``oracle/_ref/``) on identical inputs.
+The restatement is pinned by (a) ``tests/golden/`` vectors recorded from the
+reference's own CUDA kernels (compiled from its sources by
+``oracle/build_ref.py`` into ``oracle/_ref/``) on seeded inputs on a B200,
+generator ``tests/golden/make_golden.py``, which ``tests/test_golden.py``
+checks this restatement against on the CPU; (b) fp64 finite-difference checks
+of its backward passes; (c) on a GPU, comparison with those reference kernels
+on identical inputs, including the benchmarked sizes.
 """

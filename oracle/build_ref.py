@@ -15,7 +15,9 @@ tolerance (images, gradients) against the reference on identical inputs.
 
 Usage::
 
-    python oracle/build_ref.py [--reference DIR] [--jobs N]
+    python oracle/build_ref.py --reference DIR [--jobs N]
+
+(or HEXEL_REFERENCE_DIR=DIR in the environment).
 
 The reference tree is only needed when building; the built ``.so`` files
 travel with the repository snapshot.
@@ -30,7 +32,6 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-DEFAULT_REFERENCE = "/root/reference"
 
 REF_FLAGS = ["-O3", "--use_fast_math", "--expt-relaxed-constexpr"]
 ARCH = ["-gencode=arch=compute_100a,code=sm_100a"]
@@ -62,7 +63,7 @@ def _build(name: str, sources: list[str], include: list[str], jobs: int) -> str:
     return dst
 
 
-def build(reference: str = DEFAULT_REFERENCE, jobs: int = 8) -> list[str]:
+def build(reference: str, jobs: int = 8) -> list[str]:
     if not os.path.isdir(reference):
         raise FileNotFoundError(f"reference tree not found at {reference}")
     os.makedirs(OUT, exist_ok=True)
@@ -79,9 +80,12 @@ def build(reference: str = DEFAULT_REFERENCE, jobs: int = 8) -> list[str]:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=DEFAULT_REFERENCE)
+    ap.add_argument("--reference", default=os.environ.get("HEXEL_REFERENCE_DIR"),
+                    help="the reference project's source tree (or HEXEL_REFERENCE_DIR)")
     ap.add_argument("--jobs", type=int, default=8)
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference DIR or set HEXEL_REFERENCE_DIR")
     for path in build(args.reference, args.jobs):
         print(path)
     return 0

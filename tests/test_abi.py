@@ -128,3 +128,19 @@ def test_tensors_on_another_device_are_rejected():
     check_same_device(a, "pred", target=torch.zeros(4), grad=None)
     with pytest.raises(RuntimeError, match="target is on meta but pred is on cpu"):
         check_same_device(a, "pred", target=torch.zeros(4, device="meta"))
+
+
+def test_packaged_abi_table_matches_the_header():
+    """The loader binds gsplat/_abi_table.py (written by the build), so an
+    installed package reads no header: the table must be the header's."""
+    import importlib.util
+
+    pkg = os.path.join(ROOT, "hexel-kernel_b200", "gsplat")
+    spec = importlib.util.spec_from_file_location("_hx_abi", os.path.join(pkg, "_abi.py"))
+    abi = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(abi)
+    from gsplat._abi_table import SIGNATURES
+
+    parsed = abi.parse_header(HEADER)
+    assert {k: (r, list(a)) for k, (r, a) in SIGNATURES.items()} == parsed
+    assert set(parsed) == set(declared())

@@ -937,7 +937,7 @@ def roofline_3d(step, stage_ms):
 
 
 def run_ours_3d(args, world, rank, local):
-    w = workload_3d(args.config)
+    w = workload_3d(args.config, args.views)
     surface = args.config == "hexels3d_single"
     step = Hexels3DStep(w, world, rank, surface)
     clocks = ClockSampler(local)
@@ -1304,11 +1304,11 @@ def ref_cuda_timing_3d(args, w, surface, steps=None):
                     + ", same inputs and loss"}
 
 
-def workload_3d(name):
+def workload_3d(name, views=64):
     import workloads
 
     if name == "hexels3d_multiview":
-        return workloads.hexels3d_multiview(64)
+        return workloads.hexels3d_multiview(views)
     if name == "hexels3d_single":
         return workloads.hexels3d_single()
     raise ValueError(name)
@@ -1412,7 +1412,7 @@ def run_reference(args, world, rank):
     torch.set_num_threads(threads)
     three_d = args.config.startswith("hexels3d")
     if three_d:
-        w = workload_3d(args.config)
+        w = workload_3d(args.config, args.views)
         crop = args.cpu_crop_tiles_3d
         sample = lambda: cpu_sample_run_3d(w, crop)[:2]  # noqa: E731
         cam = w.cameras[0]
@@ -1529,6 +1529,9 @@ def main():
     ap.add_argument("--config", default="hexels3d_multiview",
                     choices=["hexels3d_multiview", "hexels3d_single", "imagegs_large",
                              "imagegs_small", "hexels2d"])
+    ap.add_argument("--views", type=int, default=64,
+                    help="views of the multi-view orbit (64 is the benchmark configuration; "
+                         "fewer, e.g. 1, for a small profiling case)")
     ap.add_argument("--cpu-crop-tiles", type=int, default=16)
     ap.add_argument("--cpu-crop-tiles-3d", type=int, default=8)
     ap.add_argument("--ref-max-steps", type=int, default=3)

@@ -778,7 +778,7 @@ class Hexels3DStep:
                                  surf_state=o["surf_state"],
                                  surf_normals=o["normals"] if self.surface else None,
                                  accumulate_into=dict(zip(names, self.acc)),
-                                 blend_mask=o["blend_mask"])
+                                 blend_mask=o["blend_mask"], records=o["records"])
         if keep_info:
             saved = o["saved"]
             self.info.setdefault("num_rendered", []).append(o["num_rendered"])

@@ -647,7 +647,14 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
             int g = a.point_list[range.x + bstart + t];
             g = min(max(g, 0), a.P - 1);
             s_bm[t] = a.blend_mask ? a.blend_mask[range.x + bstart + t] : (unsigned char)0xff;
-            s_box[t] = stage_surfel<SURF, PREFILTER>(a, g, W, H, &s_prim[t]);
+            if (a.records) {
+                stage_record_async(a.records, g, &s_prim[t]);
+                cp_async_wait_all();  // this thread's own row: its box is read next
+                s_box[t] = PREFILTER ? make_short4(-32768, -32768, 32767, 32767)
+                                     : s_prim[t].q.box;
+            } else {
+                s_box[t] = stage_surfel<SURF, PREFILTER>(a, g, W, H, &s_prim[t]);
+            }
         }
         for (int t = tr; t < kBatch * L.ncomp; t += kThreads) s_acc[t] = 0.f;
         __syncthreads();
@@ -1058,7 +1065,9 @@ extern "C" int hx_hexels3d_render_backward(
     float* grad_normals, int overdraw_base_count, int color_model, int use_view_grads,
     const float* final_T, const int32_t* last_index, const float* final_T_surf,
     const int32_t* last_index_surf, const float* m1_surf, const float* m2_surf,
-    const int32_t* median_index, const uint8_t* blend_mask, cudaStream_t stream) {
+    const int32_t* median_index, const uint8_t* blend_mask, const void* records,
+    cudaStream_t stream) {
+    HX_REQUIRE((uintptr_t)records % 16 == 0, "records must start on a 16-byte boundary");
     HX_REQUIRE(image_width > 0 && image_height > 0, "invalid image dimensions");
     HX_REQUIRE(color_model >= 0 && color_model <= 3, "color_model must be 0..3");
     HX_REQUIRE(view_model >= 0 && view_model <= 2, "view_model must be 0..2");
@@ -1125,6 +1134,7 @@ extern "C" int hx_hexels3d_render_backward(
     a.m2_surf = m2_surf;
     a.median_index = median_index;
     a.blend_mask = blend_mask;
+    a.records = (const Surfel3D*)records;
 
     BwdLayout L;
     const bool explicit_vd = view_model == 2 || (use_view_grads && prefilter);

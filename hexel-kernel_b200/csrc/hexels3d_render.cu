@@ -234,8 +234,12 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const R
             if ((int)range.x + progress >= (int)range.y) continue;
             int g = a.point_list[range.x + progress];
             g = min(max(g, 0), a.P - 1);
-            stage_surfel<SURF, PREFILTER>(a, g, W, H, &s_prim[t]);
+            if (a.records)
+                stage_record_async(a.records, g, &s_prim[t]);
+            else
+                stage_surfel<SURF, PREFILTER>(a, g, W, H, &s_prim[t]);
         }
+        if (a.records) cp_async_wait_all();
         __syncthreads();
 
         const int batch_size = min(k3BlockSize, to_do);
@@ -362,8 +366,9 @@ extern "C" int hx_hexels3d_render_forward(
     float* owner_uv, float* owner_sdf, float* owner_depth, float* total_alpha, float* final_T,
     int32_t* last_index, float* final_T_surf, int32_t* last_index_surf, float* m1_surf,
     float* m2_surf, int32_t* median_index, int32_t* contrib_count, uint8_t* blend_mask,
-    cudaStream_t stream) {
+    const void* records, cudaStream_t stream) {
     HX_REQUIRE(image_width > 0 && image_height > 0, "invalid image dimensions");
+    HX_REQUIRE((uintptr_t)records % 16 == 0, "records must start on a 16-byte boundary");
     HX_REQUIRE(color_model >= 0 && color_model <= 3, "color_model must be 0..3");
     HX_REQUIRE(view_model >= 0 && view_model <= 2, "view_model must be 0..2");
     HX_REQUIRE(softness_stride == 1 || softness_stride == 3, "softness_stride must be 1 or 3");
@@ -433,10 +438,76 @@ extern "C" int hx_hexels3d_render_forward(
     a.median_index = median_index;
     a.contrib_count = contrib_count;
     a.blend_mask = blend_mask;
+    a.records = (const Surfel3D*)records;
     if (surf) return prefilter ? launch_render<true, true, false>(a, stream)
                                : launch_render<true, false, false>(a, stream);
     if (owner) return prefilter ? launch_render<false, true, true>(a, stream)
                                 : launch_render<false, false, true>(a, stream);
     return prefilter ? launch_render<false, true, false>(a, stream)
                      : launch_render<false, false, false>(a, stream);
+}
+
+namespace hx {
+namespace {
+
+// One thread per surfel: its record as the compositing kernels stage it.
+template <bool SURF, bool PREFILTER>
+__global__ void __launch_bounds__(256) surfel_records_kernel(const Render3DArgs a,
+                                                             Surfel3D* __restrict__ out) {
+    const int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= a.P) return;
+    stage_surfel<SURF, PREFILTER>(a, g, a.W, a.H, out + g);
+}
+
+}  // namespace
+}  // namespace hx
+
+extern "C" int hx_hexels3d_surfel_records(
+    int P, int image_width, int image_height, const float* transMats, const float* opacities,
+    const float* softnesses, int softness_stride, const float* colors, const float* color_grads,
+    const float* view_grads, const float* view_dirs, const float* normals,
+    const float* points_xy_center, int color_model, int use_view_grads, int surface,
+    void* records, cudaStream_t stream) {
+    HX_REQUIRE(P >= 0 && image_width > 0 && image_height > 0,
+               "hexels3d_surfel_records: bad sizes");
+    if (P == 0) return HX_OK;
+    HX_REQUIRE(softness_stride == 1 || softness_stride == 3, "softness_stride must be 1 or 3");
+    HX_REQUIRE(transMats && opacities && softnesses && colors && view_dirs && records,
+               "hexels3d_surfel_records: null pointer");
+    HX_REQUIRE((uintptr_t)records % 16 == 0, "records must start on a 16-byte boundary");
+    HX_REQUIRE(color_model < 1 || color_grads, "color_grads required for color_model >= 1");
+    HX_REQUIRE(!use_view_grads || view_grads, "view_grads required with use_view_grads");
+    HX_REQUIRE(!surface || normals, "surface records need normals");
+    Render3DArgs a = {};
+    a.P = P;
+    a.W = image_width;
+    a.H = image_height;
+    a.transMats = transMats;
+    a.opacities = opacities;
+    a.softnesses = softnesses;
+    a.softness_stride = softness_stride;
+    a.colors = colors;
+    a.color_grads = color_grads;
+    a.view_grads = view_grads;
+    a.view_dirs = view_dirs;
+    a.normals = normals;
+    a.points_xy_center = (const float2*)points_xy_center;
+    a.color_model = color_model;
+    a.use_view_grads = use_view_grads != 0;
+    Surfel3D* out = (Surfel3D*)records;
+    const int blocks = ceil_div(P, 256);
+    const bool prefilter = points_xy_center != nullptr;
+    if (surface) {
+        if (prefilter)
+            surfel_records_kernel<true, true><<<blocks, 256, 0, stream>>>(a, out);
+        else
+            surfel_records_kernel<true, false><<<blocks, 256, 0, stream>>>(a, out);
+    } else {
+        if (prefilter)
+            surfel_records_kernel<false, true><<<blocks, 256, 0, stream>>>(a, out);
+        else
+            surfel_records_kernel<false, false><<<blocks, 256, 0, stream>>>(a, out);
+    }
+    HX_LAUNCH_CHECK("surfel_records_kernel");
+    return HX_OK;
 }

@@ -141,6 +141,8 @@ struct Prep3DArgs {
 };
 
 // Pointers and options of the forward compositing kernel.
+struct Surfel3D;  // the staged per-surfel record (hx_hexmath3d.cuh)
+
 struct Render3DArgs {
     const uint2* ranges;
     const int* point_list;
@@ -193,6 +195,9 @@ struct Render3DArgs {
     // optional per-intersection mask of the 8x4 pixel blocks that met the
     // surfel with alpha >= kBlendMarkAlpha while compositing, or null
     unsigned char* blend_mask;
+    // optional per-surfel staged records (hx_hexels3d_surfel_records), or
+    // null: the kernel then gathers each record from the arrays above
+    const Surfel3D* records;
 };
 
 struct Backward3DArgs {
@@ -247,6 +252,8 @@ struct Backward3DArgs {
     const int* median_index;
     // the forward's blend_mask, or null (no list entry skipped)
     const unsigned char* blend_mask;
+    // optional per-surfel staged records (hx_hexels3d_surfel_records), or null
+    const Surfel3D* records;
 };
 
 }  // namespace hx

@@ -234,6 +234,27 @@ __device__ __forceinline__ short4 stage_surfel(const Args& a, int g, int W, int 
     return box;
 }
 
+// Copies surfel g's 128-byte record (written once per view by
+// hx_hexels3d_surfel_records with the same layout stage_surfel produces)
+// into the shared row `row` as eight 16-byte asynchronous copies that bypass
+// L1; the issuing thread completes them with cp_async_wait_all() before it
+// or, after a barrier, any other thread reads the row.
+__device__ __forceinline__ void stage_record_async(const Surfel3D* records, int g,
+                                                   Surfel3D* row) {
+    const char* src = reinterpret_cast<const char*>(records + g);
+    const unsigned dst = (unsigned)__cvta_generic_to_shared(row);
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst + 16 * c),
+                     "l"(src + 16 * c)
+                     : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+
 // Ray-splat intersection of pixel (px, py) with a surfel of transform rows
 // Tu, Tv, Tw: returns false when the ray is parallel or the hit is in front
 // of the near plane; otherwise (u, v), depth, SDF, boundary weight and alpha.

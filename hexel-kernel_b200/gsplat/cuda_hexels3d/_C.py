@@ -128,8 +128,11 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                   conservative_bounds, debug, *, return_contrib=False, return_overdraw=False,
                   return_overdraw_hits=False, return_surface=False, overdraw_base_count=-1,
                   owner=False, return_median_depth=False, save=False, save_surface=False,
-                  count_contrib=False):
-    """rasterize_hexels3d_forward_impl (hexels3d_forward.cu:2679-3481)."""
+                  count_contrib=False, records=True):
+    """rasterize_hexels3d_forward_impl (hexels3d_forward.cu:2679-3481).
+    With `records` the per-surfel staged records are written once after the
+    preprocess (hx_hexels3d_surfel_records) and the compositing stages them
+    with asynchronous copies; they are returned for the backward."""
     W, H = int(image_width), int(image_height)
     P, stride = _checks(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
                         specular_ks, specular_log_s, opacities, softnesses, viewmatrix,
@@ -211,6 +214,16 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                    torch.empty((H, W), **f32), torch.empty((2, H, W), **f32),
                    torch.empty((H, W), **f32), torch.empty((H, W), **f32),
                    torch.empty((H, W), **f32))
+        rec = None
+        if records and num_rendered > 0:
+            rec = torch.empty((P, 32), **f32)  # 128-byte records
+            lib.call("hx_hexels3d_surfel_records", P, W, H, ptr(transMats), ptr(opacities_out),
+                     ptr(softnesses_out), stride, ptr(colors),
+                     ptr(color_grads) if color_model >= 1 else None,
+                     ptr(view_grads) if use_view_grads else None, ptr(view_dirs),
+                     ptr(normals) if return_surface else None,
+                     ptr(points_xy_center) if prefilter_edge_on else None, int(color_model),
+                     int(bool(use_view_grads)), int(bool(return_surface)), ptr(rec), s)
         # launched even with nothing binned: every pixel is then the background
         lib.call("hx_hexels3d_render_forward", P, num_rendered, ptr(ranges),
                  ptr(values_sorted), ptr(points_xy_center) if prefilter_edge_on else None,
@@ -232,7 +245,7 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                  *(ptr(t) for t in own) if own else (None,) * 6,
                  ptr(final_T) if save else None, ptr(last_index) if save else None,
                  *(ptr(t) for t in surf_state) if surf_state else (None,) * 5,
-                 ptr(contrib_count) if count_contrib else None, ptr(blend_mask), s)
+                 ptr(contrib_count) if count_contrib else None, ptr(blend_mask), ptr(rec), s)
         _mark("render_fwd")
         if debug:
             torch.cuda.synchronize(dev)
@@ -245,7 +258,7 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                 overdraw_hits=overdraw_hits, surf_depth=surf_depth, surf_alpha=surf_alpha,
                 surf_maps=surf_maps, saved=saved, surf_state=surf_state, normals=normals,
                 owner=own, num_rendered=num_rendered, contrib_count=contrib_count,
-                blend_mask=blend_mask)
+                blend_mask=blend_mask, records=rec)
 
 
 def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, color_quads,
@@ -255,7 +268,7 @@ def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, col
                    image_height, tan_fovx, tan_fovy, softness, scale_modifier, color_model,
                    view_model, use_view_grads, overdraw_base_count, prefilter_edge_on,
                    conservative_bounds, debug, saved, surf_state=None, surf_normals=None,
-                   accumulate_into=None, blend_mask=None):
+                   accumulate_into=None, blend_mask=None, records=None):
     """rasterize_hexels3d_backward_impl (hexels3d_forward.cu:4882-5582) on the
     forward's saved state.  With `accumulate_into` (a dict from parameter
     name -- means3d, scales, rotations, colors, color_grads, view_grads,
@@ -294,6 +307,10 @@ def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, col
     (radii, transMats, opacities_out, softnesses_out, view_dirs, normals_saved, points_xy_center,
      ranges, values_sorted, final_T, last_index) = saved
     num_rendered = values_sorted.numel()
+    if records is not None:
+        check_input(records, "records")
+        _check(records.dtype == torch.float32 and tuple(records.shape) == (P, 32),
+               "records must be the forward's (P, 32) float32 staged records")
     if blend_mask is not None:
         check_input(blend_mask, "blend_mask")
         _check(blend_mask.dtype == torch.uint8 and blend_mask.numel() >= num_rendered,
@@ -375,7 +392,7 @@ def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, col
                      int(overdraw_base_count), int(color_model), int(bool(use_view_grads)),
                      ptr(final_T), ptr(last_index),
                      *(ptr(t) for t in surf_state) if has_surface else (None,) * 5,
-                     ptr(blend_mask), s)
+                     ptr(blend_mask), ptr(records), s)
             _mark("render_bwd")
             lib.call("hx_hexels3d_geometry_backward", P, num_rendered, ptr(means3d), ptr(scales),
                      float(scale_modifier), ptr(rotations), ptr(projmatrix), ptr(campos), W, H,
@@ -497,7 +514,7 @@ def rasterize_hexels3d_backward(*args):
                       return_median_depth=median, save=True, save_surface=surface)
     return _backward_core(*args, o["saved"], surf_state=o["surf_state"],
                           surf_normals=o["normals"] if surface else None,
-                          blend_mask=o["blend_mask"])
+                          blend_mask=o["blend_mask"], records=o["records"])
 
 
 def _not_provided(name: str):

@@ -212,7 +212,7 @@ class _RasterizeHexels3D(Function):
         ctx.save_for_backward(means3d, means2d, scales, rotations, colors, color_grads,
                               color_quads, view_grads, specular_ks, specular_log_s, opacities,
                               softnesses, viewmatrix, projmatrix, campos, background, *saved,
-                              *surf, o["normals"], o["blend_mask"])
+                              *surf, o["normals"], o["blend_mask"], o["records"])
         ctx.opts = opts
         ctx.mark_non_differentiable(o["radii"], o["contrib"], o["overdraw_hits"])
         return (o["out_color"], o["radii"], o["contrib"], o["overdraw"], o["overdraw_hits"],
@@ -225,6 +225,7 @@ class _RasterizeHexels3D(Function):
         surf = t[27:27 + ctx.n_surf]
         normals = t[27 + ctx.n_surf]
         blend_mask = t[28 + ctx.n_surf]
+        records = t[29 + ctx.n_surf]
         opts = ctx.opts
         empty = _empty_like(inputs[0])
 
@@ -244,7 +245,8 @@ class _RasterizeHexels3D(Function):
             opts["use_view_grads"], opts["overdraw_base_count"], opts["prefilter_edge_on"],
             opts["conservative_bounds"], opts["debug"], saved,
             surf_state=tuple(surf) if surf else None,
-            surf_normals=normals if opts["return_surface"] else None, blend_mask=blend_mask)
+            surf_normals=normals if opts["return_surface"] else None, blend_mask=blend_mask,
+            records=records)
         means2d = inputs[1]
         g2d = grads[1] if means2d.numel() > 0 else None
         return (grads[0], g2d, *grads[2:], None, None, None, None, None)

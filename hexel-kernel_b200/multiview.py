@@ -87,7 +87,8 @@ def fit_step_views(params: Sequence[torch.Tensor], cams: Sequence, targets: Sequ
                               cam.projmatrix, cam.campos, background, g_color, e, e, e, e,
                               cam.width, cam.height, cam.tan_fovx, cam.tan_fovy, softness, 1.0,
                               color_model, view_model, use_view_grads, -1, False, False, False,
-                              o["saved"], accumulate_into=acc, blend_mask=o["blend_mask"])
+                              o["saved"], accumulate_into=acc, blend_mask=o["blend_mask"],
+                              records=o["records"])
             del o, g_color
     if pipeline is not None:
         for s in streams:

@@ -341,7 +341,27 @@ HX_API int hx_hexels3d_render_forward(
     float* owner_uv, float* owner_sdf, float* owner_depth, float* total_alpha, float* final_T,
     int32_t* last_index, float* final_T_surf, int32_t* last_index_surf, float* m1_surf,
     float* m2_surf, int32_t* median_index, int32_t* contrib_count, uint8_t* blend_mask,
-    cudaStream_t stream);
+    const void* records, cudaStream_t stream);
+
+/* Per-surfel staged records for the compositing pair (no reference
+ * counterpart: the reference gathers every field from its arrays for every
+ * list entry, hexels3d_forward.cu:673-760).  Writes, for each of the P
+ * surfels, the 128-byte record the compositing kernels stage into shared
+ * memory -- transform rows, opacity, softnesses, base colour, linear view
+ * colour, colour gradients, viewer-facing normal (surface), the pixel box
+ * outside which alpha < 1/255 (or the prefilter centre) and the id -- into
+ * `records` (P x 128 bytes, 16-byte aligned).  Passing it as `records` to
+ * hx_hexels3d_render_forward / _backward lets each list entry be staged with
+ * asynchronous 16-byte copies instead of gathered and recomputed; the
+ * records must come from the same per-surfel inputs, colour model,
+ * use_view_grads, surface and prefilter settings as those calls (both may
+ * also be given NULL, gathering as before). */
+HX_API int hx_hexels3d_surfel_records(
+    int P, int image_width, int image_height, const float* transMats, const float* opacities,
+    const float* softnesses, int softness_stride, const float* colors, const float* color_grads,
+    const float* view_grads, const float* view_dirs, const float* normals,
+    const float* points_xy_center, int color_model, int use_view_grads, int surface,
+    void* records, cudaStream_t stream);
 
 /* Reverse traversal VJP; replaces render_hexels3d_backward<S,F> and its
  * launches (hexels3d_forward.cu:1749-2492, 5323-5505).  Uses the forward's
@@ -367,7 +387,8 @@ HX_API int hx_hexels3d_render_backward(
     float* grad_normals, int overdraw_base_count, int color_model, int use_view_grads,
     const float* final_T, const int32_t* last_index, const float* final_T_surf,
     const int32_t* last_index_surf, const float* m1_surf, const float* m2_surf,
-    const int32_t* median_index, const uint8_t* blend_mask, cudaStream_t stream);
+    const int32_t* median_index, const uint8_t* blend_mask, const void* records,
+    cudaStream_t stream);
 
 /* VJP from transforms (and view directions / normals) to means3d, scales and
  * WXYZ rotations, plus the screen-gradient proxy for means2d and the

@@ -61,7 +61,7 @@ def mse_loss(pred, target):
 
 # DRAM bytes per launch of the roofline kernels, from the committed ncu
 # captures of these configurations (read + write)
-TRAFFIC_R3D_BWD_1080 = int((401.384192 + 67.767296) * 1e6)   # render3d_bwd, one 1080p view
+TRAFFIC_R3D_BWD_1080 = int((277.370624 + 56.484864) * 1e6)   # render3d_bwd, one 1080p view
 TRAFFIC_TOPK_FWD_2048 = int((45.213952 + 163.590144) * 1e6)  # topk_fwd, 2048^2 / 100k
 TRAFFIC_HEX_FWD_1024 = int((2.483712 + 7.526656) * 1e6)      # hexel_fwd, 1024^2 / 50k
 
@@ -784,8 +784,9 @@ class Hexels3DStep:
             self.info.setdefault("num_rendered", []).append(o["num_rendered"])
             self.info.setdefault("evaluated_pairs", []).append(
                 int(saved[10].to(torch.int64).sum().item()))
-            self.info.setdefault("blended_pairs", []).append(
-                int(o["contrib_count"].to(torch.int64).sum().item()))
+            counts = o["contrib_count"].to(torch.int64).sum((1, 2)).tolist()
+            self.info.setdefault("blended_pairs", []).append(int(counts[0]))
+            self.info.setdefault("culled_evaluated_pairs", []).append(int(counts[1]))
         return loss, grads
 
     def run_pipelined(self):
@@ -912,9 +913,11 @@ def roofline_3d(step, stage_ms):
     nv = len(step.views)
     blended = sum(step.info.get("blended_pairs", [0]))
     evaluated = sum(step.info.get("evaluated_pairs", [0]))
+    culled = sum(step.info.get("culled_evaluated_pairs", [0]))
     bwd_ms, fwd_ms = stage_ms["render_bwd"], stage_ms["render_fwd"]
     bwd = blended * BWD_FLOP_PER_PAIR / (bwd_ms / 1e3) / 1e12 if bwd_ms > 0 else 0.0
     fwd = evaluated * FWD_FLOP_PER_PAIR / (fwd_ms / 1e3) / 1e12 if fwd_ms > 0 else 0.0
+    fwd_c = culled * FWD_FLOP_PER_PAIR / (fwd_ms / 1e3) / 1e12 if fwd_ms > 0 else 0.0
     return {
         "kernel": "render3d_bwd_kernel (rasterize_hexels3d backward compositing)",
         "bound": "fp32",
@@ -925,14 +928,19 @@ def roofline_3d(step, stage_ms):
         "traffic": TRAFFIC_R3D_BWD_1080 if nv and step.H == 1080 and not step.surface else None,
         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum per launch (one view), "
                           "one ncu capture of this configuration "
-                          "(profiles/render3d_bwd_64views.md)",
+                          "(profiles/render3d_bwd_1080p_1M.md)",
         "peak_source": "nominal FP32 FMA rate, 148 SMs x 128 lanes x 2 x max SM clock "
                        "(MEASURED_PEAKS.json has no FP32 figure)",
         "work": f"{blended} blended (pixel, surfel) pairs over {nv} views x "
                 f"{BWD_FLOP_PER_PAIR:.0f} FLOP per step on rank 0",
         "forward": {"kernel": "render3d_fwd_kernel", "achieved": round(fwd, 3),
                     "frac": round(fwd / fp32_peak, 4),
-                    "work": f"{evaluated} evaluated pairs x {FWD_FLOP_PER_PAIR:.0f} FLOP"},
+                    "work": f"{evaluated} pairs visited before each pixel terminates (sum of "
+                            f"the last indices) x {FWD_FLOP_PER_PAIR:.0f} FLOP",
+                    "after_box_cull": {
+                        "achieved": round(fwd_c, 3), "frac": round(fwd_c / fp32_peak, 4),
+                        "work": f"{culled} pairs evaluated after the warps' pixel-box cull x "
+                                f"{FWD_FLOP_PER_PAIR:.0f} FLOP (the kernel's actual work)"}},
     }
 
 

@@ -22,7 +22,7 @@ struct FwdPixel {
     float px, py;
     bool done_color, done_surf;
     float T, C0, C1, C2;
-    int n_visited, n_blended;
+    int n_visited, n_blended, n_evaluated;
     float overdraw, overdraw_hits;
     float T_surf, D_surf, median_depth, M1, M2, distortion;
     float3 N_surf;
@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const R
         p.done_surf = SURF ? !inside[k] : true;
         p.T = 1.0f;
         p.C0 = p.C1 = p.C2 = 0.f;
-        p.n_visited = p.n_blended = 0;
+        p.n_visited = p.n_blended = p.n_evaluated = 0;
         p.overdraw = p.overdraw_hits = 0.f;
         p.T_surf = 1.0f;
         p.D_surf = p.median_depth = p.M1 = p.M2 = p.distortion = 0.f;
@@ -264,9 +264,11 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const R
             bool all_done = true, mark = false;
 #pragma unroll
             for (int k = 0; k < PPT; ++k) {
-                if (!(q[k].done_color && q[k].done_surf))
+                if (!(q[k].done_color && q[k].done_surf)) {
                     mark |= fwd_pair<SURF, PREFILTER, OWNER>(a, s, i * k3BlockSize + j, j, q[k],
                                                              s_contrib);
+                    ++q[k].n_evaluated;
+                }
                 all_done = all_done && q[k].done_color && q[k].done_surf;
             }
             if (mark) s_wmark[warp][j] = 1;  // same value from every marking lane
@@ -298,7 +300,10 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const R
             a.final_T[pix] = p.T;
             a.last_index[pix] = p.n_visited;
         }
-        if (a.contrib_count) a.contrib_count[pix] = p.n_blended;
+        if (a.contrib_count) {
+            a.contrib_count[pix] = p.n_blended;
+            a.contrib_count[HW + pix] = p.n_evaluated;
+        }
         // With nothing binned every tile range is empty and the pixel is the
         // background, as in the reference (hexels3d_forward.cu:3300-3470).
         a.out_color[pix] = p.C0 + p.T * a.bg[0];

@@ -190,7 +190,8 @@ struct Render3DArgs {
     float* m1_surf;
     float* m2_surf;
     int* median_index;
-    // optional per-pixel count of blended (contributing) pairs, or null
+    // optional per-pixel counts (2,H,W) of the blended (contributing) pairs
+    // and of the pairs evaluated after the warp's box cull, or null
     int* contrib_count;
     // optional per-intersection mask of the 8x4 pixel blocks that met the
     // surfel with alpha >= kBlendMarkAlpha while compositing, or null

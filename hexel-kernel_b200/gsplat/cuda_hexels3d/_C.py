@@ -196,7 +196,8 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
             surf_maps = torch.empty((kNumChannels + 1 + int(return_median_depth), H, W), **f32)
         else:
             surf_depth = surf_alpha = surf_maps = torch.empty((0,), **f32)
-        contrib_count = torch.empty((H, W), **i32) if count_contrib else None
+        # per pixel: blended pairs, pairs evaluated after the warps' box cull
+        contrib_count = torch.empty((2, H, W), **i32) if count_contrib else None
         # per intersection: the 8x4 pixel blocks that may blend it (lets the
         # backward skip the list entries no pixel of its block blends)
         blend_mask = (torch.empty((max(num_rendered, 1),), dtype=torch.uint8, device=dev)

@@ -319,9 +319,12 @@ HX_API int hx_hexels3d_bin(int P, int num_rendered, int image_width, int image_h
  * sdf, depth, total alpha); final_T and last_index (H,W) for the RGB
  * backward; final_T_surf, last_index_surf, m1_surf, m2_surf, median_index
  * (H,W) for the surface backward.  points_xy_center non-NULL selects the
- * prefilter path.  contrib_count (H,W int32, may be NULL; no reference
- * counterpart) receives the number of blended (pixel, surfel) pairs per pixel,
- * the work unit of the backward traversal.  blend_mask (num_rendered uint8,
+ * prefilter path.  contrib_count (2,H,W int32, may be NULL; no reference
+ * counterpart) receives per pixel the number of blended (pixel, surfel)
+ * pairs (plane 0, the work unit of the backward traversal) and of the pairs
+ * evaluated after the warp's box cull (plane 1, the forward's work).
+ * records (may be NULL) are hx_hexels3d_surfel_records' output for the same
+ * inputs and settings.  blend_mask (num_rendered uint8,
  * may be NULL; no reference counterpart) receives, per sorted intersection of
  * every list entry the traversal staged, bit w (w = 2 * (y / 4) + x / 8 for
  * the pixel (x, y) within its 16x16 tile) set when a pixel of that 8x4 block

@@ -44,9 +44,6 @@ constexpr int kFixCg = 3, kFixOp = 9, kFixSoft = 10, kFixTm = 13, kFixN = 22, kF
 // gradients): colour 0-2, colour gradients 3-8, opacity 9, transform 10-18;
 // padded to 24 slots.
 constexpr int kLiteCg = 3, kLiteOp = 9, kLiteTm = 10, kLiteComp = 19;
-// Packed plain-RGB path: list entries with at most this many blended pairs
-// in a warp skip the warp reduction (their lanes add into shared memory).
-constexpr int kPackDirect = 2;
 
 // Sum of a 24-slot vector over the warp: three reduce-scatter halvings
 // (over lane bits 4, 3, 2) leave each lane 3 slots summed over 8 lanes, then
@@ -699,14 +696,9 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
 #pragma unroll
                 for (int c = 0; c < 24; ++c) acc[c] = 0.f;
                 int halves = 0;
-                unsigned holders = 0u;  // lanes holding at least one pair
 #pragma unroll
-                for (int k = 0; k < PPT; ++k) {
-                    halves += m[k] != 0u;
-                    holders |= m[k];
-                }
+                for (int k = 0; k < PPT; ++k) halves += m[k] != 0u;
                 if (halves > 1 && n_pairs <= 32) {
-                    holders = n_pairs == 32 ? 0xffffffffu : ((1u << n_pairs) - 1u);
                     // pairs of both halves: packed one per lane (one pass)
                     __syncwarp();  // the previous entry's pairs have been read
                     int base = 0;
@@ -733,20 +725,13 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
                             rgb_pair_vjp(s, rec[k], q[k].px, q[k].py, acc);
                 }
                 float* dst = s_acc + (idx - bstart) * kLiteComp;
-                if (n_pairs <= kPackDirect) {
-                    // a few pairs: the lanes holding them add straight into the
-                    // batch accumulator (at most kPackDirect-way address conflicts)
-                    if (holders & (1u << lane)) {
-#pragma unroll
-                        for (int c = 0; c < kLiteComp; ++c) atomicAdd(dst + c, acc[c]);
-                    }
-                } else {
-                    const int start = warp_reduce_scatter24(acc, lane);
-                    const int c = lane & 3;
-                    const float val = c == 0 ? acc[0] : (c == 1 ? acc[1] : acc[2]);
-                    const int comp = start + c;
-                    if (c < 3 && comp < kLiteComp && val != 0.f) atomicAdd(dst + comp, val);
-                }
+                // (shared-memory atomics straight from the few lanes holding
+                // pairs measured slower than this reduction even for one pair)
+                const int start = warp_reduce_scatter24(acc, lane);
+                const int c = lane & 3;
+                const float val = c == 0 ? acc[0] : (c == 1 ? acc[1] : acc[2]);
+                const int comp = start + c;
+                if (c < 3 && comp < kLiteComp && val != 0.f) atomicAdd(dst + comp, val);
             } else {
             float acc[N];
 #pragma unroll

@@ -714,7 +714,7 @@ class Hexels3DStep:
     STAGES = ("preprocess", "scan", "bin", "render_fwd", "loss", "render_bwd", "geometry_bwd",
               "accumulate", "allreduce")
 
-    def __init__(self, w, world: int, rank: int, surface: bool):
+    def __init__(self, w, world: int, rank: int, surface: bool, group: int = 1):
         from gsplat.cuda_hexels3d import _C
 
         self.C = _C
@@ -739,6 +739,8 @@ class Hexels3DStep:
         self.acc = self.grads.views
         # the RGB step's views are pipelined over two streams (multiview.py)
         self.pipeline = None if surface else ViewPipeline(self.params, streams=2)
+        # the timed step bins this many of the rank's views together
+        self.group = max(1, min(group, len(self.views)))
         self.marks: list = []
         self.stage_ms = {k: 0.0 for k in self.STAGES}
         self.info: dict = {}
@@ -798,7 +800,7 @@ class Hexels3DStep:
             return self.grads.loss
         self.grads.zero_()
         fit_step_views(self.params, self.cams, self.targets, self.bg, self.w.softness,
-                       self.acc, self.grads.loss, self.pipeline)
+                       self.acc, self.grads.loss, self.pipeline, group=self.group)
         self.grads.all_reduce_(self.world)
         return self.grads.loss
 
@@ -947,7 +949,7 @@ def roofline_3d(step, stage_ms):
 def run_ours_3d(args, world, rank, local):
     w = workload_3d(args.config, args.views)
     surface = args.config == "hexels3d_single"
-    step = Hexels3DStep(w, world, rank, surface)
+    step = Hexels3DStep(w, world, rank, surface, args.group)
     clocks = ClockSampler(local)
     clocks.start()
     ms_per_step, stage_ms, launches = time_step_3d(step, args.steps, args.warmup, world)
@@ -958,7 +960,7 @@ def run_ours_3d(args, world, rank, local):
     if not args.skip_extras:
         e2e_autograd = run_e2e_3d(w, args, world, rank, surface, step.views)
         e2e = e2e_autograd if surface else run_e2e_3d_pipelined(w, args, world, rank,
-                                                                step.views)
+                                                                step.views, step.group)
     secondary = None
     if world == 1 and not args.skip_extras and not surface:
         secondary = single_view_comparison(args)
@@ -1067,7 +1069,7 @@ def single_view_comparison(args):
     return out
 
 
-def run_e2e_3d_pipelined(w, args, world, rank, views):
+def run_e2e_3d_pipelined(w, args, world, rank, views, group=1):
     """The RGB multi-view step end to end through the repo's multi-view fit
     API (multiview.fit_step_views: this rank's views pipelined over two
     streams, gradients added into one flat buffer, NCCL all-reduce in place)
@@ -1115,7 +1117,7 @@ def run_e2e_3d_pipelined(w, args, world, rank, views):
             ev["s0"].record(main)
         grads.zero_()
         fit_step_views(bufs[b][0], cams, bufs[b][1], bg, w.softness, grads.views, grads.loss,
-                       pipe)
+                       pipe, group=group)
         free[b].record(main)
         if timed:
             ev["s1"].record(main)
@@ -1540,6 +1542,8 @@ def main():
     ap.add_argument("--views", type=int, default=64,
                     help="views of the multi-view orbit (64 is the benchmark configuration; "
                          "fewer, e.g. 1, for a small profiling case)")
+    ap.add_argument("--group", type=int, default=1,
+                    help="multi-view step: views binned together per group (1 = per view)")
     ap.add_argument("--cpu-crop-tiles", type=int, default=16)
     ap.add_argument("--cpu-crop-tiles-3d", type=int, default=8)
     ap.add_argument("--ref-max-steps", type=int, default=3)

@@ -470,16 +470,21 @@ __global__ void __launch_bounds__(256) gather_counts_kernel(int n, const int* __
 // in depth order.  A warp takes 32 consecutive surfels, whose entries are one
 // contiguous run of the output: it scans their tile counts and then writes
 // the run 32 consecutive entries at a time, each lane finding the surfel
-// that owns its entry by a binary search over the warp's prefix sums.
+// that owns its entry by a binary search over the warp's prefix sums.  With
+// several views (P = views x P_view entries, view-major), entry order[i] =
+// view * P_view + surfel, the key is view * tiles + tile and the value the
+// surfel index within its view.
 __global__ void __launch_bounds__(256) emit3d_ordered_kernel(
     int P, int num_rendered, const int* __restrict__ order, const float2* __restrict__ points_xy,
     const int* __restrict__ offsets, const int* __restrict__ radii,
     const int2* __restrict__ tile_radii, uint2 grid, unsigned* __restrict__ keys,
-    int* __restrict__ vals) {
+    int* __restrict__ vals, int P_view) {
     const unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    int cnt = 0, x0 = 0, y0 = 0, w = 1, sid = 0, off = 0;
+    const unsigned tiles = grid.x * grid.y;
+    int cnt = 0, x0 = 0, y0 = 0, w = 1, sid = 0, off = 0, lid = 0;
+    unsigned key_base = 0;
     if (i < P) {
         sid = min(max(order[i], 0), P - 1);
         const int2 tr = tile_radii[sid];
@@ -494,6 +499,9 @@ __global__ void __launch_bounds__(256) emit3d_ordered_kernel(
             }
         }
         off = i == 0 ? 0 : offsets[i - 1];
+        const int view = sid / P_view;
+        key_base = (unsigned)view * tiles;
+        lid = sid - view * P_view;
     }
     int incl = cnt;
 #pragma unroll
@@ -516,14 +524,15 @@ __global__ void __launch_bounds__(256) emit3d_ordered_kernel(
         const int jx0 = __shfl_sync(full, x0, j);
         const int jy0 = __shfl_sync(full, y0, j);
         const int jw = __shfl_sync(full, w, j);
-        const int jid = __shfl_sync(full, sid, j);
+        const int jid = __shfl_sync(full, lid, j);
         const int jex = __shfl_sync(full, excl, j);
+        const unsigned jkb = __shfl_sync(full, key_base, j);
         const int pos = base + e;
         if (e < total && pos >= 0 && pos < num_rendered) {
             const int local = e - jex;
             const unsigned ty = (unsigned)(jy0 + local / jw);
             const unsigned tx = (unsigned)(jx0 + local % jw);
-            keys[pos] = ty * grid.x + tx;
+            keys[pos] = jkb + ty * grid.x + tx;
             vals[pos] = jid;
         }
     }
@@ -644,7 +653,7 @@ extern "C" int hx_hexels3d_bin_ordered(int P, int num_rendered, int image_width,
     p += align256(sizeof(int) * (size_t)num_rendered);
     emit3d_ordered_kernel<<<ceil_div(P, 256), 256, 0, stream>>>(
         P, num_rendered, order, (const float2*)points_xy_image, offsets, radii,
-        (const int2*)tile_radii, grid, keys, vals);
+        (const int2*)tile_radii, grid, keys, vals, P);
     HX_LAUNCH_CHECK("emit3d_ordered_kernel");
     int rc = sort_pairs<uint32_t>(keys, vals, keys_out, point_list, num_rendered, 0,
                                   tile_bits(num_tiles), p,
@@ -658,5 +667,127 @@ extern "C" int hx_hexels3d_bin_ordered(int P, int num_rendered, int image_width,
             num_rendered, P, keys_out, point_list, depths, (unsigned long long*)keys_sorted);
         HX_LAUNCH_CHECK("full_keys_kernel");
     }
+    return HX_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Several views of one scene binned together (view-major (views, P) arrays).
+// ---------------------------------------------------------------------------
+namespace hx {
+namespace {
+
+// (view << 32) | depth bits of each (view, surfel) entry, and its index.
+__global__ void __launch_bounds__(256) view_depth_keys_kernel(int n, int P_view,
+                                                              const float* __restrict__ depths,
+                                                              unsigned long long* __restrict__ keys,
+                                                              int* __restrict__ ids) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    keys[i] = ((unsigned long long)(i / P_view) << 32) | __float_as_uint(depths[i]);
+    ids[i] = i;
+}
+
+}  // namespace
+}  // namespace hx
+
+extern "C" size_t hx_hexels3d_depth_order_views_workspace_bytes(int views, int P) {
+    const size_t n = (views > 0 && P > 0) ? (size_t)views * P : 1;
+    return 2 * align256(sizeof(unsigned long long) * n) + align256(sizeof(int) * n) +
+           align256(sizeof(int) * n) + hx_scan_workspace_bytes((int)n) +
+           sort_workspace_bytes<unsigned long long>((int)n);
+}
+
+extern "C" int hx_hexels3d_depth_order_views(int views, int P, const float* depths,
+                                             const int32_t* tiles_touched, int32_t* order,
+                                             int32_t* offsets, int64_t* total_out,
+                                             void* workspace, size_t workspace_bytes,
+                                             cudaStream_t stream) {
+    HX_REQUIRE(views >= 1 && P >= 0, "hexels3d_depth_order_views: bad sizes");
+    HX_REQUIRE((long long)views * P <= 0x7fffffffLL,
+               "hexels3d_depth_order_views: views x P overflows int32");
+    const int n = views * P;
+    if (n == 0) {
+        if (total_out) HX_CUDA_TRY(cudaMemsetAsync(total_out, 0, sizeof(int64_t), stream));
+        return HX_OK;
+    }
+    HX_REQUIRE(depths && tiles_touched && order && offsets,
+               "hexels3d_depth_order_views: null pointer");
+    const size_t need = hx_hexels3d_depth_order_views_workspace_bytes(views, P);
+    if (!workspace || workspace_bytes < need)
+        return set_error(HX_ERR_WORKSPACE,
+                         "hexels3d_depth_order_views: workspace of %zu bytes needed", need);
+    char* p = (char*)workspace;
+    unsigned long long* keys = (unsigned long long*)p;
+    p += align256(sizeof(unsigned long long) * (size_t)n);
+    unsigned long long* keys_sorted = (unsigned long long*)p;
+    p += align256(sizeof(unsigned long long) * (size_t)n);
+    int* ids = (int*)p;
+    p += align256(sizeof(int) * (size_t)n);
+    int* counts = (int*)p;
+    p += align256(sizeof(int) * (size_t)n);
+    void* scan_ws = p;
+    const size_t scan_bytes = hx_scan_workspace_bytes(n);
+    p += scan_bytes;
+    view_depth_keys_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(n, P, depths, keys, ids);
+    HX_LAUNCH_CHECK("view_depth_keys_kernel");
+    // per view, depths are >= the near plane (> 0) for every surfel that
+    // touches a tile, so their bit patterns order like the values; the view
+    // in the high bits keeps each view's entries contiguous and in its own
+    // stable depth order
+    int rc = sort_pairs<unsigned long long>(keys, ids, keys_sorted, order, n, 0,
+                                            32 + tile_bits(views), p,
+                                            sort_workspace_bytes<unsigned long long>(n), stream);
+    if (rc != HX_OK) return rc;
+    gather_counts_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(n, order, tiles_touched, counts);
+    HX_LAUNCH_CHECK("gather_counts_kernel");
+    return hx_inclusive_scan_i32(counts, offsets, n, total_out, scan_ws, scan_bytes, stream);
+}
+
+extern "C" size_t hx_hexels3d_bin_views_workspace_bytes(int num_rendered) {
+    return hx_hexels3d_bin_ordered_workspace_bytes(num_rendered);
+}
+
+extern "C" int hx_hexels3d_bin_views(int views, int P, int num_rendered, int image_width,
+                                     int image_height, const float* points_xy_image,
+                                     const int32_t* order, const int32_t* offsets,
+                                     const int32_t* radii, const int32_t* tile_radii,
+                                     int32_t* point_list, int32_t* ranges, void* workspace,
+                                     size_t workspace_bytes, cudaStream_t stream) {
+    HX_REQUIRE(views >= 1 && P >= 0 && num_rendered >= 0, "hexels3d_bin_views: bad sizes");
+    HX_REQUIRE(image_width > 0 && image_height > 0, "invalid image dimensions");
+    HX_REQUIRE((long long)views * P <= 0x7fffffffLL, "hexels3d_bin_views: views x P overflows");
+    const uint2 grid = {(unsigned)ceil_div(image_width, k3BlockX),
+                        (unsigned)ceil_div(image_height, k3BlockY)};
+    const long long all_tiles = (long long)views * grid.x * grid.y;
+    HX_REQUIRE(all_tiles <= 0x7fffffffLL, "hexels3d_bin_views: views x tiles overflows");
+    const int num_tiles = (int)all_tiles;
+    HX_REQUIRE(ranges, "hexels3d_bin_views: null ranges");
+    HX_CUDA_TRY(cudaMemsetAsync(ranges, 0, sizeof(uint2) * (size_t)num_tiles, stream));
+    const int n = views * P;
+    if (n == 0 || num_rendered == 0) return HX_OK;
+    HX_REQUIRE(points_xy_image && order && offsets && radii && tile_radii && point_list,
+               "hexels3d_bin_views: null pointer");
+    const size_t need = hx_hexels3d_bin_views_workspace_bytes(num_rendered);
+    if (!workspace || workspace_bytes < need)
+        return set_error(HX_ERR_WORKSPACE, "hexels3d_bin_views: workspace of %zu bytes needed",
+                         need);
+    char* p = (char*)workspace;
+    unsigned* keys = (unsigned*)p;
+    p += align256(sizeof(unsigned) * (size_t)num_rendered);
+    unsigned* keys_out = (unsigned*)p;
+    p += align256(sizeof(unsigned) * (size_t)num_rendered);
+    int* vals = (int*)p;
+    p += align256(sizeof(int) * (size_t)num_rendered);
+    emit3d_ordered_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(
+        n, num_rendered, order, (const float2*)points_xy_image, offsets, radii,
+        (const int2*)tile_radii, grid, keys, vals, P);
+    HX_LAUNCH_CHECK("emit3d_ordered_kernel");
+    int rc = sort_pairs<uint32_t>(keys, vals, keys_out, point_list, num_rendered, 0,
+                                  tile_bits(num_tiles), p,
+                                  sort_workspace_bytes<uint32_t>(num_rendered), stream);
+    if (rc != HX_OK) return rc;
+    ranges3d_u32_kernel<<<ceil_div(num_rendered, 256), 256, 0, stream>>>(
+        num_rendered, num_tiles, keys_out, (uint2*)ranges);
+    HX_LAUNCH_CHECK("ranges3d_u32_kernel");
     return HX_OK;
 }

@@ -262,6 +262,98 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                 blend_mask=blend_mask, records=rec)
 
 
+def _forward_views_core(means3d, scales, rotations, colors, color_grads, view_grads, opacities,
+                        cams, background, softness, color_model=1, view_model=1,
+                        use_view_grads=True):
+    """The RGB forward of a group of views of one scene (the training path:
+    flat or linear colour, no or linear view model, one softness), binned
+    together: one preprocess per view into view-major (V, P) buffers, one
+    depth order and one binning of all the views' intersections
+    (hx_hexels3d_depth_order_views / hx_hexels3d_bin_views, one 8-byte
+    read-back for the group), then per view the staged records and the
+    compositing.  Each view's lists are the ones _forward_core gives it.
+    Returns one dict per view with out_color, radii, saved (the eleven
+    buffers _backward_core takes: that view's slices, its ranges as offsets
+    into the group's point_list), blend_mask (the group's, shared) and
+    records."""
+    e = _empty(means3d)
+    V = len(cams)
+    _check(V >= 1, "at least one view")
+    _check(int(color_model) in (0, 1) and int(view_model) in (0, 1),
+           "grouped views take the flat/linear colour and no/linear view models")
+    W, H = int(cams[0].width), int(cams[0].height)
+    _check(all(int(c.width) == W and int(c.height) == H for c in cams),
+           "grouped views share one image size")
+    P, stride = _checks(means3d, scales, rotations, colors, color_grads, e, view_grads, e, e,
+                        opacities, e, cams[0].viewmatrix, cams[0].projmatrix, cams[0].campos,
+                        background, W, H, float(softness), int(color_model), int(view_model),
+                        bool(use_view_grads))
+    dev = means3d.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    radii = torch.empty((V, P), **i32)
+    tile_radii = torch.empty((V, P, 2), **i32)
+    xy = torch.empty((V, P, 2), **f32)
+    depths = torch.empty((V, P), **f32)
+    transMats = torch.empty((V, P, 9), **f32)
+    touched = torch.empty((V, P), **i32)
+    op_out = torch.empty((V, P), **f32)
+    soft_out = torch.empty((V, P), **f32)
+    view_dirs = torch.empty((V, P, 3), **f32)
+    tx, ty = (W + 15) // 16, (H + 15) // 16
+    T = tx * ty
+    outs = []
+    with torch.cuda.device(dev):
+        st = stream(dev)
+        for v, cam in enumerate(cams):
+            lib.call("hx_hexels3d_preprocess", P, ptr(means3d), ptr(scales), 1.0, ptr(rotations),
+                     ptr(opacities), None, float(softness), stride, ptr(cam.viewmatrix),
+                     ptr(cam.projmatrix), ptr(cam.campos), W, H, 0, 0, ptr(radii[v]),
+                     ptr(tile_radii[v]), ptr(xy[v]), None, ptr(depths[v]), ptr(transMats[v]),
+                     ptr(touched[v]), ptr(op_out[v]), ptr(soft_out[v]), ptr(view_dirs[v]), None,
+                     st)
+        order = torch.empty((V * P,), **i32)
+        offsets = torch.empty((V * P,), **i32)
+        total = torch.empty((1,), dtype=torch.int64, device=dev)
+        ws = workspace(lib.query("hx_hexels3d_depth_order_views_workspace_bytes", V, P), dev)
+        lib.call("hx_hexels3d_depth_order_views", V, P, ptr(depths), ptr(touched), ptr(order),
+                 ptr(offsets), ptr(total), ptr(ws), ws.numel(), st)
+        n = int(total.item()) if P > 0 else 0
+        _check(n <= 2**31 - 1, "number of rendered intersections overflows int32")
+        ranges = torch.empty((V, T, 2), **i32)
+        point_list = torch.empty((n,), **i32)
+        ws = workspace(lib.query("hx_hexels3d_bin_views_workspace_bytes", n), dev)
+        lib.call("hx_hexels3d_bin_views", V, P, n, W, H, ptr(xy), ptr(order), ptr(offsets),
+                 ptr(radii), ptr(tile_radii), ptr(point_list), ptr(ranges), ptr(ws), ws.numel(),
+                 st)
+        blend_mask = torch.empty((max(n, 1),), dtype=torch.uint8, device=dev)
+        rec = torch.empty((V, P, 32), **f32) if n > 0 else None
+        for v, cam in enumerate(cams):
+            if rec is not None:
+                lib.call("hx_hexels3d_surfel_records", P, W, H, ptr(transMats[v]), ptr(op_out[v]),
+                         ptr(soft_out[v]), stride, ptr(colors),
+                         ptr(color_grads) if color_model >= 1 else None,
+                         ptr(view_grads) if use_view_grads else None, ptr(view_dirs[v]), None,
+                         None, int(color_model), int(bool(use_view_grads)), 0, ptr(rec[v]), st)
+            out_color = torch.empty((kNumChannels, H, W), **f32)
+            final_T = torch.empty((H, W), **f32)
+            last_index = torch.empty((H, W), **i32)
+            lib.call("hx_hexels3d_render_forward", P, n, ptr(ranges[v]), ptr(point_list), None,
+                     W, H, ptr(colors), ptr(color_grads) if color_model >= 1 else None, None,
+                     ptr(view_grads) if use_view_grads else None, None, None, ptr(view_dirs[v]),
+                     ptr(transMats[v]), ptr(op_out[v]), ptr(soft_out[v]), stride,
+                     ptr(background), None, -1, int(color_model), int(view_model),
+                     int(bool(use_view_grads)), 0, ptr(out_color), None, None, None, None, None,
+                     None, *(None,) * 6, ptr(final_T), ptr(last_index), *(None,) * 5, None,
+                     ptr(blend_mask), ptr(rec[v]) if rec is not None else None, st)
+            saved = [radii[v], transMats[v], op_out[v], soft_out[v], view_dirs[v], _empty(xy),
+                     _empty(xy), ranges[v], point_list, final_T, last_index]
+            outs.append(dict(out_color=out_color, radii=radii[v], saved=saved,
+                             blend_mask=blend_mask,
+                             records=rec[v] if rec is not None else None, num_rendered=n))
+    return outs
+
+
 def _backward_core(means3d, means2d, scales, rotations, colors, color_grads, color_quads,
                    view_grads, specular_ks, specular_log_s, opacities, softnesses, viewmatrix,
                    projmatrix, campos, background, grad_out_color, grad_out_overdraw,

@@ -44,17 +44,21 @@ def fit_step_views(params: Sequence[torch.Tensor], cams: Sequence, targets: Sequ
                    background: torch.Tensor, softness: float, grads: Sequence[torch.Tensor],
                    loss: torch.Tensor, pipeline: Optional[ViewPipeline] = None, *,
                    color_model: int = 1, view_model: int = 1,
-                   use_view_grads: bool = True) -> None:
+                   use_view_grads: bool = True, group: int = 1) -> None:
     """Forward, loss and backward of every view in `cams` (objects with
     viewmatrix, projmatrix, campos, width, height, tan_fovx, tan_fovy), the
     gradients of `params` (means3d, scales, rotations, colors, color_grads,
     view_grads, opacities) ADDED into `grads` (same order and shapes) and the
     summed per-view colour losses ADDED into `loss` (one element).  With a
     `pipeline` of several streams the views run overlapped; without one they
-    run in order on the current stream.  Each view's intermediate tensors are
-    made and used on one stream only, so the caching allocator reuses them in
-    that stream's order; the accumulators are the caller's and the current
-    stream waits for every view before this returns."""
+    run in order on the current stream.  With `group` > 1 the views are taken
+    `group` at a time and each group is binned together
+    (_C._forward_views_core: one depth order, one binning and one read-back
+    of the intersection count per group instead of per view); the groups are
+    dealt to the streams.  Each view's intermediate tensors are made and used
+    on one stream only, so the caching allocator reuses them in that
+    stream's order; the accumulators are the caller's and the current stream
+    waits for every view before this returns."""
     from gsplat.cuda_hexels3d import _C
     from gsplat.loss import l2_loss_grad
 
@@ -72,7 +76,30 @@ def fit_step_views(params: Sequence[torch.Tensor], cams: Sequence, targets: Sequ
                 t.zero_()
         for s in streams:
             s.wait_stream(main)
-    for i, (cam, tgt) in enumerate(zip(cams, targets)):
+    if group < 1:
+        raise ValueError("group must be >= 1")
+    if group > 1:
+        for gi, g0 in enumerate(range(0, len(cams), group)):
+            k = gi % len(streams)
+            acc = dict(zip(PARAM_NAMES, grads))
+            if k > 0:
+                acc.update(zip(PARAM_NAMES[:3], pipeline.geo[k - 1]))
+            with torch.cuda.stream(streams[k]):
+                outs = _C._forward_views_core(m3, sc, rot, col, cg, vg, op, cams[g0:g0 + group],
+                                              background, softness, color_model, view_model,
+                                              use_view_grads)
+                for o, cam, tgt in zip(outs, cams[g0:g0 + group], targets[g0:g0 + group]):
+                    _, g_color = l2_loss_grad(o["out_color"], tgt, loss=loss)
+                    _C._backward_core(m3, e, sc, rot, col, cg, e, vg, e, e, op, e,
+                                      cam.viewmatrix, cam.projmatrix, cam.campos, background,
+                                      g_color, e, e, e, e, cam.width, cam.height, cam.tan_fovx,
+                                      cam.tan_fovy, softness, 1.0, color_model, view_model,
+                                      use_view_grads, -1, False, False, False, o["saved"],
+                                      accumulate_into=acc, blend_mask=o["blend_mask"],
+                                      records=o["records"])
+                    del g_color
+                del outs
+    for i, (cam, tgt) in enumerate(zip(cams, targets) if group == 1 else ()):
         k = i % len(streams)
         acc = dict(zip(PARAM_NAMES, grads))
         if k > 0:

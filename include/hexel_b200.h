@@ -297,6 +297,34 @@ HX_API int hx_hexels3d_bin_ordered(int P, int num_rendered, int image_width, int
                                    int64_t* keys_sorted, int32_t* point_list, int32_t* ranges,
                                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* Depth order and binning of a group of V views of one scene at once (no
+ * reference counterpart: the reference bins one view per call,
+ * hexels3d_forward.cu:2972-3043).  Inputs are the preprocess outputs of the
+ * V views stacked view-major ((V, P) arrays).  depth_order_views sorts all
+ * V x P entries by (view, depth bits), stable, so each view's entries are
+ * contiguous and in that view's own depth order; order holds
+ * view * P + surfel; offsets and total_out are the inclusive prefix sum of
+ * the tile counts in that order over all views (one read-back per group).
+ * bin_views then emits key view * tiles + tile for every tile of each entry's
+ * rectangle with the surfel index within its view as value, sorts stably
+ * and writes ranges (V, tiles, 2) as offsets into the group's point_list:
+ * view v's lists are exactly those hx_hexels3d_bin_ordered gives for v
+ * alone, shifted by the entries of views 0..v-1, so the compositing calls of
+ * view v take ranges + 2 * v * tiles, the whole point_list and its total as
+ * num_rendered. */
+HX_API size_t hx_hexels3d_depth_order_views_workspace_bytes(int views, int P);
+HX_API int hx_hexels3d_depth_order_views(int views, int P, const float* depths,
+                                         const int32_t* tiles_touched, int32_t* order,
+                                         int32_t* offsets, int64_t* total_out, void* workspace,
+                                         size_t workspace_bytes, cudaStream_t stream);
+HX_API size_t hx_hexels3d_bin_views_workspace_bytes(int num_rendered);
+HX_API int hx_hexels3d_bin_views(int views, int P, int num_rendered, int image_width,
+                                 int image_height, const float* points_xy_image,
+                                 const int32_t* order, const int32_t* offsets,
+                                 const int32_t* radii, const int32_t* tile_radii,
+                                 int32_t* point_list, int32_t* ranges, void* workspace,
+                                 size_t workspace_bytes, cudaStream_t stream);
+
 /* Intersection emission, stable sort and tile ranges; replaces
  * duplicate_with_keys + cub::DeviceRadixSort::SortPairs + identify_tile_ranges
  * (hexels3d_forward.cu:553-604, 2990-3043).  offsets = inclusive scan of

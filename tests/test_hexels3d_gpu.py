@@ -514,3 +514,73 @@ def test_pipelined_views_equal_sequential(streams):
         assert abs(float(got_l) - float(want_l)) <= 1e-5 * abs(float(want_l))
         for name, a, b in zip(multiview.PARAM_NAMES, got_g, want_g):
             assert_grad_parity(a, b, None, name)
+
+
+@pytest.mark.parametrize("views,size", [(5, "tiny"), (3, "full")])
+def test_grouped_views_binning_equals_per_view(views, size):
+    """_C._forward_views_core (views binned together: one depth order, one
+    binning) gives each view the lists, image and saved state of that view
+    run alone through _forward_core: ranges shifted by the entries of the
+    views before it, identical point lists, bit-identical images, last
+    indices and transforms.  Tiny ragged scene and three orbit views of the
+    1M-surfel 1080p scene."""
+    import workloads
+    from gsplat.cuda_hexels3d import _C
+
+    w = (workloads.hexels3d_tiny(12, 2000, 96, 80, views, 0.06) if size == "tiny"
+         else workloads.hexels3d_multiview(64)).to("cuda")
+    cams = w.cameras[:views] if size == "tiny" else [w.cameras[v] for v in (0, 21, 42)]
+    e = torch.empty(0, device="cuda")
+    args = (w.means3d, w.scales, w.rotations, w.colors, w.color_grads, w.view_grads,
+            w.opacities)
+    outs = _C._forward_views_core(*args, cams, w.background, w.softness)
+    base = 0
+    for o, cam in zip(outs, cams):
+        one = _C._forward_core(w.means3d, w.scales, w.rotations, w.colors, w.color_grads, e,
+                               w.view_grads, e, e, w.opacities, e, cam.viewmatrix,
+                               cam.projmatrix, cam.campos, w.background, cam.width, cam.height,
+                               cam.tan_fovx, cam.tan_fovy, w.softness, 1.0, 1, 1, True, False,
+                               False, False, save=True)
+        n = one["num_rendered"]
+        r_one = one["saved"][7].to(torch.int64)
+        r_grp = o["saved"][7].to(torch.int64)
+        nonempty = r_one[:, 1] > r_one[:, 0]
+        assert torch.equal(r_grp[nonempty] - base, r_one[nonempty])
+        assert bool((r_grp[~nonempty, 1] == r_grp[~nonempty, 0]).all())
+        assert torch.equal(o["saved"][8][base:base + n], one["saved"][8])
+        assert torch.equal(o["out_color"], one["out_color"])
+        for k in (0, 1, 2, 3, 4, 9, 10):  # radii, transforms, opacity, softness, dirs, T, last
+            assert torch.equal(o["saved"][k], one["saved"][k]), k
+        base += n
+    assert base == outs[0]["saved"][8].numel()
+
+
+def test_grouped_views_step_equals_per_view():
+    """multiview.fit_step_views with the views binned in groups gives the
+    gradients and loss of the per-view step (to the order of the float
+    atomics), over one and two streams."""
+    import multiview
+    import workloads
+
+    w = workloads.hexels3d_tiny(13, 2000, 96, 80, 7, 0.06).to("cuda")
+    params = [w.means3d, w.scales, w.rotations, w.colors, w.color_grads, w.view_grads,
+              w.opacities]
+    g = torch.Generator().manual_seed(6)
+    cams = w.cameras
+    targets = [torch.rand((3, c.height, c.width), generator=g).cuda() for c in cams]
+
+    def step(pipe, group):
+        grads = [torch.zeros_like(p) for p in params]
+        loss = torch.zeros(1, device="cuda")
+        multiview.fit_step_views(params, cams, targets, w.background, w.softness, grads, loss,
+                                 pipe, group=group)
+        torch.cuda.synchronize()
+        return grads, loss
+
+    want_g, want_l = step(None, 1)
+    for pipe, group in ((None, 3), (multiview.ViewPipeline(params, streams=2), 3),
+                        (multiview.ViewPipeline(params, streams=2), 7)):
+        got_g, got_l = step(pipe, group)
+        assert abs(float(got_l) - float(want_l)) <= 1e-5 * abs(float(want_l))
+        for name, a, b in zip(multiview.PARAM_NAMES, got_g, want_g):
+            assert_grad_parity(a, b, None, name)

@@ -987,6 +987,7 @@ def run_ours_3d(args, world, rank, local):
             "outputs": "rgb + depth + alpha + normal + distortion" if surface else "rgb",
             "color_model": "linear", "view_model": "linear",
             "intersections_per_view": round(rendered_rank / max(1, len(step.views))),
+            "view_group": step.group,
             "parallelism": (f"views dealt over {world} GPUs by the device time each took in "
                             "the second warm-up step (longest first to the least-loaded rank), "
                             "surfels replicated, gradients NCCL all-reduced")
@@ -994,8 +995,9 @@ def run_ours_3d(args, world, rank, local):
             "l2": "flushed between timed steps (256 MB write)",
         },
         "stages_ms": {k: round(v, 4) for k, v in stage_ms.items()},
-        "stages_note": ("one step with CUDA events between stages, views in order on one "
-                        "stream; the timed steps pipeline the views over two streams"
+        "stages_note": ("one step with CUDA events between stages, views one at a time in "
+                        "order on one stream; the timed steps bin the views in groups and "
+                        "pipeline the groups over two streams"
                         if step.pipeline is not None else
                         "CUDA events between stages of the timed steps"),
         "roofline": roofline_3d(step, stage_ms),
@@ -1154,8 +1156,9 @@ def run_e2e_3d_pipelined(w, args, world, rank, views, group=1):
             "unit": UNIT, "ms_per_step": round(ms, 4), "steps": steps,
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
             "breakdown_ms_one_step": {k: round(v, 3) for k, v in parts.items()},
-            "path": "multiview.fit_step_views (this rank's views pipelined over two streams, "
-                    "gradients into one flat buffer, NCCL all-reduce in place) per step; the "
+            "path": f"multiview.fit_step_views (this rank's views binned {group} at a time, the "
+                    "groups pipelined over two streams, gradients into one flat buffer, NCCL "
+                    "all-reduce in place) per step; the "
                     "surfel parameters and the rank's target images copied from pinned host "
                     "memory every step on a copy stream, double-buffered (step s + 1's inputs "
                     "upload while step s runs); the loss read back every step"}
@@ -1542,7 +1545,7 @@ def main():
     ap.add_argument("--views", type=int, default=64,
                     help="views of the multi-view orbit (64 is the benchmark configuration; "
                          "fewer, e.g. 1, for a small profiling case)")
-    ap.add_argument("--group", type=int, default=1,
+    ap.add_argument("--group", type=int, default=8,
                     help="multi-view step: views binned together per group (1 = per view)")
     ap.add_argument("--cpu-crop-tiles", type=int, default=16)
     ap.add_argument("--cpu-crop-tiles-3d", type=int, default=8)

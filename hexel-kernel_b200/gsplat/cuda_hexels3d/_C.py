@@ -128,11 +128,13 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                   conservative_bounds, debug, *, return_contrib=False, return_overdraw=False,
                   return_overdraw_hits=False, return_surface=False, overdraw_base_count=-1,
                   owner=False, return_median_depth=False, save=False, save_surface=False,
-                  count_contrib=False, records=True):
+                  count_contrib=False, records=True, render=True):
     """rasterize_hexels3d_forward_impl (hexels3d_forward.cu:2679-3481).
     With `records` the per-surfel staged records are written once after the
     preprocess (hx_hexels3d_surfel_records) and the compositing stages them
-    with asynchronous copies; they are returned for the backward."""
+    with asynchronous copies; they are returned for the backward.  With
+    `render` False it stops after the binning and returns the preprocess
+    and binning buffers under "binning"."""
     W, H = int(image_width), int(image_height)
     P, stride = _checks(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
                         specular_ks, specular_log_s, opacities, softnesses, viewmatrix,
@@ -184,6 +186,12 @@ def _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, 
                  ptr(values_sorted), ptr(ranges), ptr(ws), ws.numel(), s)
 
         _mark("bin")
+        if not render:
+            return dict(num_rendered=num_rendered, normals=normals, radii=radii,
+                        binning=dict(ranges=ranges, point_list=values_sorted,
+                                     transMats=transMats, opacities=opacities_out,
+                                     softnesses=softnesses_out, view_dirs=view_dirs,
+                                     depths=depths))
         # the compositing kernel writes every pixel of these outputs
         out_color = torch.empty((kNumChannels, H, W), **f32)
         contrib = torch.zeros((P,), **f32) if return_contrib else torch.empty((0,), **f32)
@@ -610,18 +618,116 @@ def rasterize_hexels3d_backward(*args):
                           blend_mask=o["blend_mask"], records=o["records"])
 
 
-def _not_provided(name: str):
-    def fn(*args, **kwargs):
-        raise NotImplementedError(
-            f"{name} is a diagnostic exact-sort replay of the reference, off the render and "
-            "training path; it is not provided by the B200 build.")
+def _exact_core(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
+                specular_ks, specular_log_s, opacities, softnesses, viewmatrix, projmatrix,
+                campos, background, native_image, selected_mask, pixel_mask, W, H, softness,
+                scale_modifier, color_model, view_model, use_view_grads, exact_mode, crop,
+                compute_risk, debug):
+    """rasterize_hexels3d_exact_sort_forward_impl (hexels3d_forward.cu:4217-4721):
+    preprocess and binning as the forward, then each enabled crop pixel's
+    hits re-sorted by depth and composited in that order."""
+    W, H = int(W), int(H)
+    P, stride = _checks(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
+                        specular_ks, specular_log_s, opacities, softnesses, viewmatrix,
+                        projmatrix, campos, background, W, H, float(softness), int(color_model),
+                        int(view_model), bool(use_view_grads))
+    for t, n in ((native_image, "native_image"), (selected_mask, "selected_mask"),
+                 (pixel_mask, "pixel_mask")):
+        check_input(t, n)
+    dev = means3d.device
+    for t in (native_image, selected_mask, pixel_mask):
+        _check(t.device == dev, "all exact-sort tensors must be on the same CUDA device")
+    _check(selected_mask.dtype == torch.bool, "selected_mask must be bool")
+    _check(pixel_mask.dtype == torch.bool, "pixel_mask must be bool")
+    mode = int(exact_mode)
+    if mode == 5:
+        _check(selected_mask.numel() == 0, "selected_mask must be empty in pixel-mask mode")
+        _check(tuple(pixel_mask.shape) == (H, W), "pixel_mask must have shape (H,W)")
+    else:
+        _check(selected_mask.ndimension() == 1 and selected_mask.numel() == P,
+               "selected_mask must have shape (P,)")
+        _check(pixel_mask.numel() == 0, "pixel_mask must be empty outside pixel-mask mode")
+    _check(tuple(native_image.shape) == (3, H, W) and native_image.dtype == torch.float32,
+           "native_image must have shape (3,H,W)")
+    _check(W * H <= 2**32 - 1, "image has too many pixels for exact-sort keys")
+    _check(0 <= mode <= 5, "invalid exact sort mode")
+    x0, y0, x1, y1 = (int(c) for c in crop)
+    _check(0 <= x0 < x1 <= W and 0 <= y0 < y1 <= H,
+           "crop must satisfy 0 <= x0 < x1 <= W and 0 <= y0 < y1 <= H")
+    e = _empty(means3d)
+    o = _forward_core(means3d, scales, rotations, colors, color_grads, color_quads, view_grads,
+                      specular_ks, specular_log_s, opacities, softnesses, viewmatrix, projmatrix,
+                      campos, background, W, H, 1.0, 1.0, softness, scale_modifier, color_model,
+                      view_model, use_view_grads, False, False, False, records=False,
+                      render=False)
+    b = o["binning"]
+    n = o["num_rendered"]
+    i32 = dict(dtype=torch.int32, device=dev)
+    out_color = native_image.clone()
+    order_changed = torch.zeros((H, W), dtype=torch.bool, device=dev)
+    hit_counts = torch.zeros((H, W), **i32)
+    enabled = torch.zeros((H, W), dtype=torch.bool, device=dev)
+    risk = torch.zeros((H, W), dtype=torch.float32, device=dev)
+    record_counts = torch.zeros((H * W,), **i32)
+    cm, vm, uvg = int(color_model), int(view_model), bool(use_view_grads)
+    common = (P, n, ptr(b["ranges"]), ptr(b["point_list"]) if n > 0 else None, W, H,
+              ptr(colors), ptr(color_grads) if cm >= 1 else None,
+              ptr(color_quads) if cm >= 2 else None, ptr(view_grads) if uvg else None,
+              ptr(specular_ks) if vm == 2 else None, ptr(specular_log_s) if vm == 2 else None,
+              ptr(b["view_dirs"]), ptr(o["normals"]) if vm == 2 else None, ptr(b["transMats"]),
+              ptr(b["opacities"]), ptr(b["softnesses"]), stride, ptr(background),
+              ptr(b["depths"]), ptr(selected_mask) if selected_mask.numel() else None,
+              ptr(pixel_mask) if pixel_mask.numel() else None, cm, vm, int(uvg), mode, x0, y0,
+              x1, y1)
+    with torch.cuda.device(dev):
+        st = stream(dev)
+        lib.call("hx_hexels3d_exact_count", *common, ptr(hit_counts), ptr(record_counts),
+                 ptr(enabled), ptr(risk) if compute_risk else None, st)
+        offsets = torch.empty((H * W,), **i32)
+        total = torch.empty((1,), dtype=torch.int64, device=dev)
+        ws = workspace(lib.query("hx_scan_workspace_bytes", H * W), dev)
+        lib.call("hx_inclusive_scan_i32", ptr(record_counts), ptr(offsets), H * W, ptr(total),
+                 ptr(ws), ws.numel(), st)
+        num_records = int(total.item())
+        _check(num_records <= 2**31 - 1,
+               "exact-sort crop has too many hit records; use smaller crop strips")
+        ws = workspace(lib.query("hx_hexels3d_exact_resolve_workspace_bytes", num_records), dev)
+        lib.call("hx_hexels3d_exact_resolve", *common, ptr(enabled), ptr(record_counts),
+                 ptr(offsets), num_records, ptr(out_color), ptr(order_changed), ptr(ws),
+                 ws.numel(), st)
+        if debug:
+            torch.cuda.synchronize(dev)
+    return out_color, order_changed, hit_counts, enabled, risk
 
-    fn.__name__ = name
-    return fn
+
+def rasterize_hexels3d_exact_sort_forward(*args):
+    """(out_color, order_changed, hit_counts, enabled_mask): the enabled crop
+    pixels of native_image recomposited with their hits sorted by depth at
+    the pixel (hexels3d_forward.cu:4722-4791)."""
+    if len(args) != 30:
+        raise TypeError("rasterize_hexels3d_exact_sort_forward takes 30 arguments")
+    (m3, sc, rot, col, cg, cq, vg, ks, ls, op, soft, vm_, pm, cp, bg, native, selected, W, H,
+     softness, mod, cm, vm, uvg, mode, x0, y0, x1, y1, dbg) = args
+    pixel_mask = torch.empty((0,), dtype=torch.bool, device=selected.device)
+    out = _exact_core(m3, sc, rot, col, cg, cq, vg, ks, ls, op, soft, vm_, pm, cp, bg, native,
+                      selected, pixel_mask, W, H, softness, mod, cm, vm, uvg, mode,
+                      (x0, y0, x1, y1), False, dbg)
+    return out[0], out[1], out[2], out[3]
 
 
-rasterize_hexels3d_exact_sort_forward = _not_provided("rasterize_hexels3d_exact_sort_forward")
-rasterize_hexels3d_pixel_risk_forward = _not_provided("rasterize_hexels3d_pixel_risk_forward")
+def rasterize_hexels3d_pixel_risk_forward(*args):
+    """(out_color, risk_map, order_changed, hit_counts, enabled_mask): the
+    pixel-mask exact sort plus the inversion risk of the list order over the
+    crop (hexels3d_forward.cu:4793-4880)."""
+    if len(args) != 29:
+        raise TypeError("rasterize_hexels3d_pixel_risk_forward takes 29 arguments")
+    (m3, sc, rot, col, cg, cq, vg, ks, ls, op, soft, vm_, pm, cp, bg, native, pixel_mask, W, H,
+     softness, mod, cm, vm, uvg, x0, y0, x1, y1, dbg) = args
+    selected = torch.empty((0,), dtype=torch.bool, device=pixel_mask.device)
+    out = _exact_core(m3, sc, rot, col, cg, cq, vg, ks, ls, op, soft, vm_, pm, cp, bg, native,
+                      selected, pixel_mask, W, H, softness, mod, cm, vm, uvg, 5,
+                      (x0, y0, x1, y1), True, dbg)
+    return out[0], out[4], out[1], out[2], out[3]
 
 
 def _sig(name, n_tensor, n_total, returns):

@@ -12,7 +12,7 @@ traffic differ.
 
 from __future__ import annotations
 
-from typing import Literal, Tuple
+from typing import Optional, Literal, Tuple
 
 import torch
 from torch import Tensor
@@ -168,17 +168,86 @@ rasterize_hexels3d_forward_with_contrib_overdraw_hits = _forward_variant(
     "rasterize_hexels3d_forward_with_contrib_overdraw_hits", True)
 
 
-def rasterize_hexels3d_exact_sort_forward(*args, **kwargs):
-    """Diagnostic per-pixel exact depth re-sort of the reference (a tool for
-    measuring tile-sort order inversions, off the render and training path);
-    not provided by the B200 build."""
-    return _C().rasterize_hexels3d_exact_sort_forward(*args, **kwargs)
+_EXACT_SORT_MODE_TO_INT = {"center_replay": 0, "hybrid": 1, "selected_all": 2, "crop_all": 3,
+                          "boundary_tail": 4}
 
 
-def rasterize_hexels3d_pixel_risk_forward(*args, **kwargs):
-    """Diagnostic sort-inversion risk map of the reference; not provided by the
-    B200 build."""
-    return _C().rasterize_hexels3d_pixel_risk_forward(*args, **kwargs)
+def _exact_inputs(means3d, color_grads, color_quads, view_grads, specular_ks, specular_log_s,
+                  softnesses, color_model, view_model, use_view_grads, crop_xyxy, W, H,
+                  prefilter_edge_on, what):
+    if prefilter_edge_on:
+        raise ValueError(f"The {what} oracle does not support prefilter_edge_on=True")
+    if crop_xyxy is None:
+        crop_xyxy = (0, 0, int(W), int(H))
+    if len(crop_xyxy) != 4:
+        raise ValueError("crop_xyxy must contain (x0, y0, x1, y1)")
+    return _prepare(means3d, color_grads, color_quads, view_grads, specular_ks, specular_log_s,
+                    softnesses, color_model, view_model, use_view_grads), tuple(crop_xyxy)
+
+
+def rasterize_hexels3d_exact_sort_forward(means3d: Tensor, scales: Tensor, rotations: Tensor,
+                                          colors: Tensor, color_grads: Tensor, view_grads: Tensor,
+                                          opacities: Tensor, viewmatrix: Tensor,
+                                          projmatrix: Tensor, campos: Tensor, background: Tensor,
+                                          native_image: Tensor, selected_mask: Tensor,
+                                          image_width: int, image_height: int, softness: float,
+                                          softnesses: Optional[Tensor] = None, *,
+                                          color_quads: Optional[Tensor] = None,
+                                          specular_ks: Optional[Tensor] = None,
+                                          specular_log_s: Optional[Tensor] = None,
+                                          scale_modifier: float = 1.0, color_model="linear",
+                                          view_model="linear", use_view_grads: bool = True,
+                                          mode: str = "center_replay", crop_xyxy=None,
+                                          prefilter_edge_on: bool = False, debug: bool = False):
+    """Diagnostic replay of a crop with each enabled pixel's hits re-sorted
+    by the depth at the pixel (reference gsplat/rasterize_hexels3d.py:750-852):
+    returns (image, order_changed, hit_counts, enabled_mask); pixels outside
+    the crop or not enabled keep native_image.  selected_mask (P,) bool marks
+    the surfels whose pixels are replayed in the hybrid and selected modes."""
+    if mode not in _EXACT_SORT_MODE_TO_INT:
+        raise ValueError(f"Unknown exact-sort mode: {mode}")
+    (cm, vm, uvg, cg, cq, vg, ks, ls, soft), crop = _exact_inputs(
+        means3d, color_grads, color_quads, view_grads, specular_ks, specular_log_s, softnesses,
+        color_model, view_model, use_view_grads, crop_xyxy, image_width, image_height,
+        prefilter_edge_on, "exact-sort")
+    return _C().rasterize_hexels3d_exact_sort_forward(
+        means3d.contiguous(), scales.contiguous(), rotations.contiguous(), colors.contiguous(),
+        cg, cq, vg, ks, ls, opacities.contiguous(), soft, viewmatrix.contiguous(),
+        projmatrix.contiguous(), campos.contiguous(), background.contiguous(),
+        native_image.contiguous(), selected_mask.contiguous(), int(image_width),
+        int(image_height), float(softness), float(scale_modifier), cm, vm, uvg,
+        _EXACT_SORT_MODE_TO_INT[mode], *(int(c) for c in crop), bool(debug))
+
+
+def rasterize_hexels3d_pixel_risk_forward(means3d: Tensor, scales: Tensor, rotations: Tensor,
+                                          colors: Tensor, color_grads: Tensor, view_grads: Tensor,
+                                          opacities: Tensor, viewmatrix: Tensor,
+                                          projmatrix: Tensor, campos: Tensor, background: Tensor,
+                                          native_image: Tensor, pixel_mask: Tensor,
+                                          image_width: int, image_height: int, softness: float,
+                                          softnesses: Optional[Tensor] = None, *,
+                                          color_quads: Optional[Tensor] = None,
+                                          specular_ks: Optional[Tensor] = None,
+                                          specular_log_s: Optional[Tensor] = None,
+                                          scale_modifier: float = 1.0, color_model="linear",
+                                          view_model="linear", use_view_grads: bool = True,
+                                          crop_xyxy=None, prefilter_edge_on: bool = False,
+                                          debug: bool = False):
+    """Diagnostic inversion-risk map of the compositing order over a crop,
+    plus the exact depth re-sort of the pixels in pixel_mask (H,W) bool
+    (reference gsplat/rasterize_hexels3d.py:854-955): returns (image, risk,
+    order_changed, hit_counts, enabled_mask)."""
+    (cm, vm, uvg, cg, cq, vg, ks, ls, soft), crop = _exact_inputs(
+        means3d, color_grads, color_quads, view_grads, specular_ks, specular_log_s, softnesses,
+        color_model, view_model, use_view_grads, crop_xyxy, image_width, image_height,
+        prefilter_edge_on, "pixel-risk")
+    return _C().rasterize_hexels3d_pixel_risk_forward(
+        means3d.contiguous(), scales.contiguous(), rotations.contiguous(), colors.contiguous(),
+        cg, cq, vg, ks, ls, opacities.contiguous(), soft, viewmatrix.contiguous(),
+        projmatrix.contiguous(), campos.contiguous(), background.contiguous(),
+        native_image.contiguous(), pixel_mask.contiguous(), int(image_width),
+        int(image_height), float(softness), float(scale_modifier), cm, vm, uvg,
+        *(int(c) for c in crop), bool(debug))
 
 
 # ---------------------------------------------------------------------------

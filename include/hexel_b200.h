@@ -374,6 +374,48 @@ HX_API int hx_hexels3d_render_forward(
     float* m2_surf, int32_t* median_index, int32_t* contrib_count, uint8_t* blend_mask,
     const void* records, cudaStream_t stream);
 
+/* Exact-sort and pixel-risk diagnostics; together with the library's
+ * preprocess and binning they replace rasterize_hexels3d_exact_sort_forward
+ * and rasterize_hexels3d_pixel_risk_forward (hexels3d_forward.cu:4217-4880)
+ * and their kernels (1069-1747).  Shared arguments: the binned view (P,
+ * num_rendered, ranges, point_list), the per-surfel arrays of the
+ * compositing (colors ... softnesses; normals for the lobe view model),
+ * background (3), center_depths (P; the preprocess depths), selected_mask (P
+ * uint8, may be NULL), pixel_mask (H x W uint8, exact_mode 5 only), the
+ * colour and view models, exact_mode 0..5 (centre replay, hybrid, selected
+ * all, crop all, boundary tail, pixel mask) and the crop [x0,x1) x [y0,y1).
+ * exact_count: per crop pixel the number of hits (alpha >= 1/255),
+ * record_counts (the hits of enabled pixels, else 0) and enabled; with
+ * risk_map (H x W float, may be NULL) also the inversion risk of the list
+ * order.  The caller scans record_counts (inclusive, record_offsets) and
+ * calls exact_resolve with the total: it sorts each enabled pixel's hit
+ * records by (pixel, depth at the pixel or centre depth, per mode) stably,
+ * writes order_changed (H x W uint8) and the colour composited in that
+ * order into out_color (3 x H x W; other pixels untouched). */
+HX_API int hx_hexels3d_exact_count(
+    int P, int num_rendered, const int32_t* ranges, const int32_t* point_list, int image_width,
+    int image_height, const float* colors, const float* color_grads, const float* color_quads,
+    const float* view_grads, const float* specular_ks, const float* specular_log_s,
+    const float* view_dirs, const float* normals, const float* transMats,
+    const float* opacities, const float* softnesses, int softness_stride,
+    const float* background, const float* center_depths, const uint8_t* selected_mask,
+    const uint8_t* pixel_mask, int color_model, int view_model, int use_view_grads,
+    int exact_mode, int crop_x0, int crop_y0, int crop_x1, int crop_y1, int32_t* hit_counts,
+    int32_t* record_counts, uint8_t* enabled, float* risk_map, cudaStream_t stream);
+HX_API size_t hx_hexels3d_exact_resolve_workspace_bytes(int num_records);
+HX_API int hx_hexels3d_exact_resolve(
+    int P, int num_rendered, const int32_t* ranges, const int32_t* point_list, int image_width,
+    int image_height, const float* colors, const float* color_grads, const float* color_quads,
+    const float* view_grads, const float* specular_ks, const float* specular_log_s,
+    const float* view_dirs, const float* normals, const float* transMats,
+    const float* opacities, const float* softnesses, int softness_stride,
+    const float* background, const float* center_depths, const uint8_t* selected_mask,
+    const uint8_t* pixel_mask, int color_model, int view_model, int use_view_grads,
+    int exact_mode, int crop_x0, int crop_y0, int crop_x1, int crop_y1, const uint8_t* enabled,
+    const int32_t* record_counts, const int32_t* record_offsets, int num_records,
+    float* out_color, uint8_t* order_changed, void* workspace, size_t workspace_bytes,
+    cudaStream_t stream);
+
 /* Per-surfel staged records for the compositing pair (no reference
  * counterpart: the reference gathers every field from its arrays for every
  * list entry, hexels3d_forward.cu:673-760).  Writes, for each of the P

@@ -71,6 +71,37 @@ __device__ __forceinline__ int warp_reduce_scatter24(float (&v)[24], const int l
     return start;
 }
 
+// Sum of a 24-slot vector over each 16-lane half of the warp (two vectors
+// at once): reduce-scatter halvings over lane bits 3, 2, 1 leave each lane 3
+// slots summed over 8 lanes, and one exchange over lane bit 0 completes them
+// split between the two lanes: the even lane holds slots start, start + 1 in
+// v[0], v[1], the odd lane slot start + 2 in v[2].
+__device__ __forceinline__ int half_warp_reduce_scatter24(float (&v)[24], const int lane) {
+    int start = 0;
+#pragma unroll
+    for (int o = 8, n = 24; o >= 2; o >>= 1, n >>= 1) {
+        const int half = n / 2;
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+        if (upper) start += half;
+    }
+    const bool odd = (lane & 1) != 0;
+    const float r0 = __shfl_xor_sync(0xffffffffu, odd ? v[0] : v[2], 1);
+    const float r1 = __shfl_xor_sync(0xffffffffu, v[1], 1);
+    if (odd) {
+        v[2] += r0;
+    } else {
+        v[0] += r0;
+        v[1] += r1;
+    }
+    return start;
+}
+
 template <int N>
 __device__ __forceinline__ int warp_reduce_scatter(float (&v)[N], const int lane) {
     int start = 0;
@@ -517,6 +548,39 @@ __device__ __forceinline__ void rgb_pair_vjp(const Surfel3D& s, const PairRec& r
     }
 }
 
+// Packs the blended pairs of the entry in hand (ballots m[k] of the lanes'
+// pixel k, records rec[k]) into pairs[0, n) in pixel order.
+template <int PPT>
+__device__ __forceinline__ void pack_pairs(const unsigned (&m)[PPT], const PairRec (&rec)[PPT],
+                                           const int lane, PairRec* pairs) {
+    int base = 0;
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+        if (m[k] & (1u << lane)) pairs[base + __popc(m[k] & ((1u << lane) - 1u))] = rec[k];
+        base += __popc(m[k]);
+    }
+}
+
+// The VJP of a packed pair of the warp whose pixel block starts at (wx0,
+// wy0); the pair carries its lane and pixel slot (lane | k << 5).
+__device__ __forceinline__ void packed_pair_vjp(const Surfel3D& s, const PairRec& r, const int wx0,
+                                                const int wy0, float (&acc)[24]) {
+    const int code = __float_as_int(r.b.w);
+    const float px = (float)(wx0 + (code & 7));
+    const float py = (float)(wy0 + ((code & 31) >> 3) + 4 * (code >> 5));
+    rgb_pair_vjp(s, r, px, py, acc);
+}
+
+// Adds a warp-reduced 24-slot vector (warp_reduce_scatter24) into the
+// entry's shared gradient row.
+__device__ __forceinline__ void put_reduced24(float* dst, const float (&acc)[24], const int start,
+                                              const int lane) {
+    const int c = lane & 3;  // lanes 0-2 of each group of 4 write
+    const float val = c == 0 ? acc[0] : (c == 1 ? acc[1] : acc[2]);
+    const int comp = start + c;
+    if (c < 3 && comp < kLiteComp && val != 0.f) atomicAdd(dst + comp, val);
+}
+
 // One CTA per 16x16 tile, 256 / PPT threads, PPT pixels per thread: warps
 // cover 8 x (4 PPT) pixel blocks (two across, 4 / PPT down), lane l owns
 // pixels (l % 8, l / 8 + 4 k), k < PPT.  Per list index the PPT pairs of a
@@ -538,7 +602,7 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
     // the forward's blend-mask bytes of the batch's list entries
     __shared__ unsigned char s_bm[kBatch];
     // per warp: the packed pairs of the list entry in hand (PACK)
-    __shared__ PairRec s_pairs[PACK ? kThreads / 32 : 1][PACK ? 32 * PPT : 1];
+    __shared__ PairRec s_pairs[PACK ? kThreads / 32 : 1][PACK ? 32 : 1];
     static_assert(!PACK || (N == 24 && !SURF && !PREFILTER), "packed pairs: plain RGB only");
 
     // N == 32 uses the fixed slot layout (compile-time indices keep the
@@ -672,6 +736,9 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
             n_mine += __popc(m);
         }
         __syncwarp();
+        // PACK: an entry of at most 16 pairs held in the first half of the
+        // pair buffer until the next one (or the end of the batch)
+        int pend_idx = -1, pend_n = 0;
         for (int jj = n_mine - 1; jj >= 0; --jj) {
             const int idx = bstart + s_list[warp][jj];
             const Surfel3D& s = s_prim[idx - bstart];
@@ -692,6 +759,50 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
                     n_pairs += __popc(m[k]);
                 }
                 if (n_pairs == 0) continue;
+                if (n_pairs <= 16) {
+                    // packed into one half of the warp's pair buffer; two such
+                    // entries share one VJP pass and one half-warp reduction
+                    // (the per-pixel part above never reads their result)
+                    const int off = pend_idx >= 0 ? 16 : 0;
+                    if (off == 0) __syncwarp();  // the buffer's last reads are done
+                    pack_pairs<PPT>(m, rec, lane, &s_pairs[warp][off]);
+                    if (pend_idx < 0) {
+                        pend_idx = idx;
+                        pend_n = n_pairs;
+                        continue;
+                    }
+                    __syncwarp();
+                    const bool hi = lane >= 16;
+                    const int e_idx = hi ? idx : pend_idx;
+                    float acc[24];
+#pragma unroll
+                    for (int c = 0; c < 24; ++c) acc[c] = 0.f;
+                    if ((lane & 15) < (hi ? n_pairs : pend_n))
+                        packed_pair_vjp(s_prim[e_idx - bstart], s_pairs[warp][lane], wx0, wy0,
+                                        acc);
+                    const int start = half_warp_reduce_scatter24(acc, lane);
+                    float* dst = s_acc + (e_idx - bstart) * kLiteComp;
+                    const bool odd = (lane & 1) != 0;
+                    const int comp = start + (odd ? 2 : 0);
+                    const float val = odd ? acc[2] : acc[0];
+                    if (comp < kLiteComp && val != 0.f) atomicAdd(dst + comp, val);
+                    if (!odd && start + 1 < kLiteComp && acc[1] != 0.f)
+                        atomicAdd(dst + start + 1, acc[1]);
+                    pend_idx = -1;
+                    continue;
+                }
+                if (pend_idx >= 0) {  // the held entry goes alone
+                    __syncwarp();
+                    float acc[24];
+#pragma unroll
+                    for (int c = 0; c < 24; ++c) acc[c] = 0.f;
+                    if (lane < pend_n)
+                        packed_pair_vjp(s_prim[pend_idx - bstart], s_pairs[warp][lane], wx0, wy0,
+                                        acc);
+                    const int start = warp_reduce_scatter24(acc, lane);
+                    put_reduced24(s_acc + (pend_idx - bstart) * kLiteComp, acc, start, lane);
+                    pend_idx = -1;
+                }
                 float acc[24];
 #pragma unroll
                 for (int c = 0; c < 24; ++c) acc[c] = 0.f;
@@ -701,37 +812,22 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
                 if (halves > 1 && n_pairs <= 32) {
                     // pairs of both halves: packed one per lane (one pass)
                     __syncwarp();  // the previous entry's pairs have been read
-                    int base = 0;
-#pragma unroll
-                    for (int k = 0; k < PPT; ++k) {
-                        if (m[k] & (1u << lane))
-                            s_pairs[warp][base + __popc(m[k] & ((1u << lane) - 1u))] = rec[k];
-                        base += __popc(m[k]);
-                    }
+                    pack_pairs<PPT>(m, rec, lane, &s_pairs[warp][0]);
                     __syncwarp();
-                    if (lane < n_pairs) {
-                        const PairRec r = s_pairs[warp][lane];
-                        const int code = __float_as_int(r.b.w);
-                        const float px = (float)(wx0 + (code & 7));
-                        const float py = (float)(wy0 + ((code & 31) >> 3) + 4 * (code >> 5));
-                        rgb_pair_vjp(s, r, px, py, acc);
-                    }
+                    if (lane < n_pairs)
+                        packed_pair_vjp(s, s_pairs[warp][lane], wx0, wy0, acc);
                 } else {
-                    // one half holds every pair, or more than a warp of
-                    // pairs: each lane takes its own, in place
+                    // more than a warp of pairs, or (never with 16 or fewer)
+                    // one half holding every pair: each lane takes its own
 #pragma unroll
                     for (int k = 0; k < PPT; ++k)
                         if (m[k] != 0u && (m[k] & (1u << lane)))
                             rgb_pair_vjp(s, rec[k], q[k].px, q[k].py, acc);
                 }
-                float* dst = s_acc + (idx - bstart) * kLiteComp;
                 // (shared-memory atomics straight from the few lanes holding
                 // pairs measured slower than this reduction even for one pair)
                 const int start = warp_reduce_scatter24(acc, lane);
-                const int c = lane & 3;
-                const float val = c == 0 ? acc[0] : (c == 1 ? acc[1] : acc[2]);
-                const int comp = start + c;
-                if (c < 3 && comp < kLiteComp && val != 0.f) atomicAdd(dst + comp, val);
+                put_reduced24(s_acc + (idx - bstart) * kLiteComp, acc, start, lane);
             } else {
             float acc[N];
 #pragma unroll
@@ -762,6 +858,16 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
                 }
             }
             }
+        }
+        if (PACK && pend_idx >= 0) {  // the batch's last held entry goes alone
+            __syncwarp();
+            float acc[24];
+#pragma unroll
+            for (int c = 0; c < 24; ++c) acc[c] = 0.f;
+            if (lane < pend_n)
+                packed_pair_vjp(s_prim[pend_idx - bstart], s_pairs[warp][lane], wx0, wy0, acc);
+            const int start = warp_reduce_scatter24(acc, lane);
+            put_reduced24(s_acc + (pend_idx - bstart) * kLiteComp, acc, start, lane);
         }
         __syncthreads();
         // Flush this batch: one global atomic per (surfel, non-zero component).

@@ -35,11 +35,15 @@ struct FwdPixel {
 // One (pixel, surfel) pair at list index `idx` (batch slot j): the
 // reference's per-pair arithmetic (hexels3d_forward.cu:690-1000).  Returns
 // whether the pair's alpha reached k3BlendMarkAlpha (the blend-mask test).
-template <bool SURF, bool PREFILTER, bool OWNER>
+// PLAIN fixes the training configuration at compile time (linear colour,
+// linear view model with view gradients, one softness for all edges, no
+// overdraw or contribution outputs): the same arithmetic without the
+// per-pair tests of the other options.
+template <bool SURF, bool PREFILTER, bool OWNER, bool PLAIN>
 __device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& s, int idx, int j,
                                          FwdPixel& q, float* s_contrib) {
     const int g_id = s.id;
-    const bool is_base = g_id < a.overdraw_base;
+    const bool is_base = PLAIN || g_id < a.overdraw_base;
     if (SURF && q.done_color && !is_base) return false;
     const float px = q.px, py = q.py;
     const float3 Tu = {s.tu[0], s.tu[1], s.tu[2]};
@@ -54,7 +58,7 @@ __device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& 
     const float depth_sdf = (sx * Tw.x + sy * Tw.y) + Tw.z;
     if (depth_sdf < k3NearPlane) return false;
     float dist, soft;
-    if (a.softness_stride == 1) {  // one softness for all edges: no edge needed
+    if (PLAIN || a.softness_stride == 1) {  // one softness for all edges: no edge needed
         dist = hex_sdf_value(sx, sy);
         soft = s.s0;
     } else {
@@ -80,7 +84,7 @@ __device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& 
     const float depth = use_filter ? Tw.z : depth_sdf;
 
     if (!q.done_color) {
-        if (is_base && alpha_sdf >= 1.0f / 255.0f) {
+        if (!PLAIN && is_base && alpha_sdf >= 1.0f / 255.0f) {
             if (a.overdraw) q.overdraw += alpha_raw_sdf;
             if (a.overdraw_hits) q.overdraw_hits += 1.0f;
         }
@@ -101,12 +105,13 @@ __device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& 
                 }
             }
             float cx = s.cb[0], cy = s.cb[1], cz = s.cb[2];
-            if (a.color_model >= kColorLinear) {
+            if (PLAIN || a.color_model >= kColorLinear) {
                 cx += u * s.gu[0] + v * s.gv[0];
                 cy += u * s.gu[1] + v * s.gv[1];
                 cz += u * s.gu[2] + v * s.gv[2];
             }
-            if (a.color_model == kColorQuadratic || a.color_model == kColorQuadBounded) {
+            if (!PLAIN &&
+                (a.color_model == kColorQuadratic || a.color_model == kColorQuadBounded)) {
                 const float* cq = a.color_quads + 9 * g_id;
                 float uu = u, vv = v;
                 if (a.color_model == kColorQuadBounded) bounded_coords(u, v, uu, vv);
@@ -115,12 +120,12 @@ __device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& 
                 cy += u2 * cq[1] + uv * cq[4] + v2 * cq[7];
                 cz += u2 * cq[2] + uv * cq[5] + v2 * cq[8];
             }
-            if (a.use_view_grads) {
+            if (PLAIN || a.use_view_grads) {
                 cx += s.cv[0];
                 cy += s.cv[1];
                 cz += s.cv[2];
             }
-            if (a.view_model == kViewLobe) {
+            if (!PLAIN && a.view_model == kViewLobe) {
                 const float* vd = a.view_dirs + 3 * g_id;
                 const float* nr = a.normals + 3 * g_id;
                 const float cos_nv = fmaxf(-(nr[0] * vd[0] + nr[1] * vd[1] + nr[2] * vd[2]), 0.f);
@@ -137,7 +142,7 @@ __device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& 
             q.T = test_T;
             q.n_visited = idx + 1;
             ++q.n_blended;
-            if (a.contrib) atomicAdd(&s_contrib[j], w);
+            if (!PLAIN && a.contrib) atomicAdd(&s_contrib[j], w);
         }
     }
     if (SURF && !q.done_surf && is_base) {
@@ -170,8 +175,9 @@ __device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& 
 // cover 8 x (4 PPT) pixel blocks (two across, 4 / PPT down), lane l owns
 // pixels (l % 8, l / 8 + 4 k), k < PPT.  The tile's list is staged 256
 // surfels at a time; a warp skips a surfel whose pixel box misses its block.
-template <bool SURF, bool PREFILTER, bool OWNER, int PPT>
-__global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const Render3DArgs a) {
+template <bool SURF, bool PREFILTER, bool OWNER, int PPT, bool PLAIN>
+__global__ void __launch_bounds__(k3BlockSize / PPT, PLAIN ? 5 : 1)
+    render3d_fwd_kernel(const Render3DArgs a) {
     constexpr int kThreads = k3BlockSize / PPT;
     constexpr int kWarpRows = 4 * PPT;
     __shared__ Surfel3D s_prim[k3BlockSize];
@@ -265,8 +271,8 @@ __global__ void __launch_bounds__(k3BlockSize / PPT) render3d_fwd_kernel(const R
 #pragma unroll
             for (int k = 0; k < PPT; ++k) {
                 if (!(q[k].done_color && q[k].done_surf)) {
-                    mark |= fwd_pair<SURF, PREFILTER, OWNER>(a, s, i * k3BlockSize + j, j, q[k],
-                                                             s_contrib);
+                    mark |= fwd_pair<SURF, PREFILTER, OWNER, PLAIN>(a, s, i * k3BlockSize + j,
+                                                                    j, q[k], s_contrib);
                     ++q[k].n_evaluated;
                 }
                 all_done = all_done && q[k].done_color && q[k].done_surf;
@@ -351,7 +357,15 @@ int launch_render(const Render3DArgs& a, cudaStream_t stream) {
     // thread keep a lane busy until both have (measured slower on B200).
     constexpr int kPPT = 1;
     dim3 grid(ceil_div(a.W, k3BlockX), ceil_div(a.H, k3BlockY));
-    render3d_fwd_kernel<SURF, PREFILTER, OWNER, kPPT><<<grid, k3BlockSize / kPPT, 0, stream>>>(a);
+    const bool plain = !SURF && !PREFILTER && !OWNER && a.color_model == kColorLinear &&
+                       a.view_model == kViewLinear && a.use_view_grads &&
+                       a.softness_stride == 1 && !a.overdraw && !a.overdraw_hits && !a.contrib;
+    if (plain)
+        render3d_fwd_kernel<SURF, PREFILTER, OWNER, kPPT, true>
+            <<<grid, k3BlockSize / kPPT, 0, stream>>>(a);
+    else
+        render3d_fwd_kernel<SURF, PREFILTER, OWNER, kPPT, false>
+            <<<grid, k3BlockSize / kPPT, 0, stream>>>(a);
     HX_LAUNCH_CHECK("render3d_fwd_kernel");
     return HX_OK;
 }

@@ -176,7 +176,7 @@ __device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& 
 // pixels (l % 8, l / 8 + 4 k), k < PPT.  The tile's list is staged 256
 // surfels at a time; a warp skips a surfel whose pixel box misses its block.
 template <bool SURF, bool PREFILTER, bool OWNER, int PPT, bool PLAIN>
-__global__ void __launch_bounds__(k3BlockSize / PPT, PLAIN ? 5 : 1)
+__global__ void __launch_bounds__(k3BlockSize / PPT, PLAIN ? 5 : 0)
     render3d_fwd_kernel(const Render3DArgs a) {
     constexpr int kThreads = k3BlockSize / PPT;
     constexpr int kWarpRows = 4 * PPT;
@@ -357,15 +357,17 @@ int launch_render(const Render3DArgs& a, cudaStream_t stream) {
     // thread keep a lane busy until both have (measured slower on B200).
     constexpr int kPPT = 1;
     dim3 grid(ceil_div(a.W, k3BlockX), ceil_div(a.H, k3BlockY));
-    const bool plain = !SURF && !PREFILTER && !OWNER && a.color_model == kColorLinear &&
-                       a.view_model == kViewLinear && a.use_view_grads &&
-                       a.softness_stride == 1 && !a.overdraw && !a.overdraw_hits && !a.contrib;
-    if (plain)
-        render3d_fwd_kernel<SURF, PREFILTER, OWNER, kPPT, true>
-            <<<grid, k3BlockSize / kPPT, 0, stream>>>(a);
-    else
-        render3d_fwd_kernel<SURF, PREFILTER, OWNER, kPPT, false>
-            <<<grid, k3BlockSize / kPPT, 0, stream>>>(a);
+    if constexpr (!SURF && !PREFILTER && !OWNER) {
+        if (a.color_model == kColorLinear && a.view_model == kViewLinear && a.use_view_grads &&
+            a.softness_stride == 1 && !a.overdraw && !a.overdraw_hits && !a.contrib) {
+            render3d_fwd_kernel<false, false, false, kPPT, true>
+                <<<grid, k3BlockSize / kPPT, 0, stream>>>(a);
+            HX_LAUNCH_CHECK("render3d_fwd_kernel");
+            return HX_OK;
+        }
+    }
+    render3d_fwd_kernel<SURF, PREFILTER, OWNER, kPPT, false>
+        <<<grid, k3BlockSize / kPPT, 0, stream>>>(a);
     HX_LAUNCH_CHECK("render3d_fwd_kernel");
     return HX_OK;
 }
@@ -469,13 +471,21 @@ extern "C" int hx_hexels3d_render_forward(
 namespace hx {
 namespace {
 
-// One thread per surfel: its record as the compositing kernels stage it.
+// One thread per surfel: its record as the compositing kernels stage it,
+// assembled in shared memory and written out by the CTA as one contiguous
+// run of 16-byte stores (256 records, 32 KB).
 template <bool SURF, bool PREFILTER>
 __global__ void __launch_bounds__(256) surfel_records_kernel(const Render3DArgs a,
                                                              Surfel3D* __restrict__ out) {
-    const int g = blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= a.P) return;
-    stage_surfel<SURF, PREFILTER>(a, g, a.W, a.H, out + g);
+    __shared__ Surfel3D s_rec[256];
+    const int g0 = blockIdx.x * 256;
+    const int g = g0 + (int)threadIdx.x;
+    if (g < a.P) stage_surfel<SURF, PREFILTER>(a, g, a.W, a.H, &s_rec[threadIdx.x]);
+    __syncthreads();
+    const int n = min(256, a.P - g0) * (int)(sizeof(Surfel3D) / sizeof(float4));
+    const float4* src = reinterpret_cast<const float4*>(s_rec);
+    float4* dst = reinterpret_cast<float4*>(out + g0);
+    for (int i = (int)threadIdx.x; i < n; i += 256) dst[i] = src[i];
 }
 
 }  // namespace

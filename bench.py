@@ -61,7 +61,7 @@ def mse_loss(pred, target):
 
 # DRAM bytes per launch of the roofline kernels, from the committed ncu
 # captures of these configurations (read + write)
-TRAFFIC_R3D_BWD_1080 = int((277.3568 + 58.14144) * 1e6)   # render3d_bwd, one 1080p view
+TRAFFIC_R3D_BWD_1080 = int((277.773312 + 57.324032) * 1e6)  # render3d_bwd, one 1080p view
 TRAFFIC_TOPK_FWD_2048 = int((45.213952 + 163.590144) * 1e6)  # topk_fwd, 2048^2 / 100k
 TRAFFIC_HEX_FWD_1024 = int((2.483712 + 7.526656) * 1e6)      # hexel_fwd, 1024^2 / 50k
 

@@ -86,22 +86,31 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed
+    region: one nvidia-smi process per node (local rank 0) over all of the
+    job's GPUs on the node, so that N ranks do not run N pollers beside the
+    timed steps; the other ranks sample nothing."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, local_rank: int):
+        n_local = int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [v for v in visible.split(",") if v.strip().isdigit()] if visible else []
+        self.gpus = ids[:n_local] if len(ids) >= n_local else [str(i) for i in range(n_local)]
+        self.active = local_rank == 0
         self.proc = None
         self.lines: list[str] = []
         self.thread = None
 
     def start(self):
+        if not self.active:
+            return
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", f"--id={','.join(self.gpus)}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
@@ -120,6 +129,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
+        if not self.active:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [],
+                    "sampled_by": "local rank 0"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -145,7 +157,7 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "gpus": len(self.gpus)}
 
 
 def dist_setup(n_gpus: int):
@@ -243,7 +255,8 @@ class ImageGSStep:
                                    inv_n=1.0 / self.numel, grad=v_img[self.r0:self.r1])
         ev[5].record()
         v_xy, v_conic, v_colors = csrc.nd_rasterize_backward_topk_norm(
-            self.H, self.W, 16, 16, ids, bins, xys, conics, self.c, v_img, topk)
+            self.H, self.W, 16, 16, ids, bins, xys, conics, self.c, v_img, topk,
+            rows=None if self.rows is None else (self.r0, self.r1))
         ev[6].record()
         _, v_mean, v_scale, v_rot = csrc.project_gaussians_2d_scale_rot_backward(
             w.num_points, self.m, self.s, self.r, self.H, self.W, radii, conics, v_xy, v_conic)
@@ -286,9 +299,11 @@ def run_ours(args, world, rank, local):
     n_isect = int(step.info["num_intersects"])
 
     clocks = ClockSampler(local)
+    # the sampler waits for its first sample: start it before the barrier,
+    # or the other ranks' first timed step waits for this rank
+    clocks.start()
     barrier(world)
     torch.cuda.synchronize()
-    clocks.start()
     launches0 = lib.dll.hx_launch_count()
     total_ms = 0.0
     start_ev = torch.cuda.Event(enable_timing=True)
@@ -505,9 +520,11 @@ def run_ours_hex2d(args, world, rank, local):
     stored = int((info["topk"] >= 0).sum())
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     clocks = ClockSampler(local)
+    # the sampler waits for its first sample: start it before the barrier,
+    # or the other ranks' first timed step waits for this rank
+    clocks.start()
     barrier(world)
     torch.cuda.synchronize()
-    clocks.start()
     launches0 = lib.dll.hx_launch_count()
     total = 0.0
     st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -418,10 +418,12 @@ __global__ void __launch_bounds__(256) sum_bwd_kernel(
 // partials, sums them over the lanes of the warp that hold the same Gaussian
 // (KeyTree) and adds each group's sum with one global atomic.  Every lane
 // runs both passes (pixels outside the image contribute zeros) so that the
-// warp-wide sums stay converged.
+// warp-wide sums stay converged.  The grid covers pixel rows [row0, row1)
+// (the whole image, or one stripe of tile rows).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) topk_bwd_kernel(
-    unsigned img_w, unsigned img_h, int channels, int num_points, float eps,
+    unsigned img_w, unsigned img_h, unsigned row0, unsigned row1, int channels, int num_points,
+    float eps,
     const float2* __restrict__ xys, const float3* __restrict__ conics,
     const float* __restrict__ rgbs, const float* __restrict__ v_output,
     const float* __restrict__ v_weights_sum, const float* __restrict__ v_entropy,
@@ -433,11 +435,11 @@ __global__ void __launch_bounds__(256) topk_bwd_kernel(
     const int tr = threadIdx.y * kBlockX + threadIdx.x;
     const unsigned lane = tr & 31;
     const int2 lp = tile_pixel16(tr);
-    const unsigned i = blockIdx.y * kBlockY + lp.y;
+    const unsigned i = row0 + blockIdx.y * kBlockY + lp.y;
     const unsigned j = blockIdx.x * kBlockX + lp.x;
     const float px = (float)j;
     const float py = (float)i;
-    const bool inside = (i < img_h && j < img_w);
+    const bool inside = (i < row1 && i < img_h && j < img_w);
     const int pix_id = min((int)(i * img_w + j), (int)(img_w * img_h - 1));
     const float* v_out = v_output + channels * pix_id;
 
@@ -582,16 +584,18 @@ __global__ void __launch_bounds__(1024) no_tiles_fwd_kernel(
     for (int k = 0; k < kTopK; ++k) pixel_topk[pix_id * kTopK + k] = ids[k];
 }
 
-int launch_topk_bwd(unsigned img_w, unsigned img_h, int channels, int num_points, float eps,
-                    const float* xys, const float* conics, const float* colors,
-                    const float* v_output, const float* v_ws, const float* v_ent,
-                    const int* pixel_topk, float* v_xy, float* v_conic, float* v_colors,
-                    cudaStream_t stream) {
-    dim3 grid(ceil_div((int)img_w, kBlockX), ceil_div((int)img_h, kBlockY));
+int launch_topk_bwd(unsigned img_w, unsigned img_h, unsigned row0, unsigned row1, int channels,
+                    int num_points, float eps, const float* xys, const float* conics,
+                    const float* colors, const float* v_output, const float* v_ws,
+                    const float* v_ent, const int* pixel_topk, float* v_xy, float* v_conic,
+                    float* v_colors, cudaStream_t stream) {
+    if (row1 <= row0) return HX_OK;
+    dim3 grid(ceil_div((int)img_w, kBlockX), ceil_div((int)(row1 - row0), kBlockY));
     dim3 block(kBlockX, kBlockY);
     topk_bwd_kernel<<<grid, block, 0, stream>>>(
-        img_w, img_h, channels, num_points, eps, (const float2*)xys, (const float3*)conics, colors,
-        v_output, v_ws, v_ent, pixel_topk, v_xy, v_conic, v_colors);
+        img_w, img_h, row0, row1, channels, num_points, eps, (const float2*)xys,
+        (const float3*)conics, colors, v_output, v_ws, v_ent, pixel_topk, v_xy, v_conic,
+        v_colors);
     HX_LAUNCH_CHECK("topk_bwd_kernel");
     return HX_OK;
 }
@@ -694,9 +698,25 @@ extern "C" int hx_nd_rasterize_backward_topk_norm(
     if (img_width == 0 || img_height == 0 || num_points == 0) return HX_OK;
     HX_REQUIRE(xys && conics && colors && v_output && pixel_topk && v_xy && v_conic && v_colors,
                "nd_rasterize_backward_topk_norm: null pointer");
-    return launch_topk_bwd(img_width, img_height, channels, num_points, (float)kEpsTopK, xys,
-                           conics, colors, v_output, v_weights_sum, v_entropy, pixel_topk, v_xy,
-                           v_conic, v_colors, stream);
+    return launch_topk_bwd(img_width, img_height, 0u, img_height, channels, num_points,
+                           (float)kEpsTopK, xys, conics, colors, v_output, v_weights_sum,
+                           v_entropy, pixel_topk, v_xy, v_conic, v_colors, stream);
+}
+
+extern "C" int hx_nd_rasterize_backward_topk_norm_rows(
+    unsigned img_width, unsigned img_height, int channels, int num_points, const float* xys,
+    const float* conics, const float* colors, const float* v_output, const float* v_weights_sum,
+    const float* v_entropy, const int32_t* pixel_topk, int row_begin, int row_end, float* v_xy,
+    float* v_conic, float* v_colors, cudaStream_t stream) {
+    HX_REQUIRE(channels >= 1, "nd_rasterize_backward_topk_norm_rows: channels must be >= 1");
+    HX_REQUIRE(row_begin >= 0 && row_begin <= row_end && row_end <= (int)img_height,
+               "nd_rasterize_backward_topk_norm_rows: rows must satisfy 0 <= begin <= end <= H");
+    if (img_width == 0 || row_begin == row_end || num_points == 0) return HX_OK;
+    HX_REQUIRE(xys && conics && colors && v_output && pixel_topk && v_xy && v_conic && v_colors,
+               "nd_rasterize_backward_topk_norm_rows: null pointer");
+    return launch_topk_bwd(img_width, img_height, (unsigned)row_begin, (unsigned)row_end, channels,
+                           num_points, (float)kEpsTopK, xys, conics, colors, v_output,
+                           v_weights_sum, v_entropy, pixel_topk, v_xy, v_conic, v_colors, stream);
 }
 
 extern "C" int hx_nd_rasterize_forward_no_tiles(unsigned img_width, unsigned img_height,
@@ -727,7 +747,7 @@ extern "C" int hx_nd_rasterize_backward_no_tiles(unsigned img_width, unsigned im
     if (img_width == 0 || img_height == 0 || num_points == 0) return HX_OK;
     HX_REQUIRE(xys && conics && colors && v_output && pixel_topk && v_xy && v_conic && v_colors,
                "nd_rasterize_backward_no_tiles: null pointer");
-    return launch_topk_bwd(img_width, img_height, channels, num_points, (float)kEpsNoTiles, xys,
-                           conics, colors, v_output, nullptr, nullptr, pixel_topk, v_xy, v_conic,
-                           v_colors, stream);
+    return launch_topk_bwd(img_width, img_height, 0u, img_height, channels, num_points,
+                           (float)kEpsNoTiles, xys, conics, colors, v_output, nullptr, nullptr,
+                           pixel_topk, v_xy, v_conic, v_colors, stream);
 }

@@ -228,25 +228,33 @@ def nd_rasterize_forward_topk_norm_stats(tile_bounds, block, img_size, gaussian_
 
 
 def _topk_backward(img_height, img_width, BLOCK_H, BLOCK_W, xys, conics, colors, v_output,
-                   v_weights_sum, v_entropy, pixel_topk):
+                   v_weights_sum, v_entropy, pixel_topk, rows=None):
     _check_xys_colors(xys, colors)
     check_input(pixel_topk, "pixel_topk")
     _tile_bounds_for(int(img_height), int(img_width), int(BLOCK_H), int(BLOCK_W))
     n, channels, dev = xys.size(0), colors.size(1), xys.device
     v_xy, v_conic, v_colors = zero_views(dev, [(n, 2), (n, 3), (n, channels)])
     v_output = v_output.contiguous()
+    args = (int(img_width), int(img_height), channels, n, ptr(xys), ptr(conics.contiguous()),
+            ptr(colors), ptr(v_output), ptr(v_weights_sum), ptr(v_entropy), ptr(pixel_topk))
+    outs = (ptr(v_xy), ptr(v_conic), ptr(v_colors), stream(dev))
     with torch.cuda.device(dev):
-        lib.call("hx_nd_rasterize_backward_topk_norm", int(img_width), int(img_height), channels,
-                 n, ptr(xys), ptr(conics.contiguous()), ptr(colors), ptr(v_output),
-                 ptr(v_weights_sum), ptr(v_entropy), ptr(pixel_topk), ptr(v_xy), ptr(v_conic),
-                 ptr(v_colors), stream(dev))
+        if rows is None:
+            lib.call("hx_nd_rasterize_backward_topk_norm", *args, *outs)
+        else:
+            lib.call("hx_nd_rasterize_backward_topk_norm_rows", *args, int(rows[0]),
+                     int(rows[1]), *outs)
     return v_xy, v_conic, v_colors
 
 
 def nd_rasterize_backward_topk_norm(img_height, img_width, BLOCK_H, BLOCK_W, gaussians_ids_sorted,
-                                    tile_bins, xys, conics, colors, v_output, pixel_topk):
+                                    tile_bins, xys, conics, colors, v_output, pixel_topk, *,
+                                    rows=None):
+    """The reference's top-K backward.  `rows=(begin, end)` (keyword only,
+    not in the reference) back-propagates pixel rows [begin, end) only: the
+    backward of one stripe, whose upstream gradient is zero elsewhere."""
     return _topk_backward(img_height, img_width, BLOCK_H, BLOCK_W, xys, conics, colors, v_output,
-                          None, None, pixel_topk)
+                          None, None, pixel_topk, rows)
 
 
 def nd_rasterize_backward_topk_norm_stats(img_height, img_width, BLOCK_H, BLOCK_W,

@@ -87,6 +87,9 @@ class _RasterizeGaussiansSum(Function):
         ctx.BLOCK_W = BLOCK_W
         ctx.num_intersects = num_intersects
         ctx.topk_norm = topk_norm
+        # a stripe's pixels outside its rows hold no ids: the backward skips them
+        ctx.rows = (None if tile_rows is None else
+                    (tile_rows[0] * BLOCK_H, min(tile_rows[1] * BLOCK_H, img_height)))
 
         if not topk_norm:
             (out_img,) = _C.nd_rasterize_forward(
@@ -113,6 +116,6 @@ class _RasterizeGaussiansSum(Function):
             gaussian_ids_sorted, tile_bins, xys, conics, colors, pixel_topk = ctx.saved_tensors
             v_xy, v_conic, v_colors = _C.nd_rasterize_backward_topk_norm(
                 ctx.img_height, ctx.img_width, ctx.BLOCK_H, ctx.BLOCK_W, gaussian_ids_sorted,
-                tile_bins, xys, conics, colors, v_out_img, pixel_topk,
+                tile_bins, xys, conics, colors, v_out_img, pixel_topk, rows=ctx.rows,
             )
         return (v_xy, None, v_conic, None, v_colors, None, None, None, None, None, None)

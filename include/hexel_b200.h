@@ -200,6 +200,18 @@ HX_API int hx_nd_rasterize_backward_topk_norm(
     const float* v_weights_sum, const float* v_entropy, const int32_t* pixel_topk,
     float* v_xy, float* v_conic, float* v_colors, cudaStream_t stream);
 
+/* hx_nd_rasterize_backward_topk_norm over pixel rows [row_begin, row_end)
+ * only (no reference counterpart; 0 <= row_begin <= row_end <= H): the
+ * backward of one stripe of tile rows (rasterize_gaussians_sum(tile_rows=)),
+ * which reads none of the per-pixel inputs outside the stripe.  Buffers are
+ * the whole image's, as above. */
+HX_API int hx_nd_rasterize_backward_topk_norm_rows(
+    unsigned img_width, unsigned img_height, int channels, int num_points, const float* xys,
+    const float* conics, const float* colors, const float* v_output,
+    const float* v_weights_sum, const float* v_entropy, const int32_t* pixel_topk,
+    int row_begin, int row_end, float* v_xy, float* v_conic, float* v_colors,
+    cudaStream_t stream);
+
 /* ---- S4: tile-less Image-GS -------------------------------------------- */
 
 /* Replaces nd_rasterize_forward_no_tiles_tensor (bindings.cu:2459-2510;

@@ -117,6 +117,23 @@ def test_geometry_backward_rejects_misaligned_buffers():
         assert b"boundary" in lib.dll.hx_last_error()
 
 
+def test_topk_backward_rows_rejects_bad_ranges():
+    """The stripe backward checks 0 <= begin <= end <= H before any launch
+    (fake addresses; nothing is dereferenced); an empty range is a no-op."""
+    from gsplat._lib import lib
+
+    a = 0x10000
+    fn = lib.dll.hx_nd_rasterize_backward_topk_norm_rows
+
+    def call(r0, r1):
+        return fn(64, 48, 3, 10, a, a, a, a, None, None, a, r0, r1, a, a, a, None)
+
+    for r0, r1 in ((-16, 16), (32, 16), (0, 64)):
+        assert call(r0, r1) != 0
+        assert b"rows must satisfy" in lib.dll.hx_last_error()
+    assert call(16, 16) == 0
+
+
 def test_tensors_on_another_device_are_rejected():
     """Raw pointers run on the first tensor's device, so a tensor on another
     device is rejected on the host (metadata only: cpu against meta)."""

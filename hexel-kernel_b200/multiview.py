@@ -44,7 +44,7 @@ def fit_step_views(params: Sequence[torch.Tensor], cams: Sequence, targets: Sequ
                    background: torch.Tensor, softness: float, grads: Sequence[torch.Tensor],
                    loss: torch.Tensor, pipeline: Optional[ViewPipeline] = None, *,
                    color_model: int = 1, view_model: int = 1,
-                   use_view_grads: bool = True, group: int = 1) -> None:
+                   use_view_grads: bool = True, group=1) -> None:
     """Forward, loss and backward of every view in `cams` (objects with
     viewmatrix, projmatrix, campos, width, height, tan_fovx, tan_fovy), the
     gradients of `params` (means3d, scales, rotations, colors, color_grads,
@@ -52,7 +52,8 @@ def fit_step_views(params: Sequence[torch.Tensor], cams: Sequence, targets: Sequ
     summed per-view colour losses ADDED into `loss` (one element).  With a
     `pipeline` of several streams the views run overlapped; without one they
     run in order on the current stream.  With `group` > 1 the views are taken
-    `group` at a time and each group is binned together
+    `group` at a time (or, with a sequence, in groups of those sizes, which
+    sum to the number of views) and each group is binned together
     (_C._forward_views_core: one depth order, one binning and one read-back
     of the intersection count per group instead of per view); the groups are
     dealt to the streams.  Each view's intermediate tensors are made and used
@@ -66,6 +67,14 @@ def fit_step_views(params: Sequence[torch.Tensor], cams: Sequence, targets: Sequ
         raise ValueError("params and grads take the 7 tensors " + ", ".join(PARAM_NAMES))
     if len(cams) != len(targets):
         raise ValueError("one target per camera")
+    if isinstance(group, int):
+        if group < 1:
+            raise ValueError("group must be >= 1")
+        sizes = [min(group, len(cams) - g0) for g0 in range(0, len(cams), group)]
+    else:
+        sizes = [int(n) for n in group]
+        if any(n < 1 for n in sizes) or sum(sizes) != len(cams):
+            raise ValueError("group sizes must be >= 1 and sum to the number of views")
     m3, sc, rot, col, cg, vg, op = params
     e = torch.empty(0, device=m3.device)
     main = torch.cuda.current_stream(m3.device)
@@ -76,19 +85,19 @@ def fit_step_views(params: Sequence[torch.Tensor], cams: Sequence, targets: Sequ
                 t.zero_()
         for s in streams:
             s.wait_stream(main)
-    if group < 1:
-        raise ValueError("group must be >= 1")
-    if group > 1:
-        for gi, g0 in enumerate(range(0, len(cams), group)):
+    grouped = len(sizes) < len(cams)  # groups of one view take the per-view path
+    if grouped:
+        g0 = 0
+        for gi, n in enumerate(sizes):
             k = gi % len(streams)
             acc = dict(zip(PARAM_NAMES, grads))
             if k > 0:
                 acc.update(zip(PARAM_NAMES[:3], pipeline.geo[k - 1]))
             with torch.cuda.stream(streams[k]):
-                outs = _C._forward_views_core(m3, sc, rot, col, cg, vg, op, cams[g0:g0 + group],
+                outs = _C._forward_views_core(m3, sc, rot, col, cg, vg, op, cams[g0:g0 + n],
                                               background, softness, color_model, view_model,
                                               use_view_grads)
-                for o, cam, tgt in zip(outs, cams[g0:g0 + group], targets[g0:g0 + group]):
+                for o, cam, tgt in zip(outs, cams[g0:g0 + n], targets[g0:g0 + n]):
                     _, g_color = l2_loss_grad(o["out_color"], tgt, loss=loss)
                     _C._backward_core(m3, e, sc, rot, col, cg, e, vg, e, e, op, e,
                                       cam.viewmatrix, cam.projmatrix, cam.campos, background,
@@ -99,7 +108,8 @@ def fit_step_views(params: Sequence[torch.Tensor], cams: Sequence, targets: Sequ
                                       records=o["records"])
                     del g_color
                 del outs
-    for i, (cam, tgt) in enumerate(zip(cams, targets) if group == 1 else ()):
+            g0 += n
+    for i, (cam, tgt) in enumerate(zip(cams, targets) if not grouped else ()):
         k = i % len(streams)
         acc = dict(zip(PARAM_NAMES, grads))
         if k > 0:

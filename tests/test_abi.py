@@ -96,6 +96,11 @@ def test_loss_and_multiview_check_arguments_before_any_launch():
         multiview.fit_step_views(p[:6], [], [], torch.zeros(3), 10.0, p, torch.zeros(1))
     with pytest.raises(ValueError, match="one target per camera"):
         multiview.fit_step_views(p, [object()], [], torch.zeros(3), 10.0, p, torch.zeros(1))
+    three = ([object()] * 3, [torch.zeros(3)] * 3)
+    for group in (0, [2, 2], [3, 0], [1, 1]):
+        with pytest.raises(ValueError, match="group"):
+            multiview.fit_step_views(p, *three, torch.zeros(3), 10.0, p, torch.zeros(1),
+                                     group=group)
 
 
 def test_geometry_backward_rejects_misaligned_buffers():

@@ -556,9 +556,9 @@ def test_grouped_views_binning_equals_per_view(views, size):
 
 
 def test_grouped_views_step_equals_per_view():
-    """multiview.fit_step_views with the views binned in groups gives the
-    gradients and loss of the per-view step (to the order of the float
-    atomics), over one and two streams."""
+    """multiview.fit_step_views with the views binned in groups (of one size,
+    or of the sizes given) gives the gradients and loss of the per-view step
+    (to the order of the float atomics), over one and two streams."""
     import multiview
     import workloads
 
@@ -579,7 +579,8 @@ def test_grouped_views_step_equals_per_view():
 
     want_g, want_l = step(None, 1)
     for pipe, group in ((None, 3), (multiview.ViewPipeline(params, streams=2), 3),
-                        (multiview.ViewPipeline(params, streams=2), 7)):
+                        (multiview.ViewPipeline(params, streams=2), 7),
+                        (multiview.ViewPipeline(params, streams=2), [2, 1, 4])):
         got_g, got_l = step(pipe, group)
         assert abs(float(got_l) - float(want_l)) <= 1e-5 * abs(float(want_l))
         for name, a, b in zip(multiview.PARAM_NAMES, got_g, want_g):

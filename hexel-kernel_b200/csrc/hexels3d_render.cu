@@ -37,8 +37,9 @@ struct FwdPixel {
 // whether the pair's alpha reached k3BlendMarkAlpha (the blend-mask test).
 // PLAIN fixes the training configuration at compile time (linear colour,
 // linear view model with view gradients, one softness for all edges, no
-// overdraw or contribution outputs): the same arithmetic without the
-// per-pair tests of the other options.
+// overdraw or contribution outputs, every surfel a base surfel; with or
+// without the surface outputs):
+// the same arithmetic without the per-pair tests of the other options.
 template <bool SURF, bool PREFILTER, bool OWNER, bool PLAIN>
 __device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& s, int idx, int j,
                                          FwdPixel& q, float* s_contrib) {
@@ -176,7 +177,7 @@ __device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& 
 // pixels (l % 8, l / 8 + 4 k), k < PPT.  The tile's list is staged 256
 // surfels at a time; a warp skips a surfel whose pixel box misses its block.
 template <bool SURF, bool PREFILTER, bool OWNER, int PPT, bool PLAIN>
-__global__ void __launch_bounds__(k3BlockSize / PPT, PLAIN ? 5 : 0)
+__global__ void __launch_bounds__(k3BlockSize / PPT, PLAIN && !SURF ? 5 : 0)
     render3d_fwd_kernel(const Render3DArgs a) {
     constexpr int kThreads = k3BlockSize / PPT;
     constexpr int kWarpRows = 4 * PPT;
@@ -357,10 +358,12 @@ int launch_render(const Render3DArgs& a, cudaStream_t stream) {
     // thread keep a lane busy until both have (measured slower on B200).
     constexpr int kPPT = 1;
     dim3 grid(ceil_div(a.W, k3BlockX), ceil_div(a.H, k3BlockY));
-    if constexpr (!SURF && !PREFILTER && !OWNER) {
+    if constexpr (!PREFILTER && !OWNER) {
+        // (every surfel a base surfel: the surface outputs skip the others)
         if (a.color_model == kColorLinear && a.view_model == kViewLinear && a.use_view_grads &&
-            a.softness_stride == 1 && !a.overdraw && !a.overdraw_hits && !a.contrib) {
-            render3d_fwd_kernel<false, false, false, kPPT, true>
+            a.softness_stride == 1 && !a.overdraw && !a.overdraw_hits && !a.contrib &&
+            a.overdraw_base >= a.P) {
+            render3d_fwd_kernel<SURF, false, false, kPPT, true>
                 <<<grid, k3BlockSize / kPPT, 0, stream>>>(a);
             HX_LAUNCH_CHECK("render3d_fwd_kernel");
             return HX_OK;

@@ -209,6 +209,34 @@ def test_owner_and_overdraw_variants_match_reference(ref):
             assert torch.equal(x, y)
 
 
+@pytest.mark.parametrize("base", [-1, 700])
+def test_plain_surface_forward_matches_reference(ref, base):
+    """The surface forward without contribution or overdraw outputs (the
+    public API's and the fit steps' call; with every surfel a base surfel it
+    runs the plain-RGB instantiation) against the reference's forward_all;
+    with a base count below P it takes the generic one."""
+    if ref is None:
+        pytest.skip("reference kernels not built")
+    from gsplat.cuda_hexels3d import _C
+
+    w, cam, extra = _scene(seed=4)
+    t, s = _args(w, cam, extra)
+    for median in (False, True):
+        o = _C._forward_core(*t, *s, False, False, False, return_surface=True,
+                             overdraw_base_count=base, return_median_depth=median)
+        fn = "rasterize_hexels3d_forward_median" if median else "rasterize_hexels3d_forward_all"
+        theirs = getattr(ref, fn)(*t, *s, False, False, False, True, base, False, False, False)
+        mine = (o["out_color"], o["radii"], o["surf_depth"], o["surf_alpha"], o["surf_maps"])
+        for n, a, b in zip(("out_color", "radii", "depth", "alpha", "surface"), mine,
+                           (theirs[0], theirs[1], theirs[5], theirs[6], theirs[7])):
+            assert a.shape == b.shape, n
+            if a.dtype.is_floating_point:
+                torch.testing.assert_close(a, b, rtol=1e-5, atol=IMG_ATOL * max(1.0, float(
+                    b.abs().max()) if b.numel() else 1.0), msg=n)
+            else:
+                assert torch.equal(a, b), n
+
+
 def test_public_api_autograd_matches_reference_backward(ref):
     """rasterize_hexels3d(return_surface=True) through autograd, against the
     reference's uncached surface backward on the same upstream gradients."""

@@ -41,7 +41,7 @@ sys.path.insert(0, ROOT)
 
 import torch  # noqa: E402
 
-from multiview import ViewPipeline, fit_step_views  # noqa: E402
+from multiview import ViewPipeline, fit_step_views, view_groups  # noqa: E402
 from sharding import GradBuffer, balance_views, stripe_rows, view_split  # noqa: E402
 
 def l2_loss_grad(*args, **kwargs):
@@ -721,20 +721,6 @@ def make_targets(w, views, device):
         g = torch.Generator().manual_seed(20261201 + 7919 * (v + 1))
         out.append(torch.rand((3, cam.height, cam.width), generator=g).to(device))
     return out
-
-
-def view_groups(n_views: int, group: int) -> list:
-    """Group sizes of a rank's views for multiview.fit_step_views: groups of
-    at most `group` views and at most half of the views each, so that both
-    streams have a group to overlap (8 views of 1080p on one GPU: 16.19 ms as
-    2 groups of 4, 16.63 ms as 1 group of 8; a separate first group of 2
-    views, whose binning nothing overlaps, measured no faster: 15.39 against
-    15.30 ms for 8 views, 115.4 against 115.1 ms for 64)."""
-    if n_views <= 0:
-        return []
-    cap = max(1, min(group, (n_views + 1) // 2))
-    k = -(-n_views // cap)
-    return [n_views // k + (1 if i < n_views % k else 0) for i in range(k)]
 
 
 class Hexels3DStep:

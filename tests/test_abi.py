@@ -103,6 +103,22 @@ def test_loss_and_multiview_check_arguments_before_any_launch():
                                      group=group)
 
 
+def test_view_groups_split_a_ranks_views():
+    """Balanced groups of at most `group` views and at most half of the
+    views each (two streams, a group each); every view in exactly one."""
+    from multiview import view_groups
+
+    assert view_groups(64, 8) == [8] * 8
+    assert view_groups(8, 8) == [4, 4]
+    assert view_groups(9, 4) == [3, 3, 3]
+    assert view_groups(1, 8) == [1] and view_groups(0, 8) == []
+    for n in range(1, 70):
+        for g in (1, 2, 3, 8):
+            sizes = view_groups(n, g)
+            assert sum(sizes) == n and min(sizes) >= 1 and max(sizes) <= max(1, g)
+            assert max(sizes) - min(sizes) <= 1 and (n < 2 or len(sizes) >= 2)
+
+
 def test_geometry_backward_rejects_misaligned_buffers():
     """The geometry backward reads rotations as float4 and scales as float2:
     a buffer that does not start on that boundary is rejected by the C-ABI

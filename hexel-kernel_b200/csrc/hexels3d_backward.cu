@@ -144,13 +144,17 @@ struct BwdSlots {
 // VJP of one (pixel, surfel) pair at list index idx, ADDED into acc; updates
 // the pixel's running state (transmittance and "behind" terms).  Returns
 // whether the pair blended.  Per-pair arithmetic restates
-// hexels3d_forward.cu:1983-2470.
-template <bool SURF, bool PREFILTER, int N>
+// hexels3d_forward.cu:1983-2470.  PL fixes the training configuration at
+// compile time (linear colour with colour-gradient slots, linear view model
+// with view gradients, one softness, every surfel a base surfel, no
+// overdraw, softness, quadratic, lobe or explicit view-direction slots): the
+// same arithmetic without those per-pair tests.
+template <bool SURF, bool PREFILTER, int N, bool PL>
 __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayout& L,
                                          const BwdSlots& O, const Surfel3D& s, const int idx,
                                          BwdPixel& q, float (&acc)[N]) {
     const int g_id = s.id;
-    const bool is_base = g_id < a.overdraw_base;
+    const bool is_base = PL || g_id < a.overdraw_base;
     const bool active_color = idx < q.n_color;
     const bool active_surf = SURF && is_base && idx < q.n_surf;
     if (!active_color && !active_surf) return false;
@@ -160,7 +164,8 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
     const float3 Tw = {s.tw[0], s.tw[1], s.tw[2]};
     const float3 soft3 = {s.s0, s.s1, s.s2};
     HexHit h;
-    if (!hexel_hit(px, py, Tu, Tv, Tw, s.opacity, soft3, a.softness_stride == 1, h)) return false;
+    if (!hexel_hit(px, py, Tu, Tv, Tw, s.opacity, soft3, PL || a.softness_stride == 1, h))
+        return false;
     float alpha = h.alpha;
     bool use_filter = false, clamped_filter = false;
     float G = 0.f, dxf = 0.f, dyf = 0.f;
@@ -189,14 +194,14 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
         const float ua = use_filter ? 0.f : u;
         const float va = use_filter ? 0.f : v;
         c = {s.cb[0], s.cb[1], s.cb[2]};
-        if (a.color_model >= kColorLinear) {
+        if (PL || a.color_model >= kColorLinear) {
             c.x += ua * s.gu[0] + va * s.gv[0];
             c.y += ua * s.gu[1] + va * s.gv[1];
             c.z += ua * s.gu[2] + va * s.gv[2];
         }
         const float* cq = nullptr;
         float ub = ua, vb = va;
-        if (a.color_model == kColorQuadratic || a.color_model == kColorQuadBounded) {
+        if (!PL && (a.color_model == kColorQuadratic || a.color_model == kColorQuadBounded)) {
             cq = a.color_quads + 9 * g_id;
             if (a.color_model == kColorQuadBounded) bounded_coords(ua, va, ub, vb);
             const float u2 = ub * ub, uv = ub * vb, v2 = vb * vb;
@@ -204,7 +209,7 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
             c.y += u2 * cq[1] + uv * cq[4] + v2 * cq[7];
             c.z += u2 * cq[2] + uv * cq[5] + v2 * cq[8];
         }
-        if (a.use_view_grads) {
+        if (PL || a.use_view_grads) {
             c.x += s.cv[0];
             c.y += s.cv[1];
             c.z += s.cv[2];
@@ -213,7 +218,7 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
         bool log_s_clamped = false;
         const float* vd = a.view_dirs + 3 * g_id;
         float3 nr = {0.f, 0.f, 0.f};
-        if (a.view_model == kViewLobe) {
+        if (!PL && a.view_model == kViewLobe) {
             if (a.normals)
                 nr = {a.normals[3 * g_id], a.normals[3 * g_id + 1], a.normals[3 * g_id + 2]};
             cos_nv = fmaxf(-(nr.x * vd[0] + nr.y * vd[1] + nr.z * vd[2]), 0.f);
@@ -228,7 +233,7 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
         acc[0] += w * v_out_r;
         acc[1] += w * v_out_g;
         acc[2] += w * v_out_b;
-        if (L.off_cg >= 0) {
+        if (PL || L.off_cg >= 0) {
             acc[O.cg + 0] += w * v_out_r * ua;
             acc[O.cg + 1] += w * v_out_g * ua;
             acc[O.cg + 2] += w * v_out_b * ua;
@@ -236,7 +241,7 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
             acc[O.cg + 4] += w * v_out_g * va;
             acc[O.cg + 5] += w * v_out_b * va;
         }
-        if (L.off_cq >= 0 && cq) {
+        if (!PL && L.off_cq >= 0 && cq) {
             const float q3[3] = {ub * ub, ub * vb, vb * vb};
 #pragma unroll
             for (int r = 0; r < 3; ++r) {
@@ -245,13 +250,13 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
                 acc[O.cq + 3 * r + 2] += w * v_out_b * q3[r];
             }
         }
-        if (a.use_view_grads && L.off_vd >= 0 && !use_filter) {
+        if (!PL && a.use_view_grads && L.off_vd >= 0 && !use_filter) {
             const float* vg = a.view_grads + 9 * g_id;
             acc[O.vd + 0] += w * (v_out_r * vg[0] + v_out_g * vg[3] + v_out_b * vg[6]);
             acc[O.vd + 1] += w * (v_out_r * vg[1] + v_out_g * vg[4] + v_out_b * vg[7]);
             acc[O.vd + 2] += w * (v_out_r * vg[2] + v_out_g * vg[5] + v_out_b * vg[8]);
         }
-        if (a.view_model == kViewLobe) {
+        if (!PL && a.view_model == kViewLobe) {
             if (L.off_ks >= 0) {
                 acc[O.ks + 0] += w * v_out_r * spec;
                 acc[O.ks + 1] += w * v_out_g * spec;
@@ -278,11 +283,11 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
         }
         v_alpha_total += T_before * (v_out_r * (c.x - q.behind.x) + v_out_g * (c.y - q.behind.y) +
                                      v_out_b * (c.z - q.behind.z));
-        if (!use_filter && a.color_model >= kColorLinear) {
+        if (!use_filter && (PL || a.color_model >= kColorLinear)) {
             v_u += w * (v_out_r * s.gu[0] + v_out_g * s.gu[1] + v_out_b * s.gu[2]);
             v_v += w * (v_out_r * s.gv[0] + v_out_g * s.gv[1] + v_out_b * s.gv[2]);
         }
-        if (!use_filter && a.color_model == kColorQuadratic) {
+        if (!PL && !use_filter && a.color_model == kColorQuadratic) {
             const float du_r = 2.f * u * cq[0] + v * cq[3];
             const float du_g = 2.f * u * cq[1] + v * cq[4];
             const float du_b = 2.f * u * cq[2] + v * cq[5];
@@ -291,7 +296,7 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
             const float dv_b = u * cq[5] + 2.f * v * cq[8];
             v_u += w * (v_out_r * du_r + v_out_g * du_g + v_out_b * du_b);
             v_v += w * (v_out_r * dv_r + v_out_g * dv_g + v_out_b * dv_b);
-        } else if (!use_filter && a.color_model == kColorQuadBounded) {
+        } else if (!PL && !use_filter && a.color_model == kColorQuadBounded) {
             float ubb, vbb;
             bounded_coords(u, v, ubb, vbb);
             const float du_r = 2.f * ubb * cq[0] + vbb * cq[3];
@@ -370,10 +375,11 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
         v_op += v_alpha_total * h.boundary;
     }
     const bool alpha_sdf_ok = h.alpha >= (1.0f / 255.0f);
-    const bool has_overdraw = (q.v_overdraw != 0.f) && active_color && is_base && alpha_sdf_ok;
+    const bool has_overdraw =
+        !PL && (q.v_overdraw != 0.f) && active_color && is_base && alpha_sdf_ok;
     if (has_overdraw) v_op += q.v_overdraw * h.boundary;
     acc[O.op] += v_op;
-    if (L.off_soft >= 0) {
+    if (!PL && L.off_soft >= 0) {
         const float sig = h.boundary;
         float v_soft = 0.f;
         if (!use_filter && !h.clamped)
@@ -391,7 +397,8 @@ __device__ __forceinline__ bool bwd_pair(const Backward3DArgs& a, const BwdLayou
         float dist_g, ddu, ddv;
         int edge_g;
         hex_sdf3_grad(u, v, dist_g, ddu, ddv, edge_g);
-        const float soft_g = (edge_g == 0) ? soft3.x : ((edge_g == 1) ? soft3.y : soft3.z);
+        const float soft_g =
+            PL ? soft3.x : ((edge_g == 0) ? soft3.x : ((edge_g == 1) ? soft3.y : soft3.z));
         const float d_sig = -soft_g * h.boundary * (1.f - h.boundary);
         float v_ad = has_overdraw ? (q.v_overdraw * s.opacity * d_sig) : 0.f;
         if (!use_filter && !h.clamped) v_ad += v_alpha_total * s.opacity * d_sig;
@@ -585,9 +592,9 @@ __device__ __forceinline__ void put_reduced24(float* dst, const float (&acc)[24]
 // cover 8 x (4 PPT) pixel blocks (two across, 4 / PPT down), lane l owns
 // pixels (l % 8, l / 8 + 4 k), k < PPT.  Per list index the PPT pairs of a
 // thread are added into one gradient vector before the warp reduction.
-template <bool SURF, bool PREFILTER, int N, int PPT, bool PACK>
-__global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_bwd_kernel(const Backward3DArgs a,
-                                                                        const BwdLayout L) {
+template <bool SURF, bool PREFILTER, int N, int PPT, bool PACK, bool PL>
+__global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2)
+    render3d_bwd_kernel(const Backward3DArgs a, const BwdLayout L) {
     constexpr int kThreads = k3BlockSize / PPT;
     constexpr int kBatch = kThreads;  // surfels staged per batch
     constexpr int kWarpRows = 4 * PPT;
@@ -839,7 +846,7 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PPT == 2 ? 5 : 2) render3d_
 #pragma unroll
             for (int k = 0; k < PPT; ++k)
                 if (bm & (1u << (2 * ((warp >> 1) * PPT + k) + (warp & 1))))
-                    contributed |= bwd_pair<SURF, PREFILTER, N>(a, L, O, s, idx, q[k], acc);
+                    contributed |= bwd_pair<SURF, PREFILTER, N, PL>(a, L, O, s, idx, q[k], acc);
             if (__any_sync(0xffffffffu, contributed)) {
                 float* dst = s_acc + (idx - bstart) * L.ncomp;
                 if constexpr (N == 24) {
@@ -1098,7 +1105,7 @@ using namespace hx;
 
 namespace {
 
-template <bool SURF, bool PREFILTER, int N, int PPT, bool PACK>
+template <bool SURF, bool PREFILTER, int N, int PPT, bool PACK, bool PL = false>
 int launch_bwd3d(const Backward3DArgs& a, const BwdLayout& L, cudaStream_t stream) {
     constexpr int kBatch = k3BlockSize / PPT;
     const size_t smem = sizeof(Surfel3D) * kBatch + sizeof(float) * kBatch * L.ncomp;
@@ -1108,14 +1115,14 @@ int launch_bwd3d(const Backward3DArgs& a, const BwdLayout& L, cudaStream_t strea
     int dev = 0;
     HX_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
-        HX_CUDA_TRY(cudaFuncSetAttribute(render3d_bwd_kernel<SURF, PREFILTER, N, PPT, PACK>,
+        HX_CUDA_TRY(cudaFuncSetAttribute(render3d_bwd_kernel<SURF, PREFILTER, N, PPT, PACK, PL>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)(sizeof(Surfel3D) * kBatch +
                                                sizeof(float) * kBatch * N)));
         if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
     }
     dim3 grid(ceil_div(a.W, k3BlockX), ceil_div(a.H, k3BlockY));
-    render3d_bwd_kernel<SURF, PREFILTER, N, PPT, PACK>
+    render3d_bwd_kernel<SURF, PREFILTER, N, PPT, PACK, PL>
         <<<grid, k3BlockSize / PPT, smem, stream>>>(a, L);
     HX_LAUNCH_CHECK("render3d_bwd_kernel");
     return HX_OK;
@@ -1133,6 +1140,13 @@ int launch_bwd3d_n(const Backward3DArgs& a, const BwdLayout& L, int slots,
         if (slots == 24 && a.grad_out_overdraw == nullptr)
             return launch_bwd3d<false, false, 24, kPPT, true>(a, L, stream);
         if (slots == 24) return launch_bwd3d<false, false, 24, kPPT, false>(a, L, stream);
+    }
+    if constexpr (!PREFILTER) {
+        if (slots == 32 && a.color_model == kColorLinear && a.view_model == kViewLinear &&
+            a.use_view_grads && a.softness_stride == 1 && a.overdraw_base >= a.P &&
+            !a.grad_out_overdraw && L.off_cg >= 0 && L.off_cq < 0 && L.off_soft < 0 &&
+            L.off_vd < 0 && L.off_ks < 0 && L.off_ls < 0)
+            return launch_bwd3d<SURF, false, 32, kPPT, false, true>(a, L, stream);
     }
     if (slots <= 32) return launch_bwd3d<SURF, PREFILTER, 32, kPPT, false>(a, L, stream);
     return launch_bwd3d<SURF, PREFILTER, 64, kPPT, false>(a, L, stream);

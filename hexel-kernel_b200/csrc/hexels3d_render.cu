@@ -37,8 +37,8 @@ struct FwdPixel {
 // whether the pair's alpha reached k3BlendMarkAlpha (the blend-mask test).
 // PLAIN fixes the training configuration at compile time (linear colour,
 // linear view model with view gradients, one softness for all edges, no
-// overdraw or contribution outputs, every surfel a base surfel; with or
-// without the surface outputs):
+// overdraw, contribution or pair-count outputs, every surfel a base surfel;
+// with or without the surface outputs):
 // the same arithmetic without the per-pair tests of the other options.
 template <bool SURF, bool PREFILTER, bool OWNER, bool PLAIN>
 __device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& s, int idx, int j,
@@ -142,7 +142,7 @@ __device__ __forceinline__ bool fwd_pair(const Render3DArgs& a, const Surfel3D& 
             q.C2 += cz * w;
             q.T = test_T;
             q.n_visited = idx + 1;
-            ++q.n_blended;
+            if (!PLAIN) ++q.n_blended;
             if (!PLAIN && a.contrib) atomicAdd(&s_contrib[j], w);
         }
     }
@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(k3BlockSize / PPT, PLAIN && !SURF ? 5 : 0)
                 if (!(q[k].done_color && q[k].done_surf)) {
                     mark |= fwd_pair<SURF, PREFILTER, OWNER, PLAIN>(a, s, i * k3BlockSize + j,
                                                                     j, q[k], s_contrib);
-                    ++q[k].n_evaluated;
+                    if (!PLAIN) ++q[k].n_evaluated;
                 }
                 all_done = all_done && q[k].done_color && q[k].done_surf;
             }
@@ -362,7 +362,7 @@ int launch_render(const Render3DArgs& a, cudaStream_t stream) {
         // (every surfel a base surfel: the surface outputs skip the others)
         if (a.color_model == kColorLinear && a.view_model == kViewLinear && a.use_view_grads &&
             a.softness_stride == 1 && !a.overdraw && !a.overdraw_hits && !a.contrib &&
-            a.overdraw_base >= a.P) {
+            !a.contrib_count && a.overdraw_base >= a.P) {
             render3d_fwd_kernel<SURF, false, false, kPPT, true>
                 <<<grid, k3BlockSize / kPPT, 0, stream>>>(a);
             HX_LAUNCH_CHECK("render3d_fwd_kernel");

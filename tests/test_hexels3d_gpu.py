@@ -237,6 +237,30 @@ def test_plain_surface_forward_matches_reference(ref, base):
                 assert torch.equal(a, b), n
 
 
+@pytest.mark.parametrize("surface", [False, True])
+def test_plain_forward_equals_generic(surface):
+    """Asking for the per-pixel pair counts takes the generic forward; without
+    them the training instantiation runs.  Same arithmetic: the images and the
+    state saved for the backward are bit-identical, and the counts obey
+    0 <= blended <= evaluated, blended <= last index."""
+    from gsplat.cuda_hexels3d import _C
+
+    w, cam, extra = _scene(seed=5)
+    t, s = _args(w, cam, extra)
+    kw = dict(return_surface=surface, save=True, save_surface=surface)
+    plain = _C._forward_core(*t, *s, False, False, False, **kw)
+    generic = _C._forward_core(*t, *s, False, False, False, count_contrib=True, **kw)
+    for n in ("out_color", "surf_depth", "surf_alpha", "surf_maps"):
+        assert torch.equal(plain[n], generic[n]), n
+    for n, a, b in zip(("final_T", "last_index"), plain["saved"][9:], generic["saved"][9:]):
+        assert torch.equal(a, b), n
+    counts = generic["contrib_count"]
+    blended, evaluated = counts[0], counts[1]
+    assert int(blended.min()) >= 0 and bool((blended <= evaluated).all())
+    assert bool((blended <= generic["saved"][10]).all())
+    assert int(blended.sum()) > 0
+
+
 def test_public_api_autograd_matches_reference_backward(ref):
     """rasterize_hexels3d(return_surface=True) through autograd, against the
     reference's uncached surface backward on the same upstream gradients."""
